@@ -1,0 +1,167 @@
+"""CPU oracle for the HELLO hot path (pricing scan, pair costs, restricted-OT PDHG).
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke()`` (as the
+checker) and ``bench.py`` (its CPU-baseline and reference legs) may import this
+package.  The product package ``hello_ot_b200`` never imports it and has no CPU
+fallback.
+
+``liboracle.so`` (built from ``oracle.c`` by ``make -C oracle``) restates the
+reference algorithms in C; ``_ref/hello_ot_cpp`` holds the reference's own
+C++ backend (``src/hello_ot/_native/cpp/{scan,solver}.cpp``) compiled from its
+sources by ``make -C oracle ref``.  The restatement is pinned against the
+reference by the fixtures in ``tests/golden``.
+"""
+from __future__ import annotations
+
+import ctypes
+import importlib
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF_DIR = HERE / "_ref"
+KIND = {"l1": 0, "linf": 1, "l2": 2, "raw": 3, "l2^2": 3, "lowrank": 3}
+REASONS = {1: "OPTIMAL", 2: "ITERATION_LIMIT", 3: "NUMERICAL_DIVERGENCE"}
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+_LIB = None
+
+
+class PdlpInfo(ctypes.Structure):
+    _fields_ = [("iterations", ctypes.c_int64), ("restarts", ctypes.c_int64),
+                ("reason", ctypes.c_int32), ("pad", ctypes.c_int32),
+                ("pobj", ctypes.c_double), ("dobj", ctypes.c_double), ("ap", ctypes.c_double),
+                ("rp", ctypes.c_double), ("ad", ctypes.c_double), ("rd", ctypes.c_double),
+                ("gap", ctypes.c_double), ("weight", ctypes.c_double),
+                ("cost_norm", ctypes.c_double), ("mass_norm", ctypes.c_double)]
+
+
+def build(force: bool = False) -> Path:
+    """Compile liboracle.so (and the reference's CPU build when its sources exist)."""
+    lib = HERE / "liboracle.so"
+    if force or not lib.exists() or lib.stat().st_mtime < (HERE / "oracle.c").stat().st_mtime:
+        subprocess.run(["make", "-C", str(HERE), f"PYTHON={sys.executable}"], check=True,
+                       stdout=subprocess.DEVNULL)
+    ref = Path(os.environ.get("HELLO_REF", "/root/reference"))
+    if (ref / "src/hello_ot/_native/cpp/scan.cpp").exists():
+        subprocess.run(["make", "-C", str(HERE), "ref", f"REF={ref}", f"PYTHON={sys.executable}"],
+                       check=True, stdout=subprocess.DEVNULL)
+    return lib
+
+
+def _lib():
+    global _LIB
+    if _LIB is None:
+        path = HERE / "liboracle.so"
+        if not path.exists():
+            build()
+        lib = ctypes.CDLL(str(path))
+        lib.orc_scan.argtypes = [ctypes.c_int, ctypes.c_int, _f32p, _f32p, ctypes.c_int64, ctypes.c_int64,
+                                 ctypes.c_int64, _f64p, _f64p, _f64p, _f64p, ctypes.c_double,
+                                 ctypes.c_int, ctypes.c_int, _f64p, _i64p, _f64p, _i64p, _f64p, ctypes.c_int]
+        lib.orc_pair_scores.argtypes = [ctypes.c_int, _f32p, _f32p, ctypes.c_int64, _f64p, _f64p, _f64p, _f64p,
+                                        ctypes.c_double, _i64p, _i64p, ctypes.c_int64, _f64p,
+                                        ctypes.c_void_p, ctypes.c_int]
+        lib.orc_pair_costs.argtypes = [ctypes.c_int, _f32p, _f32p, ctypes.c_int64, _f64p, _f64p,
+                                       ctypes.c_double, _i64p, _i64p, ctypes.c_int64, _f64p, ctypes.c_int]
+        lib.orc_pdlp.argtypes = [_i64p, _i64p, _f64p, ctypes.c_int64, _f64p, ctypes.c_int64, ctypes.c_int64,
+                                 _f64p, _f64p, ctypes.c_int, ctypes.c_int64, ctypes.c_double, ctypes.c_double,
+                                 ctypes.c_double, ctypes.c_int, _f64p, _f64p, ctypes.POINTER(PdlpInfo)]
+        _LIB = lib
+    return _LIB
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _f64(a, n=None):
+    if a is None:
+        return np.zeros(max(n or 0, 1), dtype=np.float64)
+    return np.ascontiguousarray(a, dtype=np.float64).reshape(-1)
+
+
+def scan(kind, x, y, rowb, colb, nx=None, ny=None, *, dot_scale=1.0, rk=1, ck=1, exact=True, threads=0):
+    """Bidirectional pricing scan.  ``rowb``/``colb`` are (f-a, g-b) for the raw
+    bilinear kind and (f, g) for the norm kinds.  Returns
+    (rv, ri, cv, ci, stats[num, den, max_pos, max_abs_cost, count])."""
+    x, y = _f32(x), _f32(y)
+    q, d = x.shape
+    n = y.shape[0]
+    rv = np.empty((q, max(rk, 1))); ri = np.empty((q, max(rk, 1)), np.int64)
+    cv = np.empty((n, max(ck, 1))); ci = np.empty((n, max(ck, 1)), np.int64)
+    stats = np.zeros(5)
+    rc = _lib().orc_scan(KIND[kind], int(exact), x, y, q, n, d, _f64(rowb), _f64(colb), _f64(nx, q),
+                         _f64(ny, n), float(dot_scale), int(rk), int(ck), rv, ri, cv, ci, stats, int(threads))
+    if rc:
+        raise ValueError(f"oracle scan rejected its inputs ({rc})")
+    return rv[:, :rk], ri[:, :rk], cv[:, :ck], ci[:, :ck], stats
+
+
+def pair_scores(kind, x, y, rowb, colb, nx, ny, rows, cols, *, dot_scale=1.0, threads=0):
+    """Exact (score, cost) of selected pairs."""
+    x, y = _f32(x), _f32(y)
+    rows = np.ascontiguousarray(rows, np.int64).reshape(-1)
+    cols = np.ascontiguousarray(cols, np.int64).reshape(-1)
+    score = np.empty(rows.size)
+    cost = np.empty(rows.size)
+    _lib().orc_pair_scores(KIND[kind], x, y, x.shape[1], _f64(rowb), _f64(colb), _f64(nx, len(x)),
+                           _f64(ny, len(y)), float(dot_scale), rows, cols, rows.size, score,
+                           cost.ctypes.data, int(threads))
+    return score, cost
+
+
+def pair_costs(kind, x, y, rows, cols, a=None, b=None, *, dot_scale=1.0, threads=0):
+    """Active-support pair costs in fp64 (the SDDMM restatement)."""
+    x, y = _f32(x), _f32(y)
+    rows = np.ascontiguousarray(rows, np.int64).reshape(-1)
+    cols = np.ascontiguousarray(cols, np.int64).reshape(-1)
+    out = np.empty(rows.size)
+    rc = _lib().orc_pair_costs(KIND[kind], x, y, x.shape[1], _f64(a, len(x)), _f64(b, len(y)),
+                               float(dot_scale), rows, cols, rows.size, out, int(threads))
+    if rc:
+        raise ValueError("oracle pair_costs rejected its inputs")
+    return out
+
+
+def pdlp(rows, cols, costs, source_mass, target_mass, x0=None, y0=None, *, frequency=200,
+         iteration_limit=2**31 - 1, tolerance=1e-6, rescale=False):
+    """Single-thread restatement of the reference C++ restricted-OT PDHG."""
+    rows = np.ascontiguousarray(rows, np.int64).reshape(-1)
+    cols = np.ascontiguousarray(cols, np.int64).reshape(-1)
+    costs = _f64(costs)
+    a, b = _f64(source_mass), _f64(target_mass)
+    masses = np.ascontiguousarray(np.concatenate((a, b)))
+    x0 = np.zeros(costs.size) if x0 is None else _f64(x0)
+    y0 = np.zeros(masses.size) if y0 is None else _f64(y0)
+    if isinstance(tolerance, dict):
+        tob = float(tolerance.get("objective", 1e-6))
+        tp, td = float(tolerance.get("primal", tob)), float(tolerance.get("dual", tob))
+    else:
+        tob = tp = td = float(tolerance)
+    x = np.empty(costs.size)
+    y = np.empty(masses.size)
+    info = PdlpInfo()
+    rc = _lib().orc_pdlp(rows, cols, costs, costs.size, masses, a.size, masses.size, x0, y0, int(frequency),
+                         int(iteration_limit), tob, tp, td, int(rescale), x, y, ctypes.byref(info))
+    if rc:
+        raise ValueError(f"oracle pdlp rejected its inputs ({rc})")
+    return dict(x=x, y=y, iterations=info.iterations, restarts=info.restarts,
+                termination_reason=REASONS.get(info.reason, "UNSPECIFIED"), obj_val=info.pobj,
+                dual_obj_val=info.dobj, primal_feas=info.rp, dual_feas=info.rd, gap=info.gap,
+                abs_primal=info.ap, abs_dual=info.ad, primal_weight=info.weight)
+
+
+def load_ref(kind: str):
+    """The reference's compiled CPU module ``hello_ot_cpp._scan`` / ``._lp``."""
+    if not (REF_DIR / "hello_ot_cpp" / "__init__.py").exists():
+        raise RuntimeError("reference CPU backend not built: run `make -C oracle ref`")
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    return importlib.import_module(f"hello_ot_cpp._{kind}")

@@ -1,0 +1,119 @@
+"""Pin the oracle against the reference's own outputs (tests/golden/*.npz).
+
+The fixtures were produced by tests/golden/make_golden.py from the reference
+package and its C++ backend compiled from the reference sources.  These tests
+need no GPU and no reference checkout.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from parity import check_stats, check_topk, flatten, l2sq_error_bound, norm_error_bound
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _load(name):
+    with np.load(GOLDEN / name, allow_pickle=False) as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("scan_l2sq_*.npz")))
+def test_l2sq_scan_oracle_matches_reference(oracle, path):
+    z = _load(path)
+    x, y, a, b, f, g, k = z["x"], z["y"], z["a"], z["b"], z["f"], z["g"], int(z["k"])
+    q, n = len(x), len(y)
+    rk, ck = min(k, n), min(k, q)
+    qb, dbb = f - a, g - b
+    rv, ri, cv, ci, stats = oracle.scan("raw", x, y, qb, dbb, a, b, dot_scale=2.0,
+                                        rk=min(rk + 1, n), ck=min(ck + 1, q))
+    if rv.shape[1] == rk:  # no (k+1)-th column available: pad with -inf
+        rv = np.pad(rv, ((0, 0), (0, 1)), constant_values=-np.inf)
+        ri = np.pad(ri, ((0, 0), (0, 1)), constant_values=-1)
+    if cv.shape[1] == ck:
+        cv = np.pad(cv, ((0, 0), (0, 1)), constant_values=-np.inf)
+        ci = np.pad(ci, ((0, 0), (0, 1)), constant_values=-1)
+
+    def score(r, c):
+        return oracle.pair_scores("raw", x, y, qb, dbb, a, b, r, c, dot_scale=2.0)[0]
+
+    def eps(r, c):
+        return l2sq_error_bound(x, y, r, c, 2.0, (a[r], b[c], f[r], g[c]))
+
+    check_topk(z["rv"], z["ri"], rv, ri, score, eps, label=path + ":rows")
+    check_topk(z["cv"], z["ci"], cv, ci, lambda r, c: score(c, r), lambda r, c: eps(c, r), label=path + ":cols")
+    all_r, all_c = np.divmod(np.arange(q * n), n)
+    e = eps(all_r, all_c)
+    s = score(all_r, all_c)
+    check_stats(z["stats"], stats, float(np.sqrt(np.sum((2 * e * (np.abs(s) + e)))) + e.max()),
+                int(np.sum(np.abs(s) <= e)), label=path)
+    # candidate flattening order of the reference CPU scan
+    rows, cols = flatten(z["rv"], z["ri"], z["cv"], z["ci"])
+    assert np.array_equal(rows, z["rows"]) and np.array_equal(cols, z["cols"])
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("scan_*.npz")
+                                        if not p.name.startswith("scan_l2sq_")))
+def test_norm_scan_oracle_matches_reference(oracle, path):
+    z = _load(path)
+    kind, x, y, f, g, k = str(z["kind"]), z["x"], z["y"], z["f"], z["g"], int(z["k"])
+    q, n = len(x), len(y)
+    rk, ck = min(k, n), min(k, q)
+    rv, ri, cv, ci, stats = oracle.scan(kind, x, y, f, g, rk=rk, ck=ck)
+    rows, cols = flatten(rv, ri, cv, ci)
+    ours = set(zip(rows.tolist(), cols.tolist()))
+    ref = set(zip(z["rows"].tolist(), z["cols"].tolist()))
+    diff = np.array(sorted(ours ^ ref), dtype=np.int64).reshape(-1, 2)
+    if diff.size:
+        s, _ = oracle.pair_scores(kind, x, y, f, g, None, None, diff[:, 0], diff[:, 1])
+        e = norm_error_bound(kind, x, y, diff[:, 0], diff[:, 1], f, g)
+        # a pair may only differ when its score is within the error band of the θ=0 cut
+        # or of its row's / column's k-th score
+        full_r, _, full_c, _, _ = oracle.scan(kind, x, y, f, g, rk=rk, ck=ck)
+        near = (np.abs(s) <= 2 * e) | (np.abs(s - full_r[diff[:, 0], rk - 1]) <= 2 * e) \
+            | (np.abs(s - full_c[diff[:, 1], ck - 1]) <= 2 * e)
+        assert near.all(), f"{path}: {int((~near).sum())} unexplained candidate differences"
+    all_r, all_c = np.divmod(np.arange(q * n), n)
+    s, _ = oracle.pair_scores(kind, x, y, f, g, None, None, all_r, all_c)
+    e = norm_error_bound(kind, x, y, all_r, all_c, f, g)
+    check_stats(z["stats"], stats, float(np.sqrt(np.sum(2 * e * (np.abs(s) + e)))) + e.max(),
+                int(np.sum(np.abs(s) <= e)), label=path)
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pdlp_*.npz")))
+def test_pdlp_oracle_matches_reference(oracle, path):
+    z = _load(path)
+    x0 = z["x0"] if z["x0"].size else None
+    y0 = z["y0"] if z["y0"].size else None
+    args = (z["rows"], z["cols"], z["costs"], z["source_mass"], z["target_mass"], x0, y0)
+    # 40 iterations, evaluation every 5, tolerance 0: same operation order as the
+    # single-thread reference, so the iterates agree bit for bit
+    r = oracle.pdlp(*args, frequency=5, iteration_limit=40, tolerance=0.0)
+    assert r["iterations"] == 40 and r["termination_reason"] == "ITERATION_LIMIT"
+    assert np.array_equal(r["x"], z["cpp40_x"]) and np.array_equal(r["y"], z["cpp40_y"])
+    assert r["restarts"] == int(z["cpp40_meta"][1])
+    # and within round-off of the Torch restatement
+    np.testing.assert_allclose(r["x"], z["torch40_x"], atol=2e-11, rtol=2e-10)
+    np.testing.assert_allclose(r["y"], z["torch40_y"], atol=2e-11, rtol=2e-10)
+    # converged solve
+    r = oracle.pdlp(*args, frequency=20, iteration_limit=200000, tolerance=1e-7)
+    meta = z["cpp_meta"]
+    assert r["termination_reason"] == str(z["cpp_reason"]) == "OPTIMAL"
+    assert r["iterations"] == int(meta[0]) and r["restarts"] == int(meta[1])
+    assert np.array_equal(r["x"], z["cpp_x"]) and np.array_equal(r["y"], z["cpp_y"])
+    assert r["obj_val"] == meta[2]
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pairs_*.npz")))
+def test_pair_costs_oracle_matches_reference(oracle, path):
+    z = _load(path)
+    x, y, rows, cols = z["x"], z["y"], z["rows"], z["cols"]
+    out = oracle.pair_costs("raw", x, y, rows, cols, z["a"], z["b"], dot_scale=2.0)
+    # the reference evaluates a+b-2<x,y> entirely in fp32
+    e = l2sq_error_bound(x, y, rows, cols, 2.0, (z["a"][rows], z["b"][cols]))
+    e += 4 * 2.0 ** -24 * (np.abs(z["a"][rows]) + np.abs(z["b"][cols]) + np.abs(out))
+    assert np.all(np.abs(out - z["lowrank"]) <= e)
+    for kind in ("l1", "l2", "linf"):
+        got = oracle.pair_costs(kind, x, y, rows, cols)
+        np.testing.assert_allclose(got, z[kind], rtol=1e-13, atol=0)
