@@ -1,0 +1,178 @@
+// extern "C" entry points of libhello_b200.so (declared in include/hello_b200.h).
+// Argument validation, workspace sizing, stream synchronisation and the
+// translation of device status words into HB_* codes live here.
+#include <cstdio>
+#include <string>
+
+#include "../../include/hello_b200.h"
+#include "common.cuh"
+#include "scan_common.cuh"
+
+#include "internal.h"
+
+namespace {
+thread_local std::string g_error;
+
+int fail(int code, const std::string& msg) {
+    g_error = msg;
+    return code;
+}
+
+// Synchronise the stream, then map the scan's device status word.
+int finish(cudaStream_t st, const int* status_dev, const char* what) {
+    int status = 0;
+    if (status_dev) {
+        cudaError_t e = cudaMemcpyAsync(&status, status_dev, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return fail(HB_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail(HB_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    if (status & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, std::string(what) + ": a device-side wait timed out");
+    if (status & hb::kErrBadInput) return fail(HB_BAD_INPUT, std::string(what) + ": index out of range");
+    g_error.clear();
+    return HB_OK;
+}
+
+bool valid_k(int k) { return k >= 0 && k <= 32; }
+}  // namespace
+
+extern "C" {
+
+int hb_abi_version(void) { return HB_ABI_VERSION; }
+
+const char* hb_last_error(void) { return g_error.c_str(); }
+
+size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups) {
+    if (q < 1 || n < 1 || d < 1 || !valid_k(k)) return 0;
+    return hb::l2sq_bytes(q, n, d, k, precision, min_groups);
+}
+
+int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_cost,
+                 const double* y_cost, const double* x_bias, const double* y_bias, int k, double dot_scale,
+                 int compute_stats, int precision, int min_groups, double* row_vals, int32_t* row_idx,
+                 double* col_vals, int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+    if (!x || !y || !x_cost || !y_cost || !x_bias || !y_bias || !workspace)
+        return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
+    if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
+        return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
+    if (!valid_k(k)) return fail(HB_BAD_ARGUMENT, "k must be in 0..32");
+    if (dot_scale != 1.0 && dot_scale != 2.0) return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
+    if (precision != 1 && precision != 3) return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32)");
+    if (k > 0 && (!row_vals || !row_idx || !col_vals || !col_idx)) return fail(HB_BAD_ARGUMENT, "null output pointer");
+    if (compute_stats && !stats5) return fail(HB_BAD_ARGUMENT, "null stats pointer");
+    if (workspace_bytes < hb::l2sq_bytes(q, n, d, k, precision, min_groups))
+        return fail(HB_WORKSPACE, "workspace smaller than hb_l2sq_scan_workspace()");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::string err;
+    int status_host = 0;
+    int rc = hb::l2sq_scan(x, y, q, n, d, x_cost, y_cost, x_bias, y_bias, k, dot_scale, compute_stats, precision,
+                           min_groups, row_vals, row_idx, col_vals, col_idx, stats5, workspace, workspace_bytes,
+                           &status_host, st, err);
+    if (rc) return fail(rc == 3 ? HB_WORKSPACE : rc == 5 ? HB_TENSOR_MAP : HB_LAUNCH, err);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail(HB_CUDA, std::string("l2sq scan: ") + cudaGetErrorString(e));
+    if (status_host & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, "l2sq scan: a device-side wait timed out");
+    g_error.clear();
+    return HB_OK;
+}
+
+size_t hb_norm_scan_workspace(int64_t q, int64_t n, int k) {
+    if (q < 1 || n < 1 || !valid_k(k)) return 0;
+    return hb::norm_bytes(q, n, k);
+}
+
+int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
+                 int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
+                 int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!x || !y || !f || !g || !workspace) return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
+    if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
+        return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
+    if (cost_type < 0 || cost_type > 2) return fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2)");
+    if (!valid_k(k)) return fail(HB_BAD_ARGUMENT, "k must be in 0..32");
+    if (k > 0 && (!row_vals || !row_idx || !col_vals || !col_idx)) return fail(HB_BAD_ARGUMENT, "null output pointer");
+    if (compute_stats && !stats5) return fail(HB_BAD_ARGUMENT, "null stats pointer");
+    if (workspace_bytes < hb::norm_bytes(q, n, k)) return fail(HB_WORKSPACE, "workspace smaller than hb_norm_scan_workspace()");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::string err;
+    int rc = hb::norm_scan(x, y, q, n, d, f, g, cost_type, k, compute_stats, row_vals, row_idx, col_vals, col_idx,
+                           stats5, workspace, workspace_bytes, st, err);
+    if (rc) return fail(rc == 3 ? HB_WORKSPACE : HB_LAUNCH, err);
+    return finish(st, nullptr, "norm scan");
+}
+
+size_t hb_pair_costs_workspace(void) { return 256; }
+
+int hb_pair_costs(int cost_type, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d,
+                  const double* a, const double* b, double dot_scale, const int64_t* rows, const int64_t* cols,
+                  int64_t count, double* out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (cost_type < 0 || cost_type > 3) return fail(HB_BAD_ARGUMENT, "cost_type must be 0..3");
+    if (count < 0 || d < 1 || d >= INT32_MAX || nx < 1 || ny < 1) return fail(HB_BAD_ARGUMENT, "invalid sizes");
+    if (count == 0) { g_error.clear(); return HB_OK; }
+    if (!x || !y || !rows || !cols || !out || !workspace) return fail(HB_BAD_ARGUMENT, "null pointer");
+    if (cost_type == 3 && (!a || !b)) return fail(HB_BAD_ARGUMENT, "bilinear pair costs need a and b");
+    if (cost_type == 3 && dot_scale != 1.0 && dot_scale != 2.0)
+        return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
+    if (workspace_bytes < hb_pair_costs_workspace()) return fail(HB_WORKSPACE, "workspace smaller than 256 bytes");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int* status = static_cast<int*>(workspace);
+    cudaMemsetAsync(status, 0, sizeof(int), st);
+    std::string err;
+    int rc = hb::pair_costs(cost_type, x, y, nx, ny, d, a, b, dot_scale, rows, cols, count, out, status, st, err);
+    if (rc) return fail(rc == 2 ? HB_BAD_ARGUMENT : HB_LAUNCH, err);
+    return finish(st, status, "pair costs");
+}
+
+size_t hb_restricted_ot_workspace(int64_t n, int64_t m, int64_t e) {
+    if (n < 1 || m < 1 || e < 1) return 0;
+    return hb::pdlp_bytes(n, m, e);
+}
+
+int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const double* costs, int64_t e,
+                           const double* masses, int64_t n, int64_t m, const double* x0, const double* y0,
+                           const hb_pdlp_controls* controls, double* x_out, double* y_out, hb_pdlp_info* info,
+                           hb_pdlp_trace_row* trace, int32_t trace_capacity, int32_t* trace_length,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    if (!rows || !cols || !costs || !masses || !controls || !x_out || !y_out || !info || !workspace)
+        return fail(HB_BAD_ARGUMENT, "null pointer");
+    if (workspace_bytes < hb::pdlp_bytes(n, m, e))
+        return fail(HB_WORKSPACE, "workspace smaller than hb_restricted_ot_workspace()");
+    hb::PdlpControls ctl;
+    ctl.frequency = controls->evaluation_frequency;
+    ctl.time_limit = controls->time_limit_seconds;
+    ctl.iteration_limit = controls->iteration_limit;
+    ctl.tol_objective = controls->tol_objective;
+    ctl.tol_primal = controls->tol_primal;
+    ctl.tol_dual = controls->tol_dual;
+    ctl.rescale = controls->scalar_rescaling;
+    ctl.weight0 = controls->initial_primal_weight;
+    hb::PdlpResult r{};
+    static_assert(sizeof(hb::TraceRow) == sizeof(hb_pdlp_trace_row), "trace row layout");
+    int tlen = 0;
+    std::string err;
+    int rc = hb::pdlp_solve(rows, cols, costs, e, masses, n, m, x0, y0, ctl, x_out, y_out, &r,
+                            reinterpret_cast<hb::TraceRow*>(trace), trace ? trace_capacity : 0, &tlen, workspace,
+                            workspace_bytes, static_cast<cudaStream_t>(stream), err);
+    if (rc) return fail(rc == 2 ? HB_BAD_INPUT : rc == 3 ? HB_WORKSPACE : HB_CUDA, err);
+    info->iterations = r.iterations;
+    info->restarts = r.restarts;
+    info->termination = r.reason;
+    info->pad = 0;
+    info->primal_objective = r.pobj;
+    info->dual_objective = r.dobj;
+    info->abs_primal_residual = r.ap;
+    info->rel_primal_residual = r.rp;
+    info->abs_dual_residual = r.ad;
+    info->rel_dual_residual = r.rd;
+    info->rel_gap = r.gap;
+    info->primal_weight = r.weight;
+    info->cost_norm = r.cost_norm;
+    info->mass_norm = r.mass_norm;
+    info->setup_seconds = r.setup_seconds;
+    info->iteration_seconds = r.iteration_seconds;
+    if (trace_length) *trace_length = tlen;
+    g_error.clear();
+    return HB_OK;
+}
+
+}  // extern "C"

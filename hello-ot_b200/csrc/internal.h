@@ -1,0 +1,54 @@
+// Internal host-side interface between the kernel files and abi.cu.
+#pragma once
+#include <cstdint>
+#include <string>
+
+#include <cuda_runtime.h>
+
+namespace hb {
+
+// ℓ2² scan (scan_l2sq.cu)
+size_t l2sq_bytes(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
+int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* nx, const double* ny,
+              const double* qb, const double* dbb, int k, double dot_scale, int want_stats, int precision,
+              int min_groups, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws, size_t ws_bytes,
+              int* status_out, cudaStream_t st, std::string& err);
+
+// norm scans (scan_norm.cu)
+size_t norm_bytes(int64_t q, int64_t n, int k);
+int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
+              int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
+              size_t ws_bytes, cudaStream_t st, std::string& err);
+
+// partial top-k merge (scan_l2sq.cu)
+cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
+                      cudaStream_t st);
+
+// pair costs (pairs.cu)
+int pair_costs(int kind, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d, const double* a,
+               const double* b, double scale, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
+               int* status, cudaStream_t st, std::string& err);
+
+// restricted-OT PDHG (pdlp.cu)
+struct PdlpControls {
+    int frequency;
+    double time_limit;
+    int64_t iteration_limit;
+    double tol_objective, tol_primal, tol_dual;
+    int rescale;
+    double weight0;  // > 0: initial primal weight instead of the norm ratio
+};
+struct PdlpResult {
+    int64_t iterations, restarts;
+    int reason;  // 1 OPTIMAL, 2 ITERATION_LIMIT, 3 NUMERICAL_DIVERGENCE, 4 TIME_LIMIT
+    double pobj, dobj, ap, rp, ad, rd, gap, weight, cost_norm, mass_norm;
+    double setup_seconds, iteration_seconds;
+};
+struct TraceRow { double iteration, pobj, dobj, rp, rd, gap, weight; };
+size_t pdlp_bytes(int64_t n, int64_t m, int64_t e);
+int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, int64_t e, const double* masses,
+               int64_t n, int64_t m, const double* x0, const double* y0, const PdlpControls& ctl, double* x_out,
+               double* y_out, PdlpResult* res, TraceRow* trace, int trace_cap, int* trace_len, void* ws,
+               size_t ws_bytes, cudaStream_t st, std::string& err);
+
+}  // namespace hb

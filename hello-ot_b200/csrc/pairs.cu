@@ -1,0 +1,133 @@
+// Active-support pair costs (SDDMM): one cost per (row, col) edge.
+//
+// ℓ2²: c_e = (a_r + b_c) - s<x_r, y_c>   replaces the CSR-blocked
+//      torch.sparse.sampled_addmm of src/hello_ot/costs/pairs.py:221-440
+// ℓ1 / ℓ∞ / ℓ2: fp64 accumulation of (double)y - (double)x per feature,
+//      replaces gcost_sparse_pairs_kernel,
+//      src/hello_ot/_native/norm_cost_scan/norm_cost_scan_kernel.cu:234-245
+//
+// All arithmetic is fp64 on the fp32 features (products of two fp32 values are
+// exact in fp64).  A group of G lanes serves one edge and reads the two
+// feature rows with 128-bit loads when the rows are 16-byte aligned; the
+// group reduces with a fixed xor-shuffle tree, so results are deterministic.
+// HBM-bound: every edge gathers its database row once.
+#include <string>
+
+#include "common.cuh"
+
+namespace hb {
+namespace pairs {
+
+template <int KIND>
+__device__ __forceinline__ double step(double acc, float a, float b) {
+    if (KIND == 3) return fma((double)a, (double)b, acc);
+    const double z = (double)b - (double)a;
+    if (KIND == 0) return acc + fabs(z);
+    if (KIND == 1) return fmax(acc, fabs(z));
+    return fma(z, z, acc);
+}
+
+template <int KIND>
+__device__ __forceinline__ double combine(double a, double b) {
+    return KIND == 1 ? fmax(a, b) : a + b;
+}
+
+template <int KIND, int G, bool VEC>
+__global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, const float* __restrict__ y, int64_t nx,
+                                                   int64_t ny, int d, const double* __restrict__ a,
+                                                   const double* __restrict__ b, double scale,
+                                                   const int64_t* __restrict__ rows, const int64_t* __restrict__ cols,
+                                                   int64_t count, double* __restrict__ out, int* status) {
+    // warp-uniform loop: each warp takes 32/G consecutive edges per step
+    const int lane = threadIdx.x & 31, sub = lane & (G - 1);
+    const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    constexpr int EPW = 32 / G;
+    for (int64_t eb = warp_id * EPW; eb < count; eb += warps * EPW) {
+        const int64_t e = eb + lane / G;
+        const bool live = e < count;
+        const int64_t r = live ? rows[e] : 0, c = live ? cols[e] : 0;
+        const bool ok = live && r >= 0 && r < nx && c >= 0 && c < ny;
+        double acc = 0.0;
+        if (ok) {
+            const float* xr = x + r * d;
+            const float* yc = y + c * d;
+            if (VEC) {
+                const float4* x4 = reinterpret_cast<const float4*>(xr);
+                const float4* y4 = reinterpret_cast<const float4*>(yc);
+                for (int k = sub; k < d / 4; k += G) {
+                    const float4 u = __ldg(x4 + k), v = __ldg(y4 + k);
+                    acc = step<KIND>(acc, u.x, v.x);
+                    acc = step<KIND>(acc, u.y, v.y);
+                    acc = step<KIND>(acc, u.z, v.z);
+                    acc = step<KIND>(acc, u.w, v.w);
+                }
+            } else {
+                for (int k = sub; k < d; k += G) acc = step<KIND>(acc, __ldg(xr + k), __ldg(yc + k));
+            }
+        }
+#pragma unroll
+        for (int off = G / 2; off > 0; off >>= 1) acc = combine<KIND>(acc, __shfl_xor_sync(0xffffffffu, acc, off, G));
+        if (sub == 0 && live) {
+            if (!ok) {
+                atomicOr(status, kErrBadInput);
+                out[e] = __longlong_as_double(0x7ff8000000000000LL);
+            } else if (KIND == 3) {
+                out[e] = (a[r] + b[c]) - scale * acc;
+            } else {
+                out[e] = KIND == 2 ? sqrt(acc) : acc;
+            }
+        }
+    }
+}
+
+template <int KIND, int G>
+void launch_g(bool vec, const float* x, const float* y, int64_t nx, int64_t ny, int d, const double* a,
+              const double* b, double s, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
+              int* status, int blocks, cudaStream_t st) {
+    if (vec) pair_kernel<KIND, G, true><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status);
+    else pair_kernel<KIND, G, false><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status);
+}
+
+template <int KIND>
+void launch_kind(const float* x, const float* y, int64_t nx, int64_t ny, int d, const double* a, const double* b,
+                 double s, const int64_t* rows, const int64_t* cols, int64_t count, double* out, int* status,
+                 cudaStream_t st, int sms) {
+    const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0);
+    const int chunks = vec ? d / 4 : d;  // loads per edge
+    const int g = chunks <= 1 ? 1 : chunks <= 2 ? 2 : chunks <= 4 ? 4 : chunks <= 8 ? 8 : chunks <= 16 ? 16 : 32;
+    int64_t want = (count * g + 255) / 256;
+    const int64_t cap = (int64_t)sms * 16;
+    const int blocks = (int)(want < 1 ? 1 : (want > cap ? cap : want));
+    switch (g) {
+        case 1: launch_g<KIND, 1>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+        case 2: launch_g<KIND, 2>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+        case 4: launch_g<KIND, 4>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+        case 8: launch_g<KIND, 8>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+        case 16: launch_g<KIND, 16>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+        default: launch_g<KIND, 32>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+    }
+}
+
+}  // namespace pairs
+
+int pair_costs(int kind, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d, const double* a,
+               const double* b, double scale, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
+               int* status, cudaStream_t st, std::string& err) {
+    if (count == 0) return 0;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    switch (kind) {
+        case 0: pairs::launch_kind<0>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
+        case 1: pairs::launch_kind<1>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
+        case 2: pairs::launch_kind<2>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
+        case 3: pairs::launch_kind<3>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
+        default: err = "unknown pair cost kind"; return 2;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+    return 0;
+}
+
+}  // namespace hb

@@ -1,0 +1,543 @@
+// Restricted-OT Halpern-PDHG on the GPU, matrix-free over the active support.
+//
+// Restates the reference's restricted-OT PDLP
+// (src/hello_ot/_native/cpp/solver.cpp:39-381, the same algorithm as
+// src/hello_ot/_internal/lp/torch_restricted_ot.py:105-390) and replaces the
+// cuPDLPx CSR SpMV + update kernels used behind backend="native"
+// (src/hello_ot/_native/cupdlpx/cupdlpx/solver.cu:581-700, utils.cu:87-385).
+//
+// Layout in HBM: edges sorted by (source row, original index), so a source
+// row's edges are contiguous; a target's incident edges are kept as a list of
+// positions in that order, sorted by original edge index.  Per iteration two
+// kernels run: the source pass (primal update, reflection, Halpern averaging
+// and the source dual update, a warp per source row) and the target pass
+// (the target dual update, a warp per target).  Each node's incident sum is
+// accumulated sequentially in the reference's edge order and this file is
+// compiled without fma contraction, so with the same step sizes one block of
+// iterations reproduces the reference arithmetic bit for bit.
+//
+// Control (evaluation every `frequency` iterations, adaptive restarts, PID
+// primal weight, termination) runs on the host exactly as solver.cpp:157-312;
+// the host reads a handful of reduced scalars once per evaluation.
+#include <cub/device/device_radix_sort.cuh>
+
+#include <chrono>
+#include <cmath>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "scan_common.cuh"
+
+namespace hb {
+namespace pdlp {
+
+constexpr int RED_BLOCKS = 1184;  // reduction partial slots (8 per SM on a B200)
+constexpr int RED_THREADS = 256;
+
+struct Dev {
+    int n, m, nodes;
+    int64_t e;
+    int* e_row;     // source of each sorted edge
+    int* e_col;     // target of each sorted edge
+    int* e_orig;    // original index of each sorted edge
+    int* s_off;     // [n+1] source offsets into the sorted edges
+    int* t_off;     // [m+1] target offsets into t_pos
+    int* t_pos;     // sorted-edge positions of each target's edges, by original index
+    double *cost, *cs, *ax, *x, *px, *rx, *dx;  // per sorted edge
+    double *mass, *scale, *bs, *ns, *ay, *y, *py, *dy, *td;
+    double* red;    // [RED_BLOCKS][8]
+    double* scal;   // [16] reduced scalars
+    int* status;
+};
+
+__device__ __forceinline__ double max0(double v) { return v < 0.0 ? 0.0 : v; }  // std::max(v, 0.0)
+
+// Sequential (lane-order) sum over a warp's values; identical on every lane.
+__device__ __forceinline__ double ordered_warp_sum(double acc, double v, int count) {
+    for (int l = 0; l < count; ++l) acc += __shfl_sync(0xffffffffu, v, l);
+    return acc;
+}
+
+// ------------------------------------------------------------------ setup
+__global__ void iota_kernel(int* v, int64_t e) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < e; i += (int64_t)gridDim.x * blockDim.x)
+        v[i] = (int)i;
+}
+
+__global__ void check_convert(const int64_t* rows, const int64_t* cols, int64_t e, int n, int m, int* r32, int* c32,
+                              int* status) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < e; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = rows[i], c = cols[i];
+        if (r < 0 || r >= n || c < 0 || c >= m) { atomicOr(status, kErrBadInput); r32[i] = 0; c32[i] = 0; }
+        else { r32[i] = (int)r; c32[i] = (int)c; }
+    }
+}
+
+// offsets[k] = first position whose key is >= k (keys sorted ascending)
+__global__ void offsets_kernel(const int* keys, int64_t e, int nkeys, int* off) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k <= nkeys; k += (int64_t)gridDim.x * blockDim.x) {
+        int64_t lo = 0, hi = e;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (keys[mid] < k) lo = mid + 1; else hi = mid;
+        }
+        off[k] = (int)lo;
+    }
+}
+
+__global__ void gather_edges(const int* order, const int* c32, const double* costs, const double* x0, int64_t e,
+                             int* e_col, double* cost, double* x0s, int* inv) {
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < e; p += (int64_t)gridDim.x * blockDim.x) {
+        const int o = order[p];
+        e_col[p] = c32[o];
+        cost[p] = costs[o];
+        x0s[p] = x0 ? x0[o] : 0.0;
+        inv[o] = (int)p;
+    }
+}
+
+__global__ void map_positions(const int* t_orig, const int* inv, int64_t e, int* t_pos) {
+    for (int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; s < e; s += (int64_t)gridDim.x * blockDim.x)
+        t_pos[s] = inv[t_orig[s]];
+}
+
+// Block-partial sums of squares of two vectors (a over na, b over nb).
+__global__ void sumsq2_kernel(const double* a, int64_t na, const double* b, int64_t nb, double* red) {
+    __shared__ double sh[2][RED_THREADS];
+    double sa = 0, sb = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na; i += (int64_t)gridDim.x * blockDim.x) sa += a[i] * a[i];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb; i += (int64_t)gridDim.x * blockDim.x) sb += b[i] * b[i];
+    sh[0][threadIdx.x] = sa; sh[1][threadIdx.x] = sb;
+    __syncthreads();
+    for (int w = RED_THREADS / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) { sh[0][threadIdx.x] += sh[0][threadIdx.x + w]; sh[1][threadIdx.x] += sh[1][threadIdx.x + w]; }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) { red[blockIdx.x * 8 + 0] = sh[0][0]; red[blockIdx.x * 8 + 1] = sh[1][0]; }
+}
+
+// Fixed-order sum of the block partials: scal[base + j] = sum_b red[b][j], j < cnt.
+__global__ void finish_red(const double* red, int blocks, int cnt, double* scal, int base) {
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < cnt; ++j) {
+            double s = 0;
+            for (int b = 0; b < blocks; ++b) s += red[b * 8 + j];
+            scal[base + j] = s;
+        }
+    }
+}
+
+__global__ void degree_scale(const int* s_off, const int* t_off, int n, int m, double* scale) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n + m; i += gridDim.x * blockDim.x) {
+        const int deg = i < n ? s_off[i + 1] - s_off[i] : t_off[i - n + 1] - t_off[i - n];
+        scale[i] = sqrt((double)(deg > 1 ? deg : 1));
+    }
+}
+
+// solver.cpp:96-109
+__global__ void init_state(Dev D, const double* masses, const double* y0, const double* x0s, double bound,
+                           double objective, double variable) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
+        D.cs[p] = D.cost[p] * objective / variable;
+        const double a = max0(x0s[p]) * variable * bound;
+        D.ax[p] = a; D.x[p] = a; D.px[p] = a;
+    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < D.nodes; i += stride) {
+        D.mass[i] = masses[i];
+        D.bs[i] = masses[i] * bound / D.scale[i];
+        D.ns[i] = variable * D.scale[i];
+        const double a = (y0 ? y0[i] : 0.0) * D.scale[i] * objective;
+        D.ay[i] = a; D.y[i] = a; D.py[i] = a;
+        if (i >= D.n) D.td[i - D.n] = a / D.ns[i];
+    }
+}
+
+// ------------------------------------------------------------------ iteration
+struct Step {
+    double primal_step, dual_step, halpern;
+    int checkpoint, major;
+};
+
+// Source pass: primal update of every edge and the source dual update
+// (solver.cpp:255-271).  One warp per source row.
+__global__ void __launch_bounds__(256) source_pass(Dev D, Step s) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < D.n; i += warps) {
+        const double sdual = D.y[i] / D.ns[i];
+        const int b0 = D.s_off[i], b1 = D.s_off[i + 1];
+        double sum = 0.0;
+        for (int base = b0; base < b1; base += 32) {
+            const int p = base + lane;
+            double r = 0.0;
+            if (p < b1) {
+                const double at = sdual + D.td[D.e_col[p]];
+                const double xv = D.x[p];
+                const double pxv = max0(xv - s.primal_step * (D.cs[p] - at));
+                r = 2.0 * pxv - xv;
+                if (s.checkpoint) D.dx[p] = r - xv;
+                D.x[p] = s.halpern * r + (1.0 - s.halpern) * D.ax[p];
+                D.rx[p] = r;
+                if (s.major) D.px[p] = pxv;
+            }
+            sum = ordered_warp_sum(sum, r, min(32, b1 - base));
+        }
+        if (lane == 0) {
+            const double yv = D.y[i];
+            const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+            const double refl = 2.0 * pyv - yv;
+            if (s.checkpoint) D.dy[i] = refl - yv;
+            D.y[i] = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+            if (s.major) D.py[i] = pyv;
+        }
+    }
+}
+
+// Target pass: target dual update from the reflected primal (solver.cpp:273-281).
+__global__ void __launch_bounds__(256) target_pass(Dev D, Step s) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    for (int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < D.m; j += warps) {
+        const int b0 = D.t_off[j], b1 = D.t_off[j + 1];
+        double sum = 0.0;
+        for (int base = b0; base < b1; base += 32) {
+            const int sl = base + lane;
+            const double r = sl < b1 ? D.rx[D.t_pos[sl]] : 0.0;
+            sum = ordered_warp_sum(sum, r, min(32, b1 - base));
+        }
+        if (lane == 0) {
+            const int i = D.n + j;
+            const double yv = D.y[i];
+            const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+            const double refl = 2.0 * pyv - yv;
+            if (s.checkpoint) D.dy[i] = refl - yv;
+            const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+            D.y[i] = ynew;
+            if (s.major) D.py[i] = pyv;
+            D.td[j] = ynew / D.ns[i];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ reductions
+template <int CNT>
+__device__ __forceinline__ void block_store(double (&v)[CNT], double* red) {
+    __shared__ double sh[CNT][RED_THREADS];
+#pragma unroll
+    for (int j = 0; j < CNT; ++j) sh[j][threadIdx.x] = v[j];
+    __syncthreads();
+    for (int w = RED_THREADS / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w)
+#pragma unroll
+            for (int j = 0; j < CNT; ++j) sh[j][threadIdx.x] += sh[j][threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+#pragma unroll
+        for (int j = 0; j < CNT; ++j) red[blockIdx.x * 8 + j] = sh[j][0];
+}
+
+// Residuals of the unscaled problem (solver.cpp:115-136):
+// [0] sum of squared marginal errors, [1] sum of squared dual violations,
+// [2] primal objective, [3] dual objective.
+__global__ void __launch_bounds__(RED_THREADS) evaluate_kernel(Dev D, double vb, double objective) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    double v[4] = {0, 0, 0, 0};
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < D.nodes; i += warps) {
+        const bool src = i < D.n;
+        const int b0 = src ? D.s_off[i] : D.t_off[i - D.n], b1 = src ? D.s_off[i + 1] : D.t_off[i - D.n + 1];
+        double sum = 0.0;
+        for (int base = b0; base < b1; base += 32) {
+            const int sl = base + lane;
+            const double r = sl < b1 ? D.px[src ? sl : D.t_pos[sl]] / vb : 0.0;
+            sum = ordered_warp_sum(sum, r, min(32, b1 - base));
+        }
+        if (lane == 0) {
+            const double delta = sum - D.mass[i];
+            v[0] += delta * delta;
+            v[3] += D.mass[i] * (D.py[i] / (D.scale[i] * objective));
+        }
+    }
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
+        const int r = D.e_row[p], c = D.n + D.e_col[p];
+        const double score = D.py[r] / (D.scale[r] * objective) + D.py[c] / (D.scale[c] * objective) - D.cost[p];
+        const double viol = max0(score);
+        v[1] += viol * viol;
+        v[2] += D.cost[p] * (D.px[p] / vb);
+    }
+    block_store<4>(v, D.red);
+}
+
+// Restart distances: [0] |px - ax|^2, [1] |py - ay|^2 (solver.cpp:203-213).
+__global__ void __launch_bounds__(RED_THREADS) restart_dist_kernel(Dev D) {
+    double v[2] = {0, 0};
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
+        const double t = D.px[p] - D.ax[p];
+        v[0] += t * t;
+    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < D.nodes; i += stride) {
+        const double t = D.py[i] - D.ay[i];
+        v[1] += t * t;
+    }
+    block_store<2>(v, D.red);
+}
+
+// Restart to the last PDHG iterate (solver.cpp:238-242).
+__global__ void restart_kernel(Dev D) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
+        const double v = D.px[p];
+        D.ax[p] = v; D.x[p] = v;
+    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < D.nodes; i += stride) {
+        const double v = D.py[i];
+        D.ay[i] = v; D.y[i] = v;
+        if (i >= D.n) D.td[i - D.n] = v / D.ns[i];
+    }
+}
+
+// Fixed-point error terms (solver.cpp:286-294): [0] |dx|^2, [1] |dy|^2,
+// [2] interaction sum (dy_r/ns_r + dy_c/ns_c) dx.
+__global__ void __launch_bounds__(RED_THREADS) fixed_point_kernel(Dev D) {
+    double v[3] = {0, 0, 0};
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
+        const int r = D.e_row[p], c = D.n + D.e_col[p];
+        const double dxv = D.dx[p];
+        v[0] += dxv * dxv;
+        v[2] += (D.dy[r] / D.ns[r] + D.dy[c] / D.ns[c]) * dxv;
+    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < D.nodes; i += stride) v[1] += D.dy[i] * D.dy[i];
+    block_store<3>(v, D.red);
+}
+
+__global__ void output_kernel(Dev D, double vb, double objective, double* x_out, double* y_out) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride)
+        x_out[D.e_orig[p]] = D.px[p] / vb;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < D.nodes; i += stride)
+        y_out[i] = D.py[i] / (D.scale[i] * objective);
+}
+
+}  // namespace pdlp
+
+// ------------------------------------------------------------------ host
+struct PdlpLayout {
+    pdlp::Dev D{};
+    int *r32 = nullptr, *c32 = nullptr, *iota = nullptr, *keys_out = nullptr, *t_orig = nullptr, *t_keys = nullptr,
+        *inv = nullptr;
+    double* x0s = nullptr;
+    void* cub = nullptr;
+    size_t cub_bytes = 0;
+    size_t bytes = 0;
+    bool ok = true;
+};
+
+PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e) {
+    PdlpLayout L;
+    const int64_t nodes = n + m;
+    Arena ar{static_cast<char*>(base), size, 0};
+    auto take_i = [&](int*& p, size_t c) { p = ar.take<int>(c); if (base && !p) L.ok = false; };
+    auto take_d = [&](double*& p, size_t c) { p = ar.take<double>(c); if (base && !p) L.ok = false; };
+    pdlp::Dev& D = L.D;
+    take_i(D.e_row, e); take_i(D.e_col, e); take_i(D.e_orig, e); take_i(D.s_off, n + 1); take_i(D.t_off, m + 1);
+    take_i(D.t_pos, e);
+    take_d(D.cost, e); take_d(D.cs, e); take_d(D.ax, e); take_d(D.x, e); take_d(D.px, e); take_d(D.rx, e);
+    take_d(D.dx, e);
+    take_d(D.mass, nodes); take_d(D.scale, nodes); take_d(D.bs, nodes); take_d(D.ns, nodes); take_d(D.ay, nodes);
+    take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m);
+    take_d(D.red, (size_t)pdlp::RED_BLOCKS * 8); take_d(D.scal, 16);
+    take_i(D.status, 1);
+    take_i(L.r32, e); take_i(L.c32, e); take_i(L.iota, e); take_i(L.keys_out, e); take_i(L.t_orig, e);
+    take_i(L.t_keys, e); take_i(L.inv, e);
+    take_d(L.x0s, e);
+    size_t cub_bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, cub_bytes, (const int*)nullptr, (int*)nullptr, (const int*)nullptr,
+                                    (int*)nullptr, (int)e);
+    L.cub_bytes = cub_bytes;
+    L.cub = ar.take<char>(cub_bytes > 0 ? cub_bytes : 1);
+    if (base && !L.cub) L.ok = false;
+    L.bytes = ar.used + 256;
+    return L;
+}
+
+size_t pdlp_bytes(int64_t n, int64_t m, int64_t e) { return pdlp_layout(nullptr, 0, n, m, e).bytes; }
+
+int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, int64_t e, const double* masses,
+               int64_t n, int64_t m, const double* x0, const double* y0, const PdlpControls& ctl, double* x_out,
+               double* y_out, PdlpResult* res, TraceRow* trace, int trace_cap, int* trace_len, void* ws,
+               size_t ws_bytes, cudaStream_t st, std::string& err) {
+    using Clock = std::chrono::steady_clock;
+    const auto started = Clock::now();
+    if (n < 1 || m < 1 || e < 1 || e > INT32_MAX - 1 || n + m > INT32_MAX - 1 || ctl.frequency < 1 ||
+        ctl.iteration_limit < 1 || !(ctl.time_limit > 0)) {
+        err = "invalid restricted OT dimensions or runtime limits";
+        return 2;
+    }
+    PdlpLayout L = pdlp_layout(ws, ws_bytes, n, m, e);
+    if (!L.ok) { err = "workspace too small for the restricted OT solve"; return 3; }
+    pdlp::Dev D = L.D;
+    D.n = (int)n; D.m = (int)m; D.nodes = (int)(n + m); D.e = e;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int gb = sms * 8;
+    auto fail = [&](const char* what) {
+        cudaError_t ce = cudaGetLastError();
+        err = std::string(what) + (ce != cudaSuccess ? std::string(": ") + cudaGetErrorString(ce) : std::string());
+        return 6;
+    };
+    cudaMemsetAsync(D.status, 0, sizeof(int), st);
+    // --- incidence structure (solver.cpp:74-90): sort by source, then by target
+    pdlp::check_convert<<<gb, 256, 0, st>>>(rows, cols, e, (int)n, (int)m, L.r32, L.c32, D.status);
+    pdlp::iota_kernel<<<gb, 256, 0, st>>>(L.iota, e);
+    size_t cb = L.cub_bytes;
+    if (cub::DeviceRadixSort::SortPairs(L.cub, cb, L.r32, D.e_row, L.iota, D.e_orig, (int)e, 0, 32, st) != cudaSuccess)
+        return fail("source sort");
+    cb = L.cub_bytes;
+    if (cub::DeviceRadixSort::SortPairs(L.cub, cb, L.c32, L.t_keys, L.iota, L.t_orig, (int)e, 0, 32, st) != cudaSuccess)
+        return fail("target sort");
+    pdlp::offsets_kernel<<<(unsigned)((n + 256) / 256), 256, 0, st>>>(D.e_row, e, (int)n, D.s_off);
+    pdlp::offsets_kernel<<<(unsigned)((m + 256) / 256), 256, 0, st>>>(L.t_keys, e, (int)m, D.t_off);
+    pdlp::gather_edges<<<gb, 256, 0, st>>>(D.e_orig, L.c32, costs, x0, e, D.e_col, D.cost, L.x0s, L.inv);
+    pdlp::map_positions<<<gb, 256, 0, st>>>(L.t_orig, L.inv, e, D.t_pos);
+    pdlp::degree_scale<<<gb, 256, 0, st>>>(D.s_off, D.t_off, (int)n, (int)m, D.scale);
+    // --- norms and scaling (solver.cpp:91-110)
+    double h[16];
+    pdlp::sumsq2_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(masses, n + m, costs, e, D.red);
+    pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
+    if (cudaGetLastError() != cudaSuccess) return fail("setup");
+    cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
+    int status = 0;
+    cudaMemcpyAsync(&status, D.status, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return fail("setup sync");
+    if (status & kErrBadInput) { err = "active-support endpoint index is out of bounds"; return 2; }
+    const double mass_norm = std::sqrt(h[0]), cost_norm = std::sqrt(h[1]);
+    const double bound = ctl.rescale ? 1.0 / std::max(1.0, mass_norm) : 1.0;
+    const double objective = ctl.rescale ? 1.0 / std::max(1.0, cost_norm) : 1.0;
+    const double variable = std::sqrt(2.0);
+    const double vb = variable * bound;
+    pdlp::init_state<<<gb, 256, 0, st>>>(D, masses, y0, L.x0s, bound, objective, variable);
+    double weight = 1.0;
+    if (!ctl.rescale) {
+        pdlp::sumsq2_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D.cs, e, D.bs, n + m, D.red);
+        pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
+        cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail("weight sync");
+        weight = std::max(std::sqrt(h[0]) / std::max(std::sqrt(h[1]), 1e-16), 1e-16);
+    }
+    if (ctl.weight0 > 0) weight = ctl.weight0;
+    const double setup_seconds = std::chrono::duration<double>(Clock::now() - started).count();
+    const auto iter_started = Clock::now();
+    // --- control loop (solver.cpp:157-312)
+    const double inf = std::numeric_limits<double>::infinity();
+    double best_weight = weight, error_sum = 0.0, best_balance = inf, initial_error = inf, last_trial = inf,
+           fixed = inf;
+    int64_t count = 0, inner = 0, restarts = 0;
+    int reason = 0;
+    double pobj = 0, dobj = 0, ap = 0, rp = 0, ad = 0, rd = 0, gap = 0;
+    bool restart = false;
+    int tlen = 0;
+    const int F = ctl.frequency;
+    for (;;) {
+        pdlp::evaluate_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D, vb, objective);
+        pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 4, D.scal, 0);
+        if (cudaGetLastError() != cudaSuccess) return fail("evaluate");
+        cudaMemcpyAsync(h, D.scal, 16 * sizeof(double), cudaMemcpyDeviceToHost, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail("evaluate sync");
+        if (count > 0) {
+            // fixed-point errors of the block just run (solver.cpp:304-306), with that block's weight
+            auto fpe = [&](int b) {
+                const double sq = h[b] * weight + h[b + 1] / weight + 2.0 * 0.998 * h[b + 2];
+                return std::sqrt(std::max(0.0, sq));
+            };
+            fixed = fpe(9);
+            if (restart) initial_error = F == 1 ? fixed : fpe(5);
+        }
+        ap = std::sqrt(h[0]);
+        ad = std::sqrt(h[1]);
+        pobj = h[2];
+        dobj = h[3];
+        rp = ap / (1.0 + mass_norm);
+        rd = ad / (1.0 + cost_norm);
+        gap = std::abs(pobj - dobj) / (1.0 + std::abs(pobj) + std::abs(dobj));
+        if (trace && tlen < trace_cap) trace[tlen++] = {(double)count, pobj, dobj, rp, rd, gap, weight};
+        const bool finite = std::isfinite(pobj) && std::isfinite(dobj) && std::isfinite(ap) && std::isfinite(rp) &&
+                            std::isfinite(ad) && std::isfinite(rd) && std::isfinite(gap);
+        if (!finite || !std::isfinite(weight)) reason = 3;
+        else if (rp < ctl.tol_primal && rd < ctl.tol_dual && gap < ctl.tol_objective) reason = 1;
+        else if (count >= ctl.iteration_limit) reason = 2;
+        else if (std::chrono::duration<double>(Clock::now() - started).count() >= ctl.time_limit) reason = 4;
+        if (reason) break;
+        restart = false;
+        if (count == F) restart = true;
+        else if (count > F)
+            restart = inner >= 0.36 * count || fixed <= 0.2 * initial_error ||
+                      (fixed <= 0.5 * initial_error && fixed > last_trial);
+        last_trial = fixed;
+        if (restart) {
+            pdlp::restart_dist_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);
+            pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
+            cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
+            if (cudaStreamSynchronize(st) != cudaSuccess) return fail("restart sync");
+            const double pd = std::sqrt(h[0]), dd = std::sqrt(h[1]);
+            const double ratio = rd / std::max(rp, 1e-300);
+            if (pd > 1e-16 && pd < 1e12 && dd > 1e-16 && dd < 1e12 && ratio > 1e-8 && ratio < 1e8) {
+                const double error = std::log(dd) - std::log(pd) - std::log(weight);
+                error_sum = 0.3 * error_sum + error;
+                weight *= std::exp(0.99 * error + 0.01 * error_sum);
+            } else {
+                weight = best_weight;
+                error_sum = 0;
+            }
+            if (rp > 0 && rd > 0) {
+                const double balance = std::abs(std::log10(rd / rp));
+                if (balance < best_balance) { best_balance = balance; best_weight = weight; }
+            }
+            inner = 0;
+            last_trial = inf;
+            ++restarts;
+            pdlp::restart_kernel<<<gb, 256, 0, st>>>(D);
+        }
+        const double primal_step = 0.998 / weight, dual_step = 0.998 * weight;
+        for (int t = 0; t < F; ++t) {
+            pdlp::Step s;
+            s.primal_step = primal_step;
+            s.dual_step = dual_step;
+            s.halpern = double(inner + 1) / double(inner + 2);
+            s.major = ((count + 1) % F) == 0;
+            const bool is_restart = t == 0 && restart;
+            s.checkpoint = s.major || is_restart;
+            pdlp::source_pass<<<gb, 256, 0, st>>>(D, s);
+            pdlp::target_pass<<<gb, 256, 0, st>>>(D, s);
+            if (s.checkpoint) {
+                pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);
+                // scal[5..7]: terms at the restart iteration, scal[9..11]: at the major iteration
+                pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 3, D.scal, s.major ? 9 : 5);
+            }
+            ++count;
+            ++inner;
+        }
+        if (cudaGetLastError() != cudaSuccess) return fail("iteration");
+    }
+    pdlp::output_kernel<<<gb, 256, 0, st>>>(D, vb, objective, x_out, y_out);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return fail("output");
+    res->iterations = count;
+    res->restarts = restarts;
+    res->reason = reason;
+    res->pobj = pobj; res->dobj = dobj; res->ap = ap; res->rp = rp; res->ad = ad; res->rd = rd; res->gap = gap;
+    res->weight = weight; res->cost_norm = cost_norm; res->mass_norm = mass_norm;
+    res->setup_seconds = setup_seconds;
+    res->iteration_seconds = std::chrono::duration<double>(Clock::now() - iter_started).count();
+    if (trace_len) *trace_len = tlen;
+    return 0;
+}
+
+}  // namespace hb

@@ -1,0 +1,457 @@
+// ℓ2² (bilinear) full-space pricing scan on the sm_100a tensor cores.
+//
+// Replaces the reference's SGEMM-tile + selection kernels
+// (src/hello_ot/_native/generic_scan/pricing_small.cu:230-304, pricing.cu,
+// matrix_selection.cuh) with one fused persistent kernel per pass:
+//
+//   TMA (128B-swizzled fp32 slabs, local HBM only, no multicast)
+//     -> tcgen05.mma kind::tf32, 128x256 tile, fp32 accumulator in TMEM
+//        (two accumulators: the MMA of tile t+1 overlaps the epilogue of t)
+//     -> epilogue warps: tcgen05.ld, score, certificate sums, row top-k in
+//        registers.  No cost tile is ever written to HBM.
+//
+// Score arithmetic follows the reference raw path (matrix_selection.cuh:20-26):
+//   dot = fp32(s * <x,y>);  cost = (a_i + b_j) - dot;  score = (dot + qb_i) + dbb_j
+// in fp64.  <x,y> is computed either with one TF32 product ("tf32") or as the
+// 3-term split hi*hi + hi*lo + lo*hi ("3xtf32"), hi = x with the low 13
+// mantissa bits dropped and lo = x - hi (exact), which gives an fp32-class dot.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2-5 epilogue (thread = tile row = TMEM lane).
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+#include "scan_common.cuh"
+
+namespace hb {
+namespace l2sq {
+
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192, EPI_FIRST = 64, EPI_THREADS = 128;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+
+struct Params {
+    CUtensorMap qmap[2];  // query operand: [0] features, [1] low parts
+    CUtensorMap dmap[2];  // database operand
+    int qsel[3], dsel[3]; // map used by each product term
+    int nseg, kslabs;
+    int q, n;
+    int groups, tpg, ct, units;
+    const double* q_cost;  // a_i  (certificate only)
+    const double* d_cost;  // b_j
+    const double* q_bias;  // query-side bias
+    const double* d_bias;  // database-side bias
+    float scale;
+    double* part_v;
+    int* part_i;
+    double* cta_stats;
+    int* status;
+};
+
+struct __align__(1024) Smem {
+    uint8_t stage[STAGES][STAGE_BYTES];
+    double dbias[4][BN];  // per epilogue warp: database bias of the current tile
+    double dcost[4][BN];  // per epilogue warp: database |y|^2 of the current tile
+    double red[4 * 5];
+    uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+
+__device__ __forceinline__ void producer(const Params& p, Smem& s) {
+    uint32_t stage = 0, phase = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int rb = u / p.groups, g = u % p.groups;
+        const int ct1 = min(p.ct, (g + 1) * p.tpg);
+        for (int ct = g * p.tpg; ct < ct1; ++ct)
+            for (int sg = 0; sg < p.nseg; ++sg)
+                for (int ks = 0; ks < p.kslabs; ++ks) {
+                    if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.abort, p.status)) return;
+                    uint8_t* a = s.stage[stage];
+                    mbar_arrive_expect_tx(&s.full[stage], STAGE_BYTES);
+                    tma_load_2d(a, &p.qmap[p.qsel[sg]], &s.full[stage], ks * BK, rb * BM);
+                    tma_load_2d(a + A_BYTES, &p.dmap[p.dsel[sg]], &s.full[stage], ks * BK, ct * BN);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+    }
+}
+
+__device__ __forceinline__ void mma_issuer(const Params& p, Smem& s, uint32_t tmem) {
+    uint32_t stage = 0, phase = 0, t = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int g = u % p.groups;
+        const int ct1 = min(p.ct, (g + 1) * p.tpg);
+        for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
+            const uint32_t acc = t & 1, aph = (t >> 1) & 1;
+            if (!mbar_wait(&s.tempty[acc], aph ^ 1, &s.abort, p.status)) return;
+            tc_fence_after();
+            const uint32_t d = tmem + acc * BN;
+            uint32_t accumulate = 0;
+            for (int sg = 0; sg < p.nseg; ++sg)
+                for (int ks = 0; ks < p.kslabs; ++ks) {
+                    if (!mbar_wait(&s.full[stage], phase, &s.abort, p.status)) return;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(s.stage[stage]), b0 = a0 + A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        mma_tf32(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), IDESC, accumulate);
+                        accumulate = 1;
+                    }
+                    mma_commit(&s.empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+            mma_commit(&s.tfull[acc]);
+        }
+    }
+}
+
+template <int K, bool STATS, bool SWAP>
+__device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem, double (&acc)[5]) {
+    constexpr int KK = K > 0 ? K : 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int quarter = warp & 3;          // TMEM lanes this warp may read
+    const int r = quarter * 32 + lane;     // tile row owned by this thread
+    double* wbias = s.dbias[quarter];
+    double* wcost = s.dcost[quarter];
+    TopK<KK> top;
+    uint32_t t = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int rb = u / p.groups, g = u % p.groups;
+        const int ct1 = min(p.ct, (g + 1) * p.tpg);
+        const int row = rb * BM + r;
+        const bool rvalid = row < p.q;
+        const double rbias = rvalid ? p.q_bias[row] : 0.0;
+        const double rcost = (STATS && rvalid) ? p.q_cost[row] : 0.0;
+        top.reset();
+        for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
+            const uint32_t buf = t & 1, aph = (t >> 1) & 1;
+            const int c0 = ct * BN;
+            const int ncols = min(BN, p.n - c0);
+            __syncwarp();  // the warp is done reading the previous tile's staging
+            for (int c = lane; c < BN; c += 32) {
+                const bool ok = c < ncols;
+                wbias[c] = ok ? p.d_bias[c0 + c] : 0.0;
+                if (STATS) wcost[c] = ok ? p.d_cost[c0 + c] : 0.0;
+            }
+            __syncwarp();
+            if (!mbar_wait(&s.tfull[buf], aph, &s.abort, p.status)) return;
+            tc_fence_after();
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+            for (int ch = 0; ch < BN / 32 && ch * 32 < ncols; ++ch) {
+                float v[32];
+                tmem_ld32(taddr + ch * 32, v);
+                tmem_wait_ld();
+                double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int c = ch * 32 + j;
+                    if (c < ncols && rvalid) {
+                        const double dot = (double)(p.scale * v[j]);
+                        const double cb = wbias[c];
+                        const double sc = SWAP ? ((dot + cb) + rbias) : ((dot + rbias) + cb);
+                        if (STATS) {
+                            const double co = (rcost + wcost[c]) - dot;
+                            den4[j & 3] += co * co;
+                            acc[3] = fmax(acc[3], fabs(co));
+                            if (sc > 0.0) { num4[j & 3] += sc * sc; acc[2] = fmax(acc[2], sc); acc[4] += 1.0; }
+                        }
+                        if (K > 0) top.offer(sc, c0 + c);
+                    }
+                }
+                if (STATS) {
+                    acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
+                    acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&s.tempty[buf]);
+        }
+        if (K > 0 && rvalid) {
+            double* pv = p.part_v + ((int64_t)g * p.q + row) * KK;
+            int* pi = p.part_i + ((int64_t)g * p.q + row) * KK;
+#pragma unroll
+            for (int j = 0; j < KK; ++j) { pv[j] = top.v[j]; pi[j] = top.i[j]; }
+        }
+    }
+}
+
+template <int K, bool STATS, bool SWAP>
+__global__ void __launch_bounds__(THREADS, 1) scan_kernel(const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], EPI_THREADS); }
+        s.abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&p.qmap[0]); prefetch_tmap(&p.qmap[1]);
+        prefetch_tmap(&p.dmap[0]); prefetch_tmap(&p.dmap[1]);
+    }
+    if (warp == 1) { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+    if (warp == 0) {
+        if (lane == 0) producer(p, s);
+    } else if (warp == 1) {
+        if (lane == 0) mma_issuer(p, s, tmem);
+    } else {
+        double acc[5] = {0, 0, 0, 0, 0};
+        epilogue<K, STATS, SWAP>(p, s, tmem, acc);
+        if (STATS) {  // warp totals in a fixed shuffle order
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const double o0 = __shfl_down_sync(0xffffffffu, acc[0], off);
+                const double o1 = __shfl_down_sync(0xffffffffu, acc[1], off);
+                const double o2 = __shfl_down_sync(0xffffffffu, acc[2], off);
+                const double o3 = __shfl_down_sync(0xffffffffu, acc[3], off);
+                const double o4 = __shfl_down_sync(0xffffffffu, acc[4], off);
+                acc[0] += o0; acc[1] += o1; acc[2] = fmax(acc[2], o2); acc[3] = fmax(acc[3], o3); acc[4] += o4;
+            }
+            if (lane == 0)
+                for (int j = 0; j < 5; ++j) s.red[(warp & 3) * 5 + j] = acc[j];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();  // every role returns here, also after an aborted wait
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+    if (STATS && threadIdx.x == EPI_FIRST) {
+        double a[5] = {0, 0, 0, 0, 0};
+        for (int w = 0; w < 4; ++w) {
+            a[0] += s.red[w * 5 + 0]; a[1] += s.red[w * 5 + 1];
+            a[2] = fmax(a[2], s.red[w * 5 + 2]); a[3] = fmax(a[3], s.red[w * 5 + 3]);
+            a[4] += s.red[w * 5 + 4];
+        }
+        for (int j = 0; j < 5; ++j) p.cta_stats[blockIdx.x * 5 + j] = a[j];
+    }
+}
+
+// Copy features into a TMA-legal layout when needed (row stride a multiple
+// of 16 B) and/or write the low parts x - hi(x), hi(x) = x with its 13 low
+// mantissa bits cleared (the part a kind::tf32 MMA consumes).
+__global__ void prep_kernel(const float* __restrict__ x, int64_t rows, int d, int dp, float* __restrict__ xpad,
+                            float* __restrict__ xlo) {
+    const int64_t total = rows * dp;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / dp;
+        const int c = (int)(e - r * dp);
+        const float v = c < d ? x[r * d + c] : 0.0f;
+        if (xpad) xpad[e] = v;
+        if (xlo) {
+            const float hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+            xlo[e] = v - hi;
+        }
+    }
+}
+
+}  // namespace l2sq
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(ptr);
+    }
+    return fn;
+}
+
+bool make_map(CUtensorMap* m, const float* base, int64_t rows, int dp, int box_rows) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)dp * sizeof(float)};
+    cuuint32_t box[2] = {(cuuint32_t)l2sq::BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int K, bool STATS, bool SWAP>
+cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
+    auto fn = l2sq::scan_kernel<K, STATS, SWAP>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)l2sq::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    fn<<<grid, l2sq::THREADS, l2sq::SMEM_BYTES, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <bool STATS, bool SWAP>
+cudaError_t launch_k(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
+    switch (K) {
+        case 0: return launch_pass<0, STATS, SWAP>(p, grid, st);
+        case 1: return launch_pass<1, STATS, SWAP>(p, grid, st);
+        case 2: return launch_pass<2, STATS, SWAP>(p, grid, st);
+        case 4: return launch_pass<4, STATS, SWAP>(p, grid, st);
+        case 8: return launch_pass<8, STATS, SWAP>(p, grid, st);
+        case 16: return launch_pass<16, STATS, SWAP>(p, grid, st);
+        case 32: return launch_pass<32, STATS, SWAP>(p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+int device_sms() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+}  // namespace
+
+template <int K>
+cudaError_t launch_merge(const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
+                         cudaStream_t st) {
+    merge_partials<K><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(pv, pi, parts, rows, k_out, ov, oi);
+    return cudaGetLastError();
+}
+
+cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
+                      cudaStream_t st) {
+    switch (K) {
+        case 1: return launch_merge<1>(pv, pi, parts, rows, k_out, ov, oi, st);
+        case 2: return launch_merge<2>(pv, pi, parts, rows, k_out, ov, oi, st);
+        case 4: return launch_merge<4>(pv, pi, parts, rows, k_out, ov, oi, st);
+        case 8: return launch_merge<8>(pv, pi, parts, rows, k_out, ov, oi, st);
+        case 16: return launch_merge<16>(pv, pi, parts, rows, k_out, ov, oi, st);
+        case 32: return launch_merge<32>(pv, pi, parts, rows, k_out, ov, oi, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// Scratch layout of one ℓ2² scan call.  With base == nullptr only sizes it.
+struct L2sqLayout {
+    float *xpad = nullptr, *ypad = nullptr, *xlo = nullptr, *ylo = nullptr;
+    double *pv1 = nullptr, *pv2 = nullptr, *cta = nullptr;
+    int *pi1 = nullptr, *pi2 = nullptr, *status = nullptr;
+    ScanPlan p1{}, p2{};
+    size_t bytes = 0;
+    bool ok = true;
+};
+
+L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups) {
+    L2sqLayout L;
+    const int sms = device_sms();
+    const int K = k > 0 ? bucket_of(k) : 0;
+    const int dp = (int)((d + 3) / 4 * 4);
+    const bool pad = dp != d;
+    Arena ar{static_cast<char*>(base), size, 0};
+    auto need = [&](bool cond, auto*& ptr, size_t count) {
+        using T = std::remove_pointer_t<std::remove_reference_t<decltype(ptr)>>;
+        if (!cond) return;
+        ptr = ar.take<T>(count);
+        if (base && !ptr) L.ok = false;
+    };
+    need(pad, L.xpad, (size_t)q * dp);
+    need(pad, L.ypad, (size_t)n * dp);
+    need(precision == 3, L.xlo, (size_t)q * dp);
+    need(precision == 3, L.ylo, (size_t)n * dp);
+    // features wider than ~1k keep more column groups so the row-block slabs in flight fit in L2
+    const int wide = (int)(d / 1024) + 1;
+    L.p1 = scan_plan(q, n, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
+    L.p2 = scan_plan(n, q, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
+    need(K > 0, L.pv1, (size_t)L.p1.groups * q * K);
+    need(K > 0, L.pi1, (size_t)L.p1.groups * q * K);
+    need(K > 0, L.pv2, (size_t)L.p2.groups * n * K);
+    need(K > 0, L.pi2, (size_t)L.p2.groups * n * K);
+    need(true, L.cta, (size_t)(L.p1.grid > L.p2.grid ? L.p1.grid : L.p2.grid) * 5);
+    need(true, L.status, 1);
+    L.bytes = ar.used + 256;
+    return L;
+}
+
+size_t l2sq_bytes(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups) {
+    return l2sq_layout(nullptr, 0, q, n, d, k, precision, min_groups).bytes;
+}
+
+int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* nx, const double* ny,
+              const double* qb, const double* dbb, int k, double dot_scale, int want_stats, int precision,
+              int min_groups, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws, size_t ws_bytes,
+              int* status_out, cudaStream_t st, std::string& err) {
+    L2sqLayout L = l2sq_layout(ws, ws_bytes, q, n, d, k, precision, min_groups);
+    if (!L.ok) { err = "workspace too small for the l2sq scan"; return 3; }
+    const int K = k > 0 ? bucket_of(k) : 0;
+    const int dp = (int)((d + 3) / 4 * 4);
+    cudaError_t e = cudaMemsetAsync(L.status, 0, sizeof(int), st);
+    if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
+    const float* xs = x;
+    const float* ys = y;
+    const int prep_blocks = device_sms() * 8;
+    if (L.xpad || L.xlo) {
+        l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(x, q, (int)d, dp, L.xpad, L.xlo);
+        l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(y, n, (int)d, dp, L.ypad, L.ylo);
+        if (L.xpad) { xs = L.xpad; ys = L.ypad; }
+    }
+    l2sq::Params p;
+    std::memset(&p, 0, sizeof(p));
+    bool maps = make_map(&p.qmap[0], xs, q, dp, l2sq::BM) && make_map(&p.dmap[0], ys, n, dp, l2sq::BN);
+    if (precision == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, l2sq::BN);
+    else { p.qmap[1] = p.qmap[0]; p.dmap[1] = p.dmap[0]; }
+    if (!maps) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
+    // product terms in a fixed order: x*y, x*lo(y), lo(x)*y
+    const int qs[3] = {0, 0, 1}, ds[3] = {0, 1, 0};
+    p.nseg = precision == 3 ? 3 : 1;
+    p.kslabs = (dp + l2sq::BK - 1) / l2sq::BK;
+    p.scale = (float)dot_scale;
+    p.status = L.status;
+    p.cta_stats = L.cta;
+    // pass 1: x rows are the queries (row top-k + certificate)
+    for (int i = 0; i < 3; ++i) { p.qsel[i] = qs[i]; p.dsel[i] = ds[i]; }
+    p.q = (int)q; p.n = (int)n;
+    p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
+    p.q_cost = nx; p.d_cost = ny; p.q_bias = qb; p.d_bias = dbb;
+    p.part_v = L.pv1; p.part_i = L.pi1;
+    e = want_stats ? launch_k<true, false>(K, p, L.p1.grid, st) : launch_k<false, false>(K, p, L.p1.grid, st);
+    if (e != cudaSuccess) { err = std::string("l2sq pass 1: ") + cudaGetErrorString(e); return 6; }
+    if (want_stats) {
+        finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5);
+    }
+    if (K > 0) {
+        e = merge_any(K, L.pv1, L.pi1, L.p1.groups, q, k, rv, ri, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        // pass 2: y rows are the queries, same products in the same order
+        l2sq::Params p2 = p;
+        std::swap(p2.qmap[0], p2.dmap[0]);
+        std::swap(p2.qmap[1], p2.dmap[1]);
+        // keep the product order x*y, x*lo(y), lo(x)*y with the operands exchanged
+        for (int i = 0; i < 3; ++i) { p2.qsel[i] = ds[i]; p2.dsel[i] = qs[i]; }
+        p2.q = (int)n; p2.n = (int)q;
+        p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
+        p2.q_cost = ny; p2.d_cost = nx; p2.q_bias = dbb; p2.d_bias = qb;
+        p2.part_v = L.pv2; p2.part_i = L.pi2;
+        e = launch_k<false, true>(K, p2, L.p2.grid, st);
+        if (e != cudaSuccess) { err = std::string("l2sq pass 2: ") + cudaGetErrorString(e); return 6; }
+        e = merge_any(K, L.pv2, L.pi2, L.p2.groups, n, k, cv, ci, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+    }
+    if (status_out) cudaMemcpyAsync(status_out, L.status, sizeof(int), cudaMemcpyDeviceToHost, st);
+    return 0;
+}
+
+}  // namespace hb

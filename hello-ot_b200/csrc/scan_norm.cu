@@ -1,0 +1,298 @@
+// ℓ1 / ℓ∞ / ℓ2 full-space pricing scan on the CUDA cores (sm_100a).
+//
+// Replaces the reference's direct-norm tiles + selection
+// (src/hello_ot/_native/generic_scan/cost.cu:10-85 direct_norm_kernel,
+// pricing_small.cu:70-160 scan_kernel, matrix_selection.cuh) with one fused
+// persistent kernel per pass: no cost tile reaches HBM.
+//
+// Distances are accumulated in fp32 over the feature index in increasing
+// order (ℓ2 with an fma per term, then sqrtf), so every distance equals the
+// sequential fp32 model of the oracle bit for bit.  Score and certificate in
+// fp64 as in the reference: score = (g_j - c_ij) + f_i (pricing_small.cu:112).
+//
+// Tile 128 rows x 128 columns, 256 threads: each thread accumulates an 8x8
+// register block from k-major shared-memory slabs; the distance tile is then
+// handed through shared memory to a row-per-thread epilogue (two threads per
+// row, one per half of the columns) that keeps the row top-k in registers.
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+#include "scan_common.cuh"
+
+namespace hb {
+namespace norm {
+
+constexpr int BM = 128, BN = 128, BKS = 8, THREADS = 256;
+
+struct Smem {
+    float xs[2][BKS][BM];
+    float ys[2][BKS][BN];
+    float dist[BM][BN + 1];
+    double dbias[BN];
+    double red[8 * 5];
+};
+
+struct Params {
+    const float* x;  // query features (q x d)
+    const float* y;  // database features (n x d)
+    int q, n, d;
+    int groups, tpg, ct, units;
+    const double* q_bias;
+    const double* d_bias;
+    double* part_v;  // [groups*2][q][K]
+    int* part_i;
+    double* cta_stats;
+};
+
+template <int KIND>
+__device__ __forceinline__ float accumulate(float acc, float a, float b) {
+    const float z = a - b;
+    if (KIND == 0) return acc + fabsf(z);
+    if (KIND == 1) return fmaxf(acc, fabsf(z));
+    return fmaf(z, z, acc);
+}
+
+__device__ __forceinline__ void load_slab(const float* __restrict__ src, int rows_total, int d, int r0, int k0,
+                                          float (*dst)[BM]) {
+    // 128 rows x 8 features, stored k-major; thread t covers row t/2, features (t%2)*4..+3
+    const int t = threadIdx.x;
+    const int r = t >> 1, kb = (t & 1) * 4;
+    const int gr = r0 + r;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int k = k0 + kb + j;
+        dst[kb + j][r] = (gr < rows_total && k < d) ? src[(int64_t)gr * d + k] : 0.0f;
+    }
+}
+
+template <int KIND, int K, bool STATS, bool SWAP>
+__global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+    constexpr int KK = K > 0 ? K : 1;
+    const int t = threadIdx.x;
+    const int ty = t >> 4, tx = t & 15;           // distance block: rows ty+16i, cols tx+16j
+    const int er = t & (BM - 1), half = t >> 7;   // epilogue: row er, columns half*64..+63
+    double acc[5] = {0, 0, 0, 0, 0};
+    TopK<KK> top;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int rb = u / p.groups, g = u % p.groups;
+        const int ct1 = min(p.ct, (g + 1) * p.tpg);
+        const int row = rb * BM + er;
+        const bool rvalid = row < p.q;
+        const double rbias = rvalid ? p.q_bias[row] : 0.0;
+        top.reset();
+        for (int ct = g * p.tpg; ct < ct1; ++ct) {
+            const int c0 = ct * BN;
+            float dist[8][8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dist[i][j] = 0.0f;
+            const int nslab = (p.d + BKS - 1) / BKS;
+            load_slab(p.x, p.q, p.d, rb * BM, 0, s.xs[0]);
+            load_slab(p.y, p.n, p.d, c0, 0, s.ys[0]);
+            __syncthreads();
+            for (int sl = 0; sl < nslab; ++sl) {
+                const int cur = sl & 1;
+                if (sl + 1 < nslab) {
+                    load_slab(p.x, p.q, p.d, rb * BM, (sl + 1) * BKS, s.xs[cur ^ 1]);
+                    load_slab(p.y, p.n, p.d, c0, (sl + 1) * BKS, s.ys[cur ^ 1]);
+                }
+                const int kn = min(BKS, p.d - sl * BKS);
+                for (int k = 0; k < kn; ++k) {
+                    float xv[8], yv[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) xv[i] = s.xs[cur][k][ty + 16 * i];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) yv[j] = s.ys[cur][k][tx + 16 * j];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) dist[i][j] = accumulate<KIND>(dist[i][j], xv[i], yv[j]);
+                }
+                __syncthreads();
+            }
+            // hand the tile to the row-per-thread epilogue
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    s.dist[ty + 16 * i][tx + 16 * j] = KIND == 2 ? sqrtf(dist[i][j]) : dist[i][j];
+            const int ncols = min(BN, p.n - c0);
+            if (t < BN) s.dbias[t] = t < ncols ? p.d_bias[c0 + t] : 0.0;
+            __syncthreads();
+            if (rvalid) {
+                const int cb0 = half * 64;
+                double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
+                for (int c4 = cb0; c4 < cb0 + 64; c4 += 4) {
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const int c = c4 + jj;
+                        if (c < ncols) {
+                            const double cost = (double)s.dist[er][c];
+                            const double cbias = s.dbias[c];
+                            const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
+                            if (STATS) {
+                                den4[jj] += cost * cost;
+                                acc[3] = fmax(acc[3], fabs(cost));
+                                if (sc > 0.0) { num4[jj] += sc * sc; acc[2] = fmax(acc[2], sc); acc[4] += 1.0; }
+                            }
+                            if (K > 0) top.offer(sc, c0 + c);
+                        }
+                    }
+                }
+                if (STATS) {
+                    acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
+                    acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
+                }
+            }
+            __syncthreads();
+        }
+        if (K > 0 && rvalid) {
+            const int part = g * 2 + half;
+            double* pv = p.part_v + ((int64_t)part * p.q + row) * KK;
+            int* pi = p.part_i + ((int64_t)part * p.q + row) * KK;
+#pragma unroll
+            for (int j = 0; j < KK; ++j) { pv[j] = top.v[j]; pi[j] = top.i[j]; }
+        }
+    }
+    if (STATS) {
+        const int lane = t & 31, w = t >> 5;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const double o0 = __shfl_down_sync(0xffffffffu, acc[0], off);
+            const double o1 = __shfl_down_sync(0xffffffffu, acc[1], off);
+            const double o2 = __shfl_down_sync(0xffffffffu, acc[2], off);
+            const double o3 = __shfl_down_sync(0xffffffffu, acc[3], off);
+            const double o4 = __shfl_down_sync(0xffffffffu, acc[4], off);
+            acc[0] += o0; acc[1] += o1; acc[2] = fmax(acc[2], o2); acc[3] = fmax(acc[3], o3); acc[4] += o4;
+        }
+        if (lane == 0)
+            for (int j = 0; j < 5; ++j) s.red[w * 5 + j] = acc[j];
+        __syncthreads();
+        if (t == 0) {
+            double a[5] = {0, 0, 0, 0, 0};
+            for (int ww = 0; ww < THREADS / 32; ++ww) {
+                a[0] += s.red[ww * 5 + 0]; a[1] += s.red[ww * 5 + 1];
+                a[2] = fmax(a[2], s.red[ww * 5 + 2]); a[3] = fmax(a[3], s.red[ww * 5 + 3]);
+                a[4] += s.red[ww * 5 + 4];
+            }
+            for (int j = 0; j < 5; ++j) p.cta_stats[blockIdx.x * 5 + j] = a[j];
+        }
+    }
+}
+
+}  // namespace norm
+
+namespace {
+
+template <int KIND, int K, bool STATS, bool SWAP>
+cudaError_t norm_launch(const norm::Params& p, int grid, cudaStream_t st) {
+    auto fn = norm::scan_kernel<KIND, K, STATS, SWAP>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(norm::Smem));
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    fn<<<grid, norm::THREADS, sizeof(norm::Smem), st>>>(p);
+    return cudaGetLastError();
+}
+
+template <int KIND, bool STATS, bool SWAP>
+cudaError_t norm_k(int K, const norm::Params& p, int grid, cudaStream_t st) {
+    switch (K) {
+        case 0: return norm_launch<KIND, 0, STATS, SWAP>(p, grid, st);
+        case 1: return norm_launch<KIND, 1, STATS, SWAP>(p, grid, st);
+        case 2: return norm_launch<KIND, 2, STATS, SWAP>(p, grid, st);
+        case 4: return norm_launch<KIND, 4, STATS, SWAP>(p, grid, st);
+        case 8: return norm_launch<KIND, 8, STATS, SWAP>(p, grid, st);
+        case 16: return norm_launch<KIND, 16, STATS, SWAP>(p, grid, st);
+        case 32: return norm_launch<KIND, 32, STATS, SWAP>(p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <bool STATS, bool SWAP>
+cudaError_t norm_kind(int kind, int K, const norm::Params& p, int grid, cudaStream_t st) {
+    switch (kind) {
+        case 0: return norm_k<0, STATS, SWAP>(K, p, grid, st);
+        case 1: return norm_k<1, STATS, SWAP>(K, p, grid, st);
+        case 2: return norm_k<2, STATS, SWAP>(K, p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+}  // namespace
+
+struct NormLayout {
+    double *pv1 = nullptr, *pv2 = nullptr, *cta = nullptr;
+    int *pi1 = nullptr, *pi2 = nullptr;
+    ScanPlan p1{}, p2{};
+    size_t bytes = 0;
+    bool ok = true;
+};
+
+NormLayout norm_layout(void* base, size_t size, int64_t q, int64_t n, int k) {
+    NormLayout L;
+    const int sms = sm_count();
+    const int K = k > 0 ? bucket_of(k) : 0;
+    Arena ar{static_cast<char*>(base), size, 0};
+    L.p1 = scan_plan(q, n, norm::BM, norm::BN, 2, sms, 1);
+    L.p2 = scan_plan(n, q, norm::BM, norm::BN, 2, sms, 1);
+    if (K > 0) {
+        L.pv1 = ar.take<double>((size_t)L.p1.groups * 2 * q * K);
+        L.pi1 = ar.take<int>((size_t)L.p1.groups * 2 * q * K);
+        L.pv2 = ar.take<double>((size_t)L.p2.groups * 2 * n * K);
+        L.pi2 = ar.take<int>((size_t)L.p2.groups * 2 * n * K);
+        if (base && (!L.pv1 || !L.pi1 || !L.pv2 || !L.pi2)) L.ok = false;
+    }
+    L.cta = ar.take<double>((size_t)(L.p1.grid > L.p2.grid ? L.p1.grid : L.p2.grid) * 5);
+    if (base && !L.cta) L.ok = false;
+    L.bytes = ar.used + 256;
+    return L;
+}
+
+size_t norm_bytes(int64_t q, int64_t n, int k) { return norm_layout(nullptr, 0, q, n, k).bytes; }
+
+int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
+              int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
+              size_t ws_bytes, cudaStream_t st, std::string& err) {
+    NormLayout L = norm_layout(ws, ws_bytes, q, n, k);
+    if (!L.ok) { err = "workspace too small for the norm scan"; return 3; }
+    const int K = k > 0 ? bucket_of(k) : 0;
+    norm::Params p{};
+    p.x = x; p.y = y; p.q = (int)q; p.n = (int)n; p.d = (int)d;
+    p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
+    p.q_bias = f; p.d_bias = g;
+    p.part_v = L.pv1; p.part_i = L.pi1; p.cta_stats = L.cta;
+    cudaError_t e = want_stats ? norm_kind<true, false>(kind, K, p, L.p1.grid, st)
+                               : norm_kind<false, false>(kind, K, p, L.p1.grid, st);
+    if (e != cudaSuccess) { err = std::string("norm pass 1: ") + cudaGetErrorString(e); return 6; }
+    if (want_stats) finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5);
+    if (K > 0) {
+        e = merge_any(K, L.pv1, L.pi1, L.p1.groups * 2, q, k, rv, ri, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        norm::Params p2 = p;
+        p2.x = y; p2.y = x; p2.q = (int)n; p2.n = (int)q;
+        p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
+        p2.q_bias = g; p2.d_bias = f;
+        p2.part_v = L.pv2; p2.part_i = L.pi2;
+        e = norm_kind<false, true>(kind, K, p2, L.p2.grid, st);
+        if (e != cudaSuccess) { err = std::string("norm pass 2: ") + cudaGetErrorString(e); return 6; }
+        e = merge_any(K, L.pv2, L.pi2, L.p2.groups * 2, n, k, cv, ci, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+    }
+    return 0;
+}
+
+}  // namespace hb

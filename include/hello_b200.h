@@ -1,0 +1,151 @@
+/*
+ * hello_b200.h - C ABI of the B200-native HELLO hot path (libhello_b200.so).
+ *
+ * Plain pointers and sizes only.  Every array argument is a CUDA device
+ * pointer on the current device unless stated otherwise; `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  Functions return 0 on success
+ * and a nonzero HB_* code on failure; hb_last_error() then holds a message
+ * (per calling thread).  No entry point allocates device memory: callers
+ * provide scratch through `workspace`, sized by the matching *_workspace()
+ * query for the same shapes on the same device.  Calls that report device
+ * status (scans, pair costs, the PDHG solve) synchronise `stream` before
+ * returning.
+ *
+ * Paths in the citations are inside the reference project (WenzhouXia/hello-ot).
+ */
+#ifndef HELLO_B200_H
+#define HELLO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HB_ABI_VERSION 1
+
+enum {
+    HB_OK = 0,
+    HB_BAD_ARGUMENT = 1,   /* shapes, k, scale, cost type, null pointers */
+    HB_BAD_INPUT = 2,      /* index data out of range (pair costs, PDHG support) */
+    HB_WORKSPACE = 3,      /* workspace smaller than the *_workspace() size */
+    HB_CUDA = 4,           /* a CUDA runtime call failed */
+    HB_TENSOR_MAP = 5,     /* TMA descriptor could not be built */
+    HB_LAUNCH = 6,         /* a kernel launch failed */
+    HB_DEVICE_TIMEOUT = 7  /* a bounded device-side wait gave up */
+};
+
+int hb_abi_version(void);
+const char* hb_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * ℓ2² (bilinear) full-space pricing scan, bidirectional top-k + certificate.
+ *
+ * Replaces ScanExtension.fused_bidir_topk_stats_raw
+ * (src/hello_ot/kernels/generic_scan.py:577-597) and the kernels behind it,
+ * raw_scan_tiled (src/hello_ot/_native/generic_scan/pricing_small.cu:298-304)
+ * and pricing.scan (pricing.cu:203-212); also ScanExtension.raw_lowrank_stats_only
+ * (generic_scan.py:502-510) when k == 0.
+ *
+ * x: q x d, y: n x d, fp32 row-major.  x_cost = a (|x|^2), y_cost = b,
+ * x_bias = f - a, y_bias = g - b (fp64).  For every pair
+ *   dot = fp32(dot_scale * <x_i, y_j>), cost = (a_i + b_j) - dot,
+ *   score = (dot + x_bias_i) + y_bias_j                      (fp64)
+ * row_vals/row_idx (q x k): best k (score, j) of each x row; col_vals/col_idx
+ * (n x k): best k (score, i) of each y row; descending, lower index on ties,
+ * missing slots (-inf, -1).  k in 0..32 (0: certificate only, outputs unused).
+ * stats5 (device, 5 doubles): [sum max(s,0)^2, sum cost^2, max s+, max |cost|,
+ * count s>0] over all q*n pairs; written when compute_stats != 0.
+ * precision: 1 = one TF32 tensor-core product, 3 = 3xTF32 split (fp32-class).
+ * min_groups: column groups per row block (0 = automatic).
+ * ------------------------------------------------------------------------- */
+size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
+int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_cost,
+                 const double* y_cost, const double* x_bias, const double* y_bias, int k, double dot_scale,
+                 int compute_stats, int precision, int min_groups, double* row_vals, int32_t* row_idx,
+                 double* col_vals, int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* ---------------------------------------------------------------------------
+ * ℓ1 / ℓ∞ / ℓ2 full-space pricing scan (CUDA cores), bidirectional top-k +
+ * certificate.  cost_type: 0 l1, 1 linf, 2 l2.
+ *
+ * Replaces ScanExtension.fused_gcost_bidir_certificate and
+ * ScanExtension.fused_gcost_certificate (src/hello_ot/kernels/generic_scan.py:533-558)
+ * with their unperturbed generic_scan.bidirectional / certificate_only paths
+ * (generic_scan.py:328-465; kernels cost.cu:10-85, pricing_small.cu:70-160).
+ *
+ * score = (g_j - c_ij) + f_i with c_ij the fp32 distance (features summed in
+ * index order, ℓ2 via fma then sqrtf).  Outputs and k as for hb_l2sq_scan.
+ * ------------------------------------------------------------------------- */
+size_t hb_norm_scan_workspace(int64_t q, int64_t n, int k);
+int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
+                 int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
+                 int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Active-support pair costs (SDDMM), fp64 output in input order.
+ * cost_type 3 (bilinear): out_e = (a_r + b_c) - dot_scale <x_r, y_c>, replacing
+ *   _cost_pairs_lowrank_batched (src/hello_ot/costs/pairs.py:221-440).
+ * cost_type 0/1/2 (ℓ1/ℓ∞/ℓ2): replacing fused_gcost_pairs
+ *   (src/hello_ot/_native/norm_cost_scan/norm_cost_scan_kernel.cu:249-275)
+ *   without perturbation; a and b are ignored (may be NULL).
+ * rows/cols: int64 indices into x (nx rows) and y (ny rows).  An index out of
+ * range gives HB_BAD_INPUT (its output is NaN).
+ * ------------------------------------------------------------------------- */
+size_t hb_pair_costs_workspace(void);
+int hb_pair_costs(int cost_type, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d,
+                  const double* a, const double* b, double dot_scale, const int64_t* rows, const int64_t* cols,
+                  int64_t count, double* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Restricted-OT Halpern-PDHG (balanced transport LP on the active support).
+ *
+ * Replaces RestrictedOTPDLP.solve_restricted / _solve_once
+ * (src/hello_ot/_internal/lp/restricted_ot_pdlp.py:39-100,
+ * cpp_restricted_ot.py:40-72 -> src/hello_ot/_native/cpp/solver.cpp:39-381)
+ * and, behind backend="native", the cuPDLPx loop (cupdlpx/solver.cu:581-700).
+ * One call is one _solve_once: the NUMERICAL_DIVERGENCE retry with scalar
+ * rescaling is the caller's (restricted_ot_pdlp.py:76-100).
+ *
+ * rows/cols/costs: E edges (int64, int64, fp64); masses: n source masses
+ * followed by m target masses; x0 (E) and y0 (n+m) warm starts or NULL.
+ * x_out (E), y_out (n+m): unscaled primal and dual.
+ * trace (host memory, may be NULL): one hb_pdlp_trace_row per evaluation.
+ * ------------------------------------------------------------------------- */
+typedef struct hb_pdlp_controls {
+    int32_t evaluation_frequency;  /* iterations between evaluations (200 in the reference) */
+    int32_t scalar_rescaling;      /* 1: bound/objective scalar rescaling (the retry mode) */
+    int64_t iteration_limit;
+    double time_limit_seconds;
+    double tol_objective, tol_primal, tol_dual;
+    double initial_primal_weight;  /* > 0 overrides the initial norm-ratio weight */
+} hb_pdlp_controls;
+
+enum { HB_PDLP_OPTIMAL = 1, HB_PDLP_ITERATION_LIMIT = 2, HB_PDLP_NUMERICAL_DIVERGENCE = 3, HB_PDLP_TIME_LIMIT = 4 };
+
+typedef struct hb_pdlp_info {
+    int64_t iterations, restarts;
+    int32_t termination, pad;
+    double primal_objective, dual_objective;
+    double abs_primal_residual, rel_primal_residual, abs_dual_residual, rel_dual_residual, rel_gap;
+    double primal_weight, cost_norm, mass_norm;
+    double setup_seconds, iteration_seconds;
+} hb_pdlp_info;
+
+typedef struct hb_pdlp_trace_row {
+    double iteration, primal_objective, dual_objective, rel_primal, rel_dual, rel_gap, primal_weight;
+} hb_pdlp_trace_row;
+
+size_t hb_restricted_ot_workspace(int64_t n, int64_t m, int64_t e);
+int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const double* costs, int64_t e,
+                           const double* masses, int64_t n, int64_t m, const double* x0, const double* y0,
+                           const hb_pdlp_controls* controls, double* x_out, double* y_out, hb_pdlp_info* info,
+                           hb_pdlp_trace_row* trace, int32_t trace_capacity, int32_t* trace_length,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HELLO_B200_H */

@@ -63,7 +63,9 @@ typedef struct {
  *        h/_native/generic_scan/matrix_selection.cuh:20-26 (RAW branch) with
  *        the SGEMM alpha applied in fp32, pricing_small.cu:241-256.
  * norms: score = (g_j - c_ij) + f_i, pricing_small.cu:112;
- *        c = sum|x-y| / max|x-y| / sqrt(sum (x-y)^2), pricing_small.cu:62-67. */
+ *        c = sum|x-y| / max|x-y| / sqrt(sum (x-y)^2), pricing_small.cu:62-67;
+ *        the fp32 model (exact == 0) accumulates in feature order, ℓ2 with one
+ *        fma per term. */
 static inline void orc_pair(const orc_scan_ctx* c, int64_t i, int64_t j, double* score, double* cost) {
     const float* xi = c->x + i * c->d;
     const float* yj = c->y + j * c->d;
@@ -98,7 +100,7 @@ static inline void orc_pair(const orc_scan_ctx* c, int64_t i, int64_t j, double*
             float z = xi[k] - yj[k];
             if (c->kind == 0) acc = acc + fabsf(z);
             else if (c->kind == 1) acc = fmaxf(acc, fabsf(z));
-            else acc = acc + z * z;
+            else acc = fmaf(z, z, acc);
         }
         dist = c->kind == 2 ? (double)sqrtf(acc) : (double)acc;
     }

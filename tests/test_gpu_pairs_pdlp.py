@@ -1,0 +1,124 @@
+"""Pair-cost (SDDMM) and restricted-OT PDHG parity on the GPU through the C ABI."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.mark.parametrize("d", [1, 3, 4, 16, 70, 257, 1024])
+@pytest.mark.parametrize("kind", ["l1", "linf", "l2", "lowrank"])
+def test_pair_costs_match_oracle(hb, cuda, oracle, d, kind):
+    rng = np.random.default_rng(d)
+    x = rng.normal(size=(300, d)).astype(np.float32)
+    y = rng.normal(size=(200, d)).astype(np.float32)
+    e = 5000
+    rows, cols = rng.integers(0, 300, e), rng.integers(0, 200, e)
+    a = (x.astype(np.float64) ** 2).sum(1)
+    b = (y.astype(np.float64) ** 2).sum(1)
+    if kind == "lowrank":
+        got = hb.cost_pairs_lowrank(dict(F=x, G=y, a=a, b=b, dot_scale=2.0), rows, cols)
+        exp = oracle.pair_costs("raw", x, y, rows, cols, a, b, dot_scale=2.0)
+        np.testing.assert_allclose(got, exp, rtol=0, atol=1e-12 * (np.abs(a[rows]) + np.abs(b[cols]) + 1).max())
+    else:
+        got = hb.pair_costs_metric(source_points=x, target_points=y, rows=rows, cols=cols, cost_type=kind)
+        exp = oracle.pair_costs(kind, x, y, rows, cols)
+        if kind == "linf":
+            assert np.array_equal(got, exp)
+        else:
+            np.testing.assert_allclose(got, exp, rtol=1e-13, atol=0)
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pairs_*.npz")))
+def test_pair_costs_golden(hb, cuda, path):
+    with np.load(GOLDEN / path) as z:
+        z = {k: z[k] for k in z.files}
+    for kind in ("l1", "l2", "linf"):
+        got = hb.pair_costs_metric(source_points=z["x"], target_points=z["y"], rows=z["rows"], cols=z["cols"],
+                                   cost_type=kind)
+        np.testing.assert_allclose(got, z[kind], rtol=1e-13, atol=0)
+    got = hb.cost_pairs_lowrank(dict(F=z["x"], G=z["y"], a=z["a"], b=z["b"], dot_scale=2.0), z["rows"], z["cols"])
+    # the reference evaluates this in fp32
+    np.testing.assert_allclose(got, z["lowrank"], rtol=1e-5, atol=1e-4)
+
+
+def test_pair_costs_edges_and_errors(hb, cuda):
+    x = torch.randn(10, 8, device=cuda)
+    y = torch.randn(12, 8, device=cuda)
+    empty = torch.empty(0, dtype=torch.int64, device=cuda)
+    assert hb.pair_costs(0, x, y, empty, empty).numel() == 0
+    with pytest.raises(ValueError, match="index out of range"):
+        hb.pair_costs(0, x, y, torch.tensor([0, 10], device=cuda), torch.tensor([1, 2], device=cuda))
+    with pytest.raises(ValueError):
+        hb.pair_costs(0, x, y, torch.tensor([0, 1], device=cuda), torch.tensor([1, 12], device=cuda))
+
+
+def _random_support(ns, nt, extra, seed):
+    rng = np.random.default_rng(seed)
+    rows = np.concatenate([np.arange(ns), rng.integers(0, ns, extra), rng.integers(0, ns, nt)])
+    cols = np.concatenate([rng.integers(0, nt, ns), rng.integers(0, nt, extra), np.arange(nt)])
+    key = np.unique(rows * nt + cols)
+    rows, cols = key // nt, key % nt
+    perm = rng.permutation(rows.size)
+    wa, wb = rng.uniform(0.5, 1.5, ns), rng.uniform(0.5, 1.5, nt)
+    return rows[perm], cols[perm], rng.random(rows.size) * 3, wa / wa.sum(), wb / wb.sum()
+
+
+@pytest.mark.parametrize("shape", [(30, 40, 180), (300, 400, 4000), (1000, 700, 20000)])
+def test_pdlp_block_is_bit_exact(hb, cuda, oracle, shape):
+    """One block of iterations with the same step sizes reproduces the reference
+    arithmetic exactly (no restart inside the block)."""
+    rows, cols, c, a, b = _random_support(*shape, seed=shape[0])
+    F = 60
+    ref = oracle.pdlp(rows, cols, c, a, b, frequency=F, iteration_limit=F, tolerance=0.0)
+    solver = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=F, iteration_limit=F,
+                                       initial_primal_weight=ref["primal_weight"])
+    got = solver.solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=0.0)
+    assert got.iterations == ref["iterations"] == F
+    assert np.array_equal(got.x.cpu().numpy(), ref["x"])
+    assert np.array_equal(got.y.cpu().numpy(), ref["y"])
+
+
+@pytest.mark.parametrize("shape", [(30, 40, 180), (300, 400, 4000), (1000, 700, 20000)])
+def test_pdlp_converges_like_oracle(hb, cuda, oracle, shape):
+    rows, cols, c, a, b = _random_support(*shape, seed=shape[1])
+    ref = oracle.pdlp(rows, cols, c, a, b, frequency=200, tolerance=1e-7)
+    got = hb.NativeRestrictedOTPDLP(device=cuda).solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a,
+                                                                   target_mass=b, tolerance=1e-7)
+    assert ref["termination_reason"] == got.termination_reason == "OPTIMAL"
+    assert got.obj_val == pytest.approx(ref["obj_val"], rel=1e-6)
+    assert got.primal_feas < 1e-7 and got.dual_feas < 1e-7 and got.gap < 1e-7
+    assert abs(got.iterations - ref["iterations"]) <= 2 * 200
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pdlp_*.npz")))
+def test_pdlp_golden(hb, cuda, path):
+    with np.load(GOLDEN / path) as z:
+        z = {k: z[k] for k in z.files}
+    x0 = z["x0"] if z["x0"].size else None
+    y0 = z["y0"] if z["y0"].size else None
+    got = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=20, iteration_limit=200000).solve_restricted(
+        rows=z["rows"], cols=z["cols"], costs=z["costs"], source_mass=z["source_mass"], target_mass=z["target_mass"],
+        warm_start_primal=x0, warm_start_dual=y0, tolerance=1e-7)
+    meta = z["cpp_meta"]
+    assert got.termination_reason == "OPTIMAL"
+    assert got.obj_val == pytest.approx(meta[2], rel=1e-6, abs=1e-9)
+    np.testing.assert_allclose(got.x.cpu().numpy(), z["cpp_x"], atol=1e-5)
+
+
+def test_pdlp_input_errors(hb, cuda):
+    rows, cols = np.array([0, 0, 1, 1]), np.array([0, 1, 0, 1])
+    costs = np.array([0.0, 2.0, 1.0, 0.0])
+    s = hb.NativeRestrictedOTPDLP(device=cuda)
+    with pytest.raises(ValueError, match="equal source and target total mass"):
+        s.solve_restricted(rows=rows, cols=cols, costs=costs, source_mass=[0.4, 0.6], target_mass=[0.4, 0.5])
+    with pytest.raises(ValueError, match="out of bounds"):
+        s.solve_restricted(rows=[0, 0, 1, 2], cols=cols, costs=costs, source_mass=[0.4, 0.6], target_mass=[0.5, 0.5])
+    with pytest.raises(ValueError, match="must not be empty"):
+        s.solve_restricted(rows=[], cols=[], costs=[], source_mass=[0.4, 0.6], target_mass=[0.5, 0.5])
+    r = s.solve_restricted(rows=rows, cols=cols, costs=costs, source_mass=[0.4, 0.6], target_mass=[0.5, 0.5],
+                           tolerance=1e-7)
+    assert r.success and r.obj_val == pytest.approx(0.1, abs=2e-6)

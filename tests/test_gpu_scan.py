@@ -1,0 +1,170 @@
+"""Pricing-scan parity on the GPU: libhello_b200 (through the C ABI) vs the oracle.
+
+ℓ2² (tensor cores): every reported value lies within the stated error bound of
+its exact fp64 score, index sets equal the exact top-k wherever the boundary
+gap exceeds twice the bound, and the certificate agrees within the bound.
+ℓ1/ℓ∞/ℓ2 (CUDA cores): distances are accumulated in the oracle's fp32 order,
+so top-k values and indices must be identical bit for bit.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from parity import check_stats, check_topk, flatten
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+U32 = 2.0 ** -24
+
+# (q, n, d, k): tiny, ragged tiles, d % 4 != 0, k > n, wide features, big k
+L2SQ_CASES = [(37, 53, 8, 3), (200, 150, 16, 2), (129, 257, 5, 1), (5, 3, 4, 8), (300, 520, 64, 8),
+              (1000, 700, 130, 32), (2048, 1500, 256, 4), (4100, 300, 33, 16), (640, 900, 2048, 8)]
+
+
+def _cloud(q, n, d, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.normal(size=(q, d)).astype(np.float32)
+    y = (x[rng.integers(0, q, n)] + 0.5 * rng.normal(size=(n, d))).astype(np.float32)
+    a = (x.astype(np.float64) ** 2).sum(1)
+    b = (y.astype(np.float64) ** 2).sum(1)
+    scale = float(np.median(a)) + 1.0
+    f = 0.5 * a + rng.normal(size=q) * 0.3 * scale
+    g = 0.5 * b + rng.normal(size=n) * 0.3 * scale
+    return x, y, a, b, f, g
+
+
+def _bound(x, y, r, c, scale, biases, precision):
+    """Per-pair error bound of the tensor-core score.
+    3xTF32: dropped lo*lo term and truncation of lo parts ~ 2^-20 |x||y| per product,
+    plus fp32 accumulation (d+2)u (any order).  TF32: 2^-9 per product."""
+    x64, y64 = np.asarray(x, np.float64), np.asarray(y, np.float64)
+    d = x64.shape[1]
+    absdot = np.einsum("ij,ij->i", np.abs(x64[r]), np.abs(y64[c]))
+    prod = 2.0 ** -9 if precision == "tf32" else 2.0 ** -19
+    mag = sum(np.abs(v) for v in biases) + scale * absdot
+    return scale * (prod + 2 * (d + 2) * U32) * absdot + 16 * 2.0 ** -53 * mag
+
+
+def _pad(v, i, width):
+    if v.shape[1] < width:
+        v = np.pad(v, ((0, 0), (0, width - v.shape[1])), constant_values=-np.inf)
+        i = np.pad(i, ((0, 0), (0, width - i.shape[1])), constant_values=-1)
+    return v, i
+
+
+def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0, min_clear=0.5):
+    q, n = len(x), len(y)
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    qb, dbb = f - a, g - b
+    rv, ri, cv, ci, stats = hb.l2sq_scan(T(x, torch.float32), T(y, torch.float32), T(a, torch.float64),
+                                         T(b, torch.float64), T(qb, torch.float64), T(dbb, torch.float64), k,
+                                         dot_scale=dot_scale, precision=precision)
+    rv, ri, cv, ci, stats = (t.cpu().numpy() for t in (rv, ri, cv, ci, stats))
+    ev, ei, fv, fi, es = oracle.scan("raw", x, y, qb, dbb, a, b, dot_scale=dot_scale, rk=min(k + 1, n),
+                                     ck=min(k + 1, q))
+    ev, ei = _pad(ev, ei, k + 1)
+    fv, fi = _pad(fv, fi, k + 1)
+
+    def score(r, c):
+        return oracle.pair_scores("raw", x, y, qb, dbb, a, b, r, c, dot_scale=dot_scale)[0]
+
+    def eps(r, c):
+        return _bound(x, y, r, c, dot_scale, (a[r], b[c], qb[r], dbb[c]), precision)
+
+    check_topk(rv, ri, ev, ei, score, eps, min_clear=min_clear, label="rows")
+    check_topk(cv, ci, fv, fi, lambda r, c: score(c, r), lambda r, c: eps(c, r), min_clear=min_clear, label="cols")
+    if q * n <= 4_000_000:
+        rr, cc = np.divmod(np.arange(q * n), n)
+        e, s = eps(rr, cc), score(rr, cc)
+        check_stats(stats, es, float(np.sqrt(np.sum(2 * e * (np.abs(s) + e)))) + e.max(),
+                    int(np.sum(np.abs(s) <= e)), label="stats")
+    return rv, ri, cv, ci, stats
+
+
+@pytest.mark.parametrize("q,n,d,k", L2SQ_CASES)
+@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+def test_l2sq_scan_matches_oracle(hb, cuda, oracle, q, n, d, k, precision):
+    x, y, a, b, f, g = _cloud(q, n, d, seed=q * 7 + n + d)
+    _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision,
+                min_clear=0.5 if precision == "fp32" else 0.05)
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("scan_l2sq_*.npz")))
+def test_l2sq_scan_golden(hb, cuda, oracle, path):
+    with np.load(GOLDEN / path) as z:
+        z = {k: z[k] for k in z.files}
+    k = int(z["k"])
+    rv, ri, cv, ci, _ = _check_l2sq(hb, oracle, cuda, z["x"], z["y"], z["a"], z["b"], z["f"], z["g"], k, "fp32")
+    # candidate pairs: equal to the reference's except pairs inside the error band
+    rows, cols = flatten(rv, ri, cv, ci)
+    ours = set(zip(rows.tolist(), cols.tolist()))
+    ref = set(zip(z["rows"].tolist(), z["cols"].tolist()))
+    assert len(ours ^ ref) <= max(2, len(ref) // 100), f"{len(ours ^ ref)} candidate differences"
+
+
+def test_l2sq_certificate_only_and_scale1(hb, cuda, oracle):
+    x, y, a, b, f, g = _cloud(500, 333, 40, seed=3)
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    out = hb.l2sq_scan(T(x, torch.float32), T(y, torch.float32), T(a, torch.float64), T(b, torch.float64),
+                       T(f - a, torch.float64), T(g - b, torch.float64), 0, dot_scale=1.0)
+    es = oracle.scan("raw", x, y, f - a, g - b, a, b, dot_scale=1.0, rk=0, ck=0)[4]
+    s = out[4].cpu().numpy()
+    np.testing.assert_allclose(s[[0, 1, 2, 3]], es[[0, 1, 2, 3]], rtol=1e-6)
+    assert abs(s[4] - es[4]) <= 1e-4 * 500 * 333
+
+
+def test_l2sq_pass_symmetry(hb, cuda):
+    """Row and column passes see bit-identical scores for the same pair."""
+    x, y, a, b, f, g = _cloud(256, 512, 96, seed=11)
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    rv, ri, cv, ci, _ = hb.l2sq_scan(T(x, torch.float32), T(y, torch.float32), T(a, torch.float64),
+                                     T(b, torch.float64), T(f - a, torch.float64), T(g - b, torch.float64), 1,
+                                     dot_scale=2.0)
+    rv, ri, cv, ci = (t.cpu().numpy() for t in (rv, ri, cv, ci))
+    # the best pair overall is the top of its row and of its column
+    i = int(np.argmax(rv[:, 0]))
+    j = int(ri[i, 0])
+    assert ci[j, 0] == i and cv[j, 0] == rv[i, 0]
+
+
+NORM_CASES = [(41, 29, 3, 2), (64, 80, 20, 8), (129, 257, 1, 1), (300, 200, 128, 4), (1000, 1200, 3, 16),
+              (5, 3, 2, 8), (513, 260, 9, 32)]
+
+
+@pytest.mark.parametrize("kind", ["l1", "linf", "l2"])
+@pytest.mark.parametrize("q,n,d,k", NORM_CASES)
+def test_norm_scan_bit_exact(hb, cuda, oracle, kind, q, n, d, k):
+    rng = np.random.default_rng(q + n * 3 + d)
+    x = rng.normal(size=(q, d)).astype(np.float32)
+    y = (x[rng.integers(0, q, n)] + 0.4 * rng.normal(size=(n, d))).astype(np.float32)
+    f = rng.normal(size=q) * d * 0.5
+    g = rng.normal(size=n) * d * 0.5 + d
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    rv, ri, cv, ci, stats = hb.norm_scan(T(x, torch.float32), T(y, torch.float32), T(f, torch.float64),
+                                         T(g, torch.float64), k, kind)
+    rv, ri, cv, ci, stats = (t.cpu().numpy() for t in (rv, ri, cv, ci, stats))
+    ev, ei, fv, fi, es = oracle.scan(kind, x, y, f, g, rk=min(k, n), ck=min(k, q), exact=False)
+    ev, ei = _pad(ev, ei, k)
+    fv, fi = _pad(fv, fi, k)
+    assert np.array_equal(ri, ei) and np.array_equal(ci, fi)
+    assert np.array_equal(rv, ev) and np.array_equal(cv, fv)
+    assert stats[2] == es[2] and stats[3] == es[3] and stats[4] == es[4]
+    np.testing.assert_allclose(stats[:2], es[:2], rtol=1e-12)
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("scan_l*.npz") if "l2sq" not in p.name))
+def test_norm_scan_golden_certificate(hb, cuda, oracle, path):
+    with np.load(GOLDEN / path) as z:
+        z = {k: z[k] for k in z.files}
+    kind, k = str(z["kind"]), int(z["k"])
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    ext = hb.ScanExtension()
+    out = ext.fused_gcost_bidir_certificate(T(z["x"], torch.float32), T(z["y"], torch.float32),
+                                            T(z["f"], torch.float64), T(z["g"], torch.float64), hb.topk_bucket(k),
+                                            kind)
+    num, den = float(out[4]), float(out[5])
+    feas = np.sqrt(num) / (1 + np.sqrt(den))
+    assert feas == pytest.approx(float(z["dual_feasibility"]), rel=1e-5, abs=1e-9)
+    assert abs(int(out[8]) - int(z["stats"][4])) <= 2

@@ -1,0 +1,88 @@
+"""CPU-only checks: the C ABI's export table, host-side logic and error paths.
+
+No kernel runs here (no GPU in this container); entry points that need CUDA
+must raise instead of falling back to a CPU path.
+"""
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from parity import flatten
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def test_library_exports_every_declared_symbol(hb):
+    header = (REPO / "include" / "hello_b200.h").read_text()
+    declared = set(re.findall(r"^\s*(?:size_t|int|const char\*)\s+(hb_\w+)\s*\(", header, flags=re.M))
+    assert declared, "no declarations parsed"
+    lib = hb.load_library()
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in hello_b200.h but not exported"
+    assert declared == set(hb._lib.EXPORTS)
+    assert lib.hb_abi_version() == 1
+
+
+def test_header_cites_reference_interfaces():
+    header = (REPO / "include" / "hello_b200.h").read_text()
+    for cite in ("generic_scan.py:577-597", "generic_scan.py:533-558", "pairs.py:221-440",
+                 "norm_cost_scan_kernel.cu:249-275", "restricted_ot_pdlp.py:39-100", "solver.cpp:39-381"):
+        assert cite in header
+
+
+def test_no_cpu_fallback(hb, monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    with pytest.raises(hb.HBError, match="requires a CUDA device"):
+        hb.lib()
+    x = torch.zeros(4, 3)
+    with pytest.raises(hb.HBError):
+        hb.l2sq_scan(x, x, torch.zeros(4, dtype=torch.float64), torch.zeros(4, dtype=torch.float64),
+                     torch.zeros(4, dtype=torch.float64), torch.zeros(4, dtype=torch.float64), 2)
+    with pytest.raises(hb.HBError):
+        hb.raw_lowrank_bidir_feasibility_pricing_scan(x.numpy(), x.numpy(), np.zeros(4), np.zeros(4), np.zeros(4),
+                                                      np.zeros(4), topk=2)
+
+
+def test_topk_buckets(hb):
+    assert [hb.topk_bucket(k) for k in (1, 2, 3, 4, 5, 8, 9, 17, 32)] == [1, 2, 4, 4, 8, 8, 16, 32, 32]
+    with pytest.raises(ValueError):
+        hb.topk_bucket(0)
+    with pytest.raises(ValueError, match="topk <= 32"):
+        hb.topk_bucket(33)
+
+
+def test_flatten_candidates_matches_reference_order(hb):
+    rng = np.random.default_rng(0)
+    rv = rng.normal(size=(50, 4))
+    ri = rng.integers(-1, 70, size=(50, 4)).astype(np.int32)
+    cv = rng.normal(size=(70, 4))
+    ci = rng.integers(-1, 50, size=(70, 4)).astype(np.int32)
+    rows, cols = hb.flatten_candidates(*(torch.as_tensor(v) for v in (rv, ri, cv, ci)), theta=0.1)
+    er, ec = flatten(rv, ri, cv, ci, theta=0.1)
+    assert np.array_equal(rows.numpy(), er) and np.array_equal(cols.numpy(), ec)
+    # target-side queries swap the roles
+    rows2, cols2 = hb.flatten_candidates(*(torch.as_tensor(v) for v in (rv, ri, cv, ci)), theta=0.1,
+                                         query_is_source=False)
+    assert np.array_equal(rows2.numpy(), ec) and np.array_equal(cols2.numpy(), er)
+
+
+def test_scan_extension_validates_before_launch(hb):
+    ext = hb.ScanExtension()
+    x = torch.zeros(4, 3)
+    v = torch.zeros(4, dtype=torch.float64)
+    with pytest.raises(ValueError, match="CUDA FP32 feature"):
+        ext.fused_bidir_topk_stats_raw(x, x, v, v, v, v, 8, 8, 64, 2, True, True, False, 2, 2.0)
+    with pytest.raises(ValueError, match="power-of-two bucket"):
+        ext.fused_bidir_topk_stats_raw(x, x, v, v, v, v, 8, 8, 64, 3, True, True, False, 0, 2.0)
+    with pytest.raises(NotImplementedError, match="perturbation"):
+        ext.fused_gcost_bidir_certificate(x, x, v, v, 2, 0, sigma=0.1)
+
+
+def test_pdlp_validates_controls(hb):
+    with pytest.raises(ValueError):
+        hb.NativeRestrictedOTPDLP(device="cpu")
+    with pytest.raises(ValueError):
+        hb.NativeRestrictedOTPDLP(device="cuda:0", evaluation_frequency=0)
