@@ -1,0 +1,417 @@
+"""Benchmark of the HELLO pricing scan on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--cost l2sq] [--n 1048576] [--d 256] [--k 8] [--precision fp32]
+
+Workload (default): config 5 of the baseline, the isolated pricing scan with
+m = n = 1,048,576 points, d = 256, ℓ2² cost, top-k = 8 per row and column;
+points ~ N(0, I) fp32, duals f, g ~ N(0, 1) x the median pairwise cost
+(estimated from 65,536 sampled pairs, seed 42).  Synthetic data stands in
+for the reference's public benchmark features, which are not available here.
+
+A step is one full bidirectional scan: both top-k directions, the five
+certificate sums and candidate extraction to device buffers.  `value` is
+m*n / (device time per step), inputs resident in HBM, timed with CUDA events
+between barriers (max over ranks).  `e2e` runs the host-facing API
+(raw_lowrank_bidir_feasibility_pricing_scan) from pinned host arrays with the
+uploads and the candidate read-back inside the timed region.  The clouds are
+2 GB, larger than L2, so no flush is needed between steps.
+
+With --gpus N (launched under torchrun) source rows are split across ranks
+(strong scaling: total work fixed); the target cloud is broadcast once and the
+target duals every step, column lists are all-gathered and merged over NCCL.
+
+--impl reference times the reference's own CPU scan (its C++ dot_tile kernel,
+built from its sources into oracle/_ref, driven like cpp_violation_scan) on a
+bounded row sample of the same workload on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per pair of one pass-1 launch, from an ncu capture of the
+# scan kernel scaled by the pairs it processed (see profiles/ for the capture and command).
+DRAM_BYTES_PER_PAIR: dict = {}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--cost", default="l2sq", choices=["l2sq"])
+    p.add_argument("--n", type=int, default=1_048_576)
+    p.add_argument("--d", type=int, default=256)
+    p.add_argument("--k", type=int, default=8)
+    p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ workload
+def make_workload(n, d, seed, device, rows=None):
+    """Points ~ N(0, I), duals ~ N(0, 1) * median pairwise ℓ2² cost.  `rows`
+    (start, stop) limits the source cloud to a block (same values as the full
+    cloud's rows).  Generated on `device` with torch's Philox generator."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    y = torch.randn(n, d, device=device, generator=g)
+    x_full_seed = seed + 1
+    gx = torch.Generator(device=device)
+    gx.manual_seed(x_full_seed)
+    lo, hi = rows if rows is not None else (0, n)
+    # generate the source cloud in fixed 65536-row chunks so a block equals the full cloud's rows
+    chunk = 65536
+    parts = []
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        gc = torch.Generator(device=device)
+        gc.manual_seed(x_full_seed * 1_000_003 + c0)
+        if c1 <= lo or c0 >= hi:
+            continue
+        block = torch.randn(c1 - c0, d, device=device, generator=gc)
+        parts.append(block[max(lo, c0) - c0:min(hi, c1) - c0])
+    x = torch.cat(parts)
+    a = (x.double() ** 2).sum(1)
+    b = (y.double() ** 2).sum(1)
+    # median pairwise cost from 65536 sampled pairs (seed 42)
+    gs = torch.Generator(device=device)
+    gs.manual_seed(42)
+    si = torch.randint(0, x.shape[0], (65536,), device=device, generator=gs)
+    sj = torch.randint(0, n, (65536,), device=device, generator=gs)
+    med = float(((x[si].double() - y[sj].double()) ** 2).sum(1).median().item())
+    f = torch.randn(x.shape[0], device=device, dtype=torch.float64, generator=gs) * med
+    gd = torch.randn(n, device=device, dtype=torch.float64, generator=gs) * med
+    return x, y, a, b, f, gd, med
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.path = Path(tempfile.mkstemp(prefix="clocks", suffix=".csv")[1])
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ reference CPU scan
+def reference_cpu_scan(x, y, a, b, f, g, k, scale, threads):
+    """The reference's CPU ℓ2² scan: torch.mm product tiles and its C++ dot_tile
+    kernel (src/hello_ot/kernels/cpp_scan.py:95-182, _native/cpp/scan.cpp:137-227),
+    with the tile shape of torch_scan._tile_shape (64 MB budget)."""
+    import oracle
+
+    ext = oracle.load_ref("scan")
+    ns, m = x.shape[0], y.shape[0]
+    rk, ck = min(k, m), min(k, ns)
+    rv = torch.full((ns, rk), -torch.inf, dtype=torch.float64)
+    ri = torch.full((ns, rk), -1, dtype=torch.int64)
+    cv = torch.full((m, ck), -torch.inf, dtype=torch.float64)
+    ci = torch.full((m, ck), -1, dtype=torch.int64)
+    sb = min(ns, 256)
+    tb = min(m, max(1, (64 * 1024 * 1024 // 32) // sb))
+    stats = [0.0, 0.0, 0, 0.0, 0.0]
+    for s0 in range(0, ns, sb):
+        s1 = min(ns, s0 + sb)
+        for t0 in range(0, m, tb):
+            t1 = min(m, t0 + tb)
+            prod = torch.mm(x[s0:s1], y[t0:t1].T)
+            num, den, cnt, mx, cm = ext.dot_tile(prod.numpy(), a[s0:s1].numpy(), b[t0:t1].numpy(),
+                                                 f[s0:s1].numpy(), g[t0:t1].numpy(), rv[s0:s1].numpy(),
+                                                 ri[s0:s1].numpy(), cv[t0:t1].numpy(), ci[t0:t1].numpy(), scale,
+                                                 s0, t0, 0, threads)
+            stats[0] += num; stats[1] += den; stats[2] += cnt
+            stats[3] = max(stats[3], mx); stats[4] = max(stats[4], cm)
+    rm, cmk = rv > 0, cv > 0
+    rows = torch.cat((torch.arange(ns)[:, None].expand(-1, rk)[rm], ci[cmk]))
+    return rows.numel(), stats
+
+
+def cpu_reference_rate(x, y, a, b, f, g, k, scale, target_s, threads):
+    """Gpairs/s of the reference CPU scan on a row sample sized for ~target_s seconds."""
+    x, y, a, b, f, g = (t.detach().cpu() for t in (x, y, a, b, f, g))
+    probe = min(64, x.shape[0])
+    t0 = time.perf_counter()
+    reference_cpu_scan(x[:probe], y, a[:probe], b, f[:probe], g, k, scale, threads)
+    dt = time.perf_counter() - t0
+    rows = int(min(x.shape[0], max(probe, probe * target_s / max(dt, 1e-3))))
+    rows = max(probe, (rows // 64) * 64)
+    t0 = time.perf_counter()
+    reference_cpu_scan(x[:rows], y, a[:rows], b, f[:rows], g, k, scale, threads)
+    dt = time.perf_counter() - t0
+    return rows * y.shape[0] / dt / 1e9, rows, dt
+
+
+# ------------------------------------------------------------------ main arms
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    try:
+        oracle.load_ref("scan")
+    except Exception as exc:  # the reference's CPU build is missing
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU backend not built: {exc}"}))
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n, d, k = args.n, args.d, args.k
+    # same distribution, generated on the CPU (the reference arm uses no GPU)
+    x, y, a, b, f, g, med = make_workload(n, d, 42, torch.device("cpu"), rows=(0, 16384))
+    # one step ~ cpu_seconds / 2 of reference work
+    probe = 64
+    t0 = time.perf_counter()
+    reference_cpu_scan(x[:probe], y, a[:probe], b, f[:probe], g, k, 2.0, threads)
+    dt = time.perf_counter() - t0
+    rows = int(min(x.shape[0], max(probe, probe * (args.cpu_seconds / 2) / max(dt, 1e-3))))
+    rows = max(probe, rows // 64 * 64)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        reference_cpu_scan(x[:rows], y, a[:rows], b, f[:rows], g, k, 2.0, threads)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = rows * n / sec / 1e9
+    sample = f"{rows} source rows x {n} targets per step (d={d}, k={k}), reference dot_tile + torch.mm"
+    print(json.dumps({
+        "impl": "reference", "metric": "pricing-scan Gpairs/s (m·n)", "value": value, "unit": "Gpairs/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": value, "unit": "Gpairs/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "Gpairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def workload_config(args):
+    return {"workload": f"C5 isolated pricing scan, l2sq, m=n={args.n}, d={args.d}, k={args.k}",
+            "n": args.n, "m": args.n, "d": args.d, "topk": args.k, "cost": "l2sq", "dot_scale": 2.0,
+            "precision": {"fp32": "3xTF32 (fp32-class dot)", "tf32": "1xTF32"}[args.precision],
+            "parallelism": f"source-row shards x{args.gpus}",
+            "l2_policy": "inputs (2 GB clouds) larger than L2; no flush"}
+
+
+def run_ours(args):
+    import __graft_entry__ as entry
+
+    hb = entry.load_package()
+    from hello_ot_b200.sharded import ShardedPricingScan, row_partition
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    n, d, k = args.n, args.d, args.k
+    lo, hi = row_partition(n, world, rank)
+    x, y, a, b, f, g, med = make_workload(n, d, 42, dev, rows=(lo, hi))
+    if world > 1:  # the target cloud is replicated from rank 0 (once per solve)
+        dist.broadcast(y, 0)
+        dist.broadcast(b, 0)
+    sharded = ShardedPricingScan(precision=args.precision)
+    g_step = g.clone()
+
+    def step():
+        if world > 1:
+            dist.broadcast(g_step, 0)  # target duals change every scan
+        r = sharded.scan(x, y, a, b, f, g_step, k, row_offset=lo)
+        return r
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches0 = hb.kernel_launch_count()
+    hb.set_kernel_timing(True)
+    pass_ms = []  # device time of each scan pass kernel, CUDA events inside the library
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start.record()
+        for _ in range(args.steps):
+            step()
+            pass_ms.append(hb.last_kernel_times()[:2])
+        stop.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    hb.set_kernel_timing(False)
+    launches = hb.kernel_launch_count() - launches0
+    elapsed = start.elapsed_time(stop) / 1e3
+    t = torch.tensor([elapsed], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sec = float(t.item()) / args.steps
+    value = n * n / sec / 1e9
+
+    times = [sum(p[j] for p in pass_ms) / len(pass_ms) for j in range(2)] if all(len(p) == 2 for p in pass_ms) \
+        else []
+    out = None
+    if rank == 0:
+        peaks, peak_kind = load_peaks()
+        rows_local = hi - lo
+        pass1_ms = times[0] if times else float("nan")
+        flops = 2.0 * d * rows_local * n  # algorithmic flops of one pass: one dot product per pair
+        achieved = flops / (pass1_ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+        per_pair = DRAM_BYTES_PER_PAIR.get((d, args.precision))
+        traffic = per_pair * rows_local * n if per_pair else None
+        out = {
+            "metric": "pricing-scan Gpairs/s (m·n)", "value": value, "unit": "Gpairs/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "tf32x3/f64" if args.precision == "fp32" else "tf32/f64",
+            "data": "synthetic (seeded N(0,I) clouds, Gaussian duals scaled by the median cost)",
+            "config": workload_config(args),
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "hb::l2sq::scan_kernel (pass 1: source rows, certificate)",
+                         "pass_ms": times[:2], "peak_source": f"{peak_kind} bf16 dense (sustained)",
+                         "note": ("algorithmic flops 2*d per pair; the 3xTF32 split issues 3 tf32 products "
+                                  "per pair on a pipe with half the bf16 rate")},
+            "clocks": clocks.summary(),
+            "median_pair_cost": med,
+        }
+    # ---- end to end through the host-facing API (pinned host inputs, candidates back to host)
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory(); yh = y.cpu().pin_memory()
+        ah, bh, fh, gh = (v.cpu().pin_memory() for v in (a, b, f, g))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e2e_times, h2d, d2h = [], 0, 0
+        for i in range(max(1, args.steps) + 1):
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            if world == 1:
+                r = hb.raw_lowrank_bidir_feasibility_pricing_scan(xh, yh, ah, bh, fh, gh, topk=k, dot_scale=2.0,
+                                                                  compute_precision=args.precision)
+                h2d = sum(v.numel() * v.element_size() for v in (xh, yh, ah, bh, fh, gh))
+                d2h = (r.rows.size + r.cols.size) * 8 + 5 * 8
+            else:
+                xd, yd = xh.to(dev, non_blocking=True), yh.to(dev, non_blocking=True)
+                ad, bd, fd, gd = (v.to(dev, non_blocking=True) for v in (ah, bh, fh, gh))
+                r = sharded.scan(xd, yd, ad, bd, fd, gd, k, row_offset=lo)
+                h2d = sum(v.numel() * v.element_size() for v in (xh, yh, ah, bh, fh, gh))
+                if rank == 0:
+                    rows_h, cols_h = r.rows.cpu().numpy(), r.cols.cpu().numpy()
+                    d2h = (rows_h.size + cols_h.size) * 8
+                s = r.stats.cpu()
+                d2h += 5 * 8
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            if i > 0:
+                e2e_times.append(time.perf_counter() - t0)
+        et = torch.tensor([sum(e2e_times) / len(e2e_times)], device=dev)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            out["e2e"] = {"value": n * n / float(et.item()) / 1e9, "unit": "Gpairs/s",
+                          "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                          "api": "raw_lowrank_bidir_feasibility_pricing_scan (host arrays)" if world == 1
+                          else "ShardedPricingScan.scan from pinned host blocks"}
+    # ---- CPU baseline: the reference's CPU scan on a bounded row sample (rank 0, N=1)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            threads = os.cpu_count() or 1
+            torch.set_num_threads(threads)
+            rate, rows, dt = cpu_reference_rate(x[:65536], y, a[:65536], b, f[:65536], g, k, 2.0,
+                                                args.cpu_seconds, threads)
+            out["cpu_baseline"] = {"value": rate, "unit": "Gpairs/s", "cores": threads, "kind": "reference",
+                                   "sample": f"{rows} source rows x {n} targets (d={d}, k={k}) in {dt:.1f} s; "
+                                             "reference dot_tile (scan.cpp) + torch.mm tiles"}
+        except Exception as exc:  # reference CPU build missing
+            out["cpu_baseline"] = {"value": None, "unit": "Gpairs/s", "cores": 0, "kind": "reference",
+                                   "sample": f"unavailable: {exc}"}
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

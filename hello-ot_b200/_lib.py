@@ -18,8 +18,9 @@ ABI_VERSION = 1
 HB_OK, HB_BAD_ARGUMENT, HB_BAD_INPUT, HB_WORKSPACE = 0, 1, 2, 3
 HB_CUDA, HB_TENSOR_MAP, HB_LAUNCH, HB_DEVICE_TIMEOUT = 4, 5, 6, 7
 
-EXPORTS = ("hb_abi_version", "hb_last_error", "hb_l2sq_scan_workspace", "hb_l2sq_scan", "hb_norm_scan_workspace",
-           "hb_norm_scan", "hb_pair_costs_workspace", "hb_pair_costs", "hb_restricted_ot_workspace",
+EXPORTS = ("hb_abi_version", "hb_last_error", "hb_kernel_launch_count", "hb_set_kernel_timing",
+           "hb_last_kernel_times", "hb_l2sq_scan_workspace", "hb_l2sq_scan", "hb_norm_scan_workspace",
+           "hb_norm_scan", "hb_merge_topk", "hb_pair_costs_workspace", "hb_pair_costs", "hb_restricted_ot_workspace",
            "hb_restricted_ot_solve")
 
 
@@ -67,6 +68,11 @@ def load_library(path: Path | str = LIB_PATH):
     P = c_void_p
     lib.hb_abi_version.restype = c_int
     lib.hb_last_error.restype = ctypes.c_char_p
+    lib.hb_kernel_launch_count.restype = ctypes.c_ulonglong
+    lib.hb_set_kernel_timing.argtypes = [c_int]
+    lib.hb_set_kernel_timing.restype = None
+    lib.hb_last_kernel_times.argtypes = [POINTER(c_double), c_int]
+    lib.hb_last_kernel_times.restype = c_int
     lib.hb_l2sq_scan_workspace.restype = c_size_t
     lib.hb_l2sq_scan_workspace.argtypes = [c_int64, c_int64, c_int64, c_int, c_int, c_int]
     lib.hb_l2sq_scan.restype = c_int
@@ -77,6 +83,8 @@ def load_library(path: Path | str = LIB_PATH):
     lib.hb_norm_scan.restype = c_int
     lib.hb_norm_scan.argtypes = [P, P, c_int64, c_int64, c_int64, P, P, c_int, c_int, c_int, P, P, P, P, P, P,
                                  c_size_t, P]
+    lib.hb_merge_topk.restype = c_int
+    lib.hb_merge_topk.argtypes = [P, P, c_int, c_int64, c_int, c_int, P, P, P]
     lib.hb_pair_costs_workspace.restype = c_size_t
     lib.hb_pair_costs.restype = c_int
     lib.hb_pair_costs.argtypes = [c_int, P, P, c_int64, c_int64, c_int64, P, P, c_double, P, P, c_int64, P, P,
@@ -106,6 +114,22 @@ def check(rc: int) -> None:
         if rc in (HB_BAD_ARGUMENT, HB_BAD_INPUT):
             raise ValueError(f"[hello_b200 error {rc}] {msg}")
         raise HBError(rc, msg)
+
+
+def kernel_launch_count() -> int:
+    """Kernels launched by libhello_b200 in this process so far."""
+    return int(load_library().hb_kernel_launch_count())
+
+
+def set_kernel_timing(enable: bool) -> None:
+    load_library().hb_set_kernel_timing(int(bool(enable)))
+
+
+def last_kernel_times() -> list:
+    """Device times (ms) of the main kernels of this thread's last call."""
+    buf = (c_double * 16)()
+    n = load_library().hb_last_kernel_times(buf, 16)
+    return [buf[i] for i in range(min(n, 16))]
 
 
 def ptr(t) -> int | None:

@@ -10,14 +10,40 @@
 
 #include "internal.h"
 
+#include <atomic>
+#include <vector>
+
 namespace {
 thread_local std::string g_error;
+std::atomic<unsigned long long> g_launches{0};
+
+// Per-thread event timing of the kernels of the last call.
+struct Timing {
+    bool on = false;
+    std::vector<cudaEvent_t> events;
+    int used = 0;
+    std::vector<double> last_ms;
+};
+thread_local Timing g_timing;
 
 int fail(int code, const std::string& msg) {
     g_error = msg;
     return code;
 }
 
+// Called after the call's stream has been synchronised: turn the marks into
+// per-interval device times (marks are placed in pairs around kernels).
+void collect_timing() {
+    Timing& t = g_timing;
+    if (t.used == 0) return;  // a call without timed kernels keeps the previous times
+    t.last_ms.clear();
+    for (int i = 0; i + 1 < t.used; i += 2) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, t.events[i], t.events[i + 1]);
+        t.last_ms.push_back(ms);
+    }
+    t.used = 0;
+}
 // Synchronise the stream, then map the scan's device status word.
 int finish(cudaStream_t st, const int* status_dev, const char* what) {
     int status = 0;
@@ -27,6 +53,7 @@ int finish(cudaStream_t st, const int* status_dev, const char* what) {
     }
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(HB_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    collect_timing();
     if (status & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, std::string(what) + ": a device-side wait timed out");
     if (status & hb::kErrBadInput) return fail(HB_BAD_INPUT, std::string(what) + ": index out of range");
     g_error.clear();
@@ -34,13 +61,41 @@ int finish(cudaStream_t st, const int* status_dev, const char* what) {
 }
 
 bool valid_k(int k) { return k >= 0 && k <= 32; }
+
 }  // namespace
+
+namespace hb {
+void count_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+void timing_mark(cudaStream_t st) {
+    Timing& t = g_timing;
+    if (!t.on) return;
+    if (t.used == (int)t.events.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return;
+        t.events.push_back(e);
+    }
+    cudaEventRecord(t.events[t.used++], st);
+}
+}  // namespace hb
 
 extern "C" {
 
 int hb_abi_version(void) { return HB_ABI_VERSION; }
 
 const char* hb_last_error(void) { return g_error.c_str(); }
+
+unsigned long long hb_kernel_launch_count(void) { return g_launches.load(); }
+
+void hb_set_kernel_timing(int enable) {
+    g_timing.on = enable != 0;
+    g_timing.used = 0;
+}
+
+int hb_last_kernel_times(double* ms, int capacity) {
+    const int n = (int)g_timing.last_ms.size();
+    for (int i = 0; i < n && i < capacity; ++i) ms[i] = g_timing.last_ms[i];
+    return n;
+}
 
 size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups) {
     if (q < 1 || n < 1 || d < 1 || !valid_k(k)) return 0;
@@ -72,6 +127,7 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (rc) return fail(rc == 3 ? HB_WORKSPACE : rc == 5 ? HB_TENSOR_MAP : HB_LAUNCH, err);
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(HB_CUDA, std::string("l2sq scan: ") + cudaGetErrorString(e));
+    collect_timing();
     if (status_host & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, "l2sq scan: a device-side wait timed out");
     g_error.clear();
     return HB_OK;
@@ -99,6 +155,19 @@ int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
                            stats5, workspace, workspace_bytes, st, err);
     if (rc) return fail(rc == 3 ? HB_WORKSPACE : HB_LAUNCH, err);
     return finish(st, nullptr, "norm scan");
+}
+
+int hb_merge_topk(const double* vals, const int32_t* idx, int parts, int64_t rows, int width, int k,
+                  double* out_vals, int32_t* out_idx, void* stream) {
+    if (!vals || !idx || !out_vals || !out_idx) return fail(HB_BAD_ARGUMENT, "null pointer");
+    if (parts < 1 || rows < 0 || width < 1 || width > 32 || k < 1 || k > 32)
+        return fail(HB_BAD_ARGUMENT, "merge needs parts >= 1, 1 <= width, k <= 32");
+    if (rows == 0) { g_error.clear(); return HB_OK; }
+    const int K = hb::bucket_of(width > k ? width : k);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = hb::merge_lists(K, vals, idx, parts, rows, width, k, out_vals, out_idx, st);
+    if (e != cudaSuccess) return fail(HB_LAUNCH, std::string("merge: ") + cudaGetErrorString(e));
+    return finish(st, nullptr, "merge");
 }
 
 size_t hb_pair_costs_workspace(void) { return 256; }

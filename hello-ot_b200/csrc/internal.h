@@ -7,6 +7,11 @@
 
 namespace hb {
 
+// Instrumentation: a process-wide count of kernel launches issued by this
+// library, and optional CUDA-event timing of the main kernels of a call.
+void count_launches(int n);
+void timing_mark(cudaStream_t st);  // no-op unless timing is enabled on this thread
+
 // ℓ2² scan (scan_l2sq.cu)
 size_t l2sq_bytes(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
 int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* nx, const double* ny,
@@ -20,7 +25,9 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
               int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
               size_t ws_bytes, cudaStream_t st, std::string& err);
 
-// partial top-k merge (scan_l2sq.cu)
+// partial top-k merge (scan_l2sq.cu): lists of `width` entries, bucket K >= width
+cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out,
+                        double* ov, int* oi, cudaStream_t st);
 cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
                       cudaStream_t st);
 

@@ -14,6 +14,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace hb {
 namespace pairs {
@@ -85,8 +86,11 @@ template <int KIND, int G>
 void launch_g(bool vec, const float* x, const float* y, int64_t nx, int64_t ny, int d, const double* a,
               const double* b, double s, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
               int* status, int blocks, cudaStream_t st) {
+    timing_mark(st);
     if (vec) pair_kernel<KIND, G, true><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status);
     else pair_kernel<KIND, G, false><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status);
+    timing_mark(st);
+    count_launches(1);
 }
 
 template <int KIND>

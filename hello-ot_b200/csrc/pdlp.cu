@@ -370,6 +370,8 @@ PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e)
 
 size_t pdlp_bytes(int64_t n, int64_t m, int64_t e) { return pdlp_layout(nullptr, 0, n, m, e).bytes; }
 
+#define HB_LAUNCHED(n) count_launches(n)
+
 int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, int64_t e, const double* masses,
                int64_t n, int64_t m, const double* x0, const double* y0, const PdlpControls& ctl, double* x_out,
                double* y_out, PdlpResult* res, TraceRow* trace, int trace_cap, int* trace_len, void* ws,
@@ -397,22 +399,33 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     cudaMemsetAsync(D.status, 0, sizeof(int), st);
     // --- incidence structure (solver.cpp:74-90): sort by source, then by target
     pdlp::check_convert<<<gb, 256, 0, st>>>(rows, cols, e, (int)n, (int)m, L.r32, L.c32, D.status);
+    HB_LAUNCHED(1);
     pdlp::iota_kernel<<<gb, 256, 0, st>>>(L.iota, e);
+    HB_LAUNCHED(1);
     size_t cb = L.cub_bytes;
     if (cub::DeviceRadixSort::SortPairs(L.cub, cb, L.r32, D.e_row, L.iota, D.e_orig, (int)e, 0, 32, st) != cudaSuccess)
         return fail("source sort");
+    HB_LAUNCHED(1);
     cb = L.cub_bytes;
     if (cub::DeviceRadixSort::SortPairs(L.cub, cb, L.c32, L.t_keys, L.iota, L.t_orig, (int)e, 0, 32, st) != cudaSuccess)
         return fail("target sort");
+    HB_LAUNCHED(1);
     pdlp::offsets_kernel<<<(unsigned)((n + 256) / 256), 256, 0, st>>>(D.e_row, e, (int)n, D.s_off);
+    HB_LAUNCHED(1);
     pdlp::offsets_kernel<<<(unsigned)((m + 256) / 256), 256, 0, st>>>(L.t_keys, e, (int)m, D.t_off);
+    HB_LAUNCHED(1);
     pdlp::gather_edges<<<gb, 256, 0, st>>>(D.e_orig, L.c32, costs, x0, e, D.e_col, D.cost, L.x0s, L.inv);
+    HB_LAUNCHED(1);
     pdlp::map_positions<<<gb, 256, 0, st>>>(L.t_orig, L.inv, e, D.t_pos);
+    HB_LAUNCHED(1);
     pdlp::degree_scale<<<gb, 256, 0, st>>>(D.s_off, D.t_off, (int)n, (int)m, D.scale);
+    HB_LAUNCHED(1);
     // --- norms and scaling (solver.cpp:91-110)
     double h[16];
     pdlp::sumsq2_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(masses, n + m, costs, e, D.red);
+    HB_LAUNCHED(1);
     pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
+    HB_LAUNCHED(1);
     if (cudaGetLastError() != cudaSuccess) return fail("setup");
     cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
     int status = 0;
@@ -425,10 +438,13 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     const double variable = std::sqrt(2.0);
     const double vb = variable * bound;
     pdlp::init_state<<<gb, 256, 0, st>>>(D, masses, y0, L.x0s, bound, objective, variable);
+    HB_LAUNCHED(1);
     double weight = 1.0;
     if (!ctl.rescale) {
         pdlp::sumsq2_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D.cs, e, D.bs, n + m, D.red);
+        HB_LAUNCHED(1);
         pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
+        HB_LAUNCHED(1);
         cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
         if (cudaStreamSynchronize(st) != cudaSuccess) return fail("weight sync");
         weight = std::max(std::sqrt(h[0]) / std::max(std::sqrt(h[1]), 1e-16), 1e-16);
@@ -448,7 +464,9 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     const int F = ctl.frequency;
     for (;;) {
         pdlp::evaluate_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D, vb, objective);
+        HB_LAUNCHED(1);
         pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 4, D.scal, 0);
+        HB_LAUNCHED(1);
         if (cudaGetLastError() != cudaSuccess) return fail("evaluate");
         cudaMemcpyAsync(h, D.scal, 16 * sizeof(double), cudaMemcpyDeviceToHost, st);
         if (cudaStreamSynchronize(st) != cudaSuccess) return fail("evaluate sync");
@@ -484,7 +502,9 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         last_trial = fixed;
         if (restart) {
             pdlp::restart_dist_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);
+            HB_LAUNCHED(1);
             pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
+            HB_LAUNCHED(1);
             cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
             if (cudaStreamSynchronize(st) != cudaSuccess) return fail("restart sync");
             const double pd = std::sqrt(h[0]), dd = std::sqrt(h[1]);
@@ -505,8 +525,11 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             last_trial = inf;
             ++restarts;
             pdlp::restart_kernel<<<gb, 256, 0, st>>>(D);
+            HB_LAUNCHED(1);
         }
         const double primal_step = 0.998 / weight, dual_step = 0.998 * weight;
+        const bool first_block = count == 0;
+        if (first_block) timing_mark(st);
         for (int t = 0; t < F; ++t) {
             pdlp::Step s;
             s.primal_step = primal_step;
@@ -516,18 +539,24 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             const bool is_restart = t == 0 && restart;
             s.checkpoint = s.major || is_restart;
             pdlp::source_pass<<<gb, 256, 0, st>>>(D, s);
+            HB_LAUNCHED(1);
             pdlp::target_pass<<<gb, 256, 0, st>>>(D, s);
+            HB_LAUNCHED(1);
             if (s.checkpoint) {
                 pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);
+                HB_LAUNCHED(1);
                 // scal[5..7]: terms at the restart iteration, scal[9..11]: at the major iteration
                 pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 3, D.scal, s.major ? 9 : 5);
+                HB_LAUNCHED(1);
             }
             ++count;
             ++inner;
         }
+        if (first_block) timing_mark(st);
         if (cudaGetLastError() != cudaSuccess) return fail("iteration");
     }
     pdlp::output_kernel<<<gb, 256, 0, st>>>(D, vb, objective, x_out, y_out);
+    HB_LAUNCHED(1);
     if (cudaStreamSynchronize(st) != cudaSuccess) return fail("output");
     res->iterations = count;
     res->restarts = restarts;

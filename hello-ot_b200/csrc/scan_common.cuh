@@ -40,23 +40,23 @@ inline ScanPlan scan_plan(int64_t q, int64_t n, int bm, int bn, int ctas_per_sm,
     return p;
 }
 
-// Merge the `parts` partial k-lists of each row (rows x K per part, parts
-// stored part-major) into the first `k_out` entries of the final list.  Empty
-// slots come out as (-inf, -1).  Thread per row.
+// Merge the `parts` partial lists of each row (rows x width per part, parts
+// stored part-major, width <= K) into the first `k_out` entries of the final
+// list.  Slots with index INT32_MAX or negative are empty; empty output slots
+// come out as (-inf, -1).  Thread per row.
 template <int K>
 __global__ void merge_partials(const double* __restrict__ pv, const int* __restrict__ pi, int parts, int64_t rows,
-                               int k_out, double* __restrict__ out_v, int* __restrict__ out_i) {
+                               int width, int k_out, double* __restrict__ out_v, int* __restrict__ out_i) {
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     TopK<K> top;
     top.reset();
     for (int c = 0; c < parts; ++c) {
-        const double* v = pv + ((int64_t)c * rows + r) * K;
-        const int* ix = pi + ((int64_t)c * rows + r) * K;
-#pragma unroll
-        for (int s = 0; s < K; ++s) {
+        const double* v = pv + ((int64_t)c * rows + r) * width;
+        const int* ix = pi + ((int64_t)c * rows + r) * width;
+        for (int s = 0; s < width; ++s) {
             const int id = ix[s];
-            if (id != INT32_MAX) top.offer(v[s], id);
+            if (id != INT32_MAX && id >= 0) top.offer(v[s], id);
         }
     }
 #pragma unroll

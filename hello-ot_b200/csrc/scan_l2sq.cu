@@ -145,27 +145,52 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
             for (int ch = 0; ch < BN / 32 && ch * 32 < ncols; ++ch) {
                 float v[32];
                 tmem_ld32(taddr + ch * 32, v);
-                tmem_wait_ld();
+                tmem_wait_ld(v);
+                const int cb = ch * 32;
+                const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
+                // phase 1, branch-free: scores, certificate terms and a mask of the
+                // columns that beat the row's k-th entry as it stood at chunk start
+                const double tv = top.v[KK - 1];
+                const int ti = top.i[KK - 1];
+                uint32_t mask = 0;
                 double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
+                double mpos = 0.0, mcost = 0.0;
+                int cnt = 0;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int c = ch * 32 + j;
-                    if (c < ncols && rvalid) {
-                        const double dot = (double)(p.scale * v[j]);
-                        const double cb = wbias[c];
-                        const double sc = SWAP ? ((dot + cb) + rbias) : ((dot + rbias) + cb);
-                        if (STATS) {
-                            const double co = (rcost + wcost[c]) - dot;
-                            den4[j & 3] += co * co;
-                            acc[3] = fmax(acc[3], fabs(co));
-                            if (sc > 0.0) { num4[j & 3] += sc * sc; acc[2] = fmax(acc[2], sc); acc[4] += 1.0; }
-                        }
-                        if (K > 0) top.offer(sc, c0 + c);
+                    const bool ok = j < live;
+                    const double dot = (double)(p.scale * v[j]);
+                    const double cbias = wbias[cb + j];
+                    const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
+                    if (STATS) {
+                        const double co = (rcost + wcost[cb + j]) - dot;
+                        den4[j & 3] += ok ? co * co : 0.0;
+                        mcost = fmax(mcost, ok ? fabs(co) : 0.0);
+                        const bool pos = ok && sc > 0.0;
+                        num4[j & 3] += pos ? sc * sc : 0.0;
+                        mpos = fmax(mpos, pos ? sc : 0.0);
+                        cnt += pos ? 1 : 0;
                     }
+                    if (K > 0) mask |= (ok && better(sc, c0 + cb + j, tv, ti)) ? (1u << j) : 0u;
                 }
                 if (STATS) {
                     acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
                     acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
+                    acc[2] = fmax(acc[2], mpos);
+                    acc[3] = fmax(acc[3], mcost);
+                    acc[4] += (double)cnt;
+                }
+                // phase 2 (rare once the list has filled): insert the masked columns
+                while (K > 0 && mask) {
+                    const int j = __ffs(mask) - 1;
+                    mask &= mask - 1;
+                    float vj = 0.0f;
+#pragma unroll
+                    for (int t2 = 0; t2 < 32; ++t2) vj = t2 == j ? v[t2] : vj;
+                    const double dot = (double)(p.scale * vj);
+                    const double cbias = wbias[cb + j];
+                    const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
+                    top.offer(sc, c0 + cb + j);
                 }
             }
             tc_fence_before();
@@ -298,7 +323,10 @@ cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
+    timing_mark(st);
     fn<<<grid, l2sq::THREADS, l2sq::SMEM_BYTES, st>>>(p);
+    timing_mark(st);
+    count_launches(1);
     return cudaGetLastError();
 }
 
@@ -326,21 +354,27 @@ int device_sms() {
 }  // namespace
 
 template <int K>
-cudaError_t launch_merge(const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
-                         cudaStream_t st) {
-    merge_partials<K><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(pv, pi, parts, rows, k_out, ov, oi);
+cudaError_t launch_merge(const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out, double* ov,
+                         int* oi, cudaStream_t st) {
+    merge_partials<K><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(pv, pi, parts, rows, width, k_out, ov, oi);
+    count_launches(1);
     return cudaGetLastError();
 }
 
 cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
                       cudaStream_t st) {
+    return merge_lists(K, pv, pi, parts, rows, K, k_out, ov, oi, st);
+}
+
+cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out,
+                        double* ov, int* oi, cudaStream_t st) {
     switch (K) {
-        case 1: return launch_merge<1>(pv, pi, parts, rows, k_out, ov, oi, st);
-        case 2: return launch_merge<2>(pv, pi, parts, rows, k_out, ov, oi, st);
-        case 4: return launch_merge<4>(pv, pi, parts, rows, k_out, ov, oi, st);
-        case 8: return launch_merge<8>(pv, pi, parts, rows, k_out, ov, oi, st);
-        case 16: return launch_merge<16>(pv, pi, parts, rows, k_out, ov, oi, st);
-        case 32: return launch_merge<32>(pv, pi, parts, rows, k_out, ov, oi, st);
+        case 1: return launch_merge<1>(pv, pi, parts, rows, width, k_out, ov, oi, st);
+        case 2: return launch_merge<2>(pv, pi, parts, rows, width, k_out, ov, oi, st);
+        case 4: return launch_merge<4>(pv, pi, parts, rows, width, k_out, ov, oi, st);
+        case 8: return launch_merge<8>(pv, pi, parts, rows, width, k_out, ov, oi, st);
+        case 16: return launch_merge<16>(pv, pi, parts, rows, width, k_out, ov, oi, st);
+        case 32: return launch_merge<32>(pv, pi, parts, rows, width, k_out, ov, oi, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -406,6 +440,7 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (L.xpad || L.xlo) {
         l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(x, q, (int)d, dp, L.xpad, L.xlo);
         l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(y, n, (int)d, dp, L.ypad, L.ylo);
+        count_launches(2);
         if (L.xpad) { xs = L.xpad; ys = L.ypad; }
     }
     l2sq::Params p;
@@ -431,14 +466,20 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (e != cudaSuccess) { err = std::string("l2sq pass 1: ") + cudaGetErrorString(e); return 6; }
     if (want_stats) {
         finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5);
+        count_launches(1);
     }
     if (K > 0) {
         e = merge_any(K, L.pv1, L.pi1, L.p1.groups, q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
         // pass 2: y rows are the queries, same products in the same order
+        // pass 2: y rows are the queries, same products in the same order;
+        // the maps are rebuilt because a map fixes its box height (A 128 rows, B 256 rows)
         l2sq::Params p2 = p;
-        std::swap(p2.qmap[0], p2.dmap[0]);
-        std::swap(p2.qmap[1], p2.dmap[1]);
+        bool maps2 = make_map(&p2.qmap[0], ys, n, dp, l2sq::BM) && make_map(&p2.dmap[0], xs, q, dp, l2sq::BN);
+        if (precision == 3)
+            maps2 = maps2 && make_map(&p2.qmap[1], L.ylo, n, dp, l2sq::BM) && make_map(&p2.dmap[1], L.xlo, q, dp, l2sq::BN);
+        else { p2.qmap[1] = p2.qmap[0]; p2.dmap[1] = p2.dmap[0]; }
+        if (!maps2) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
         // keep the product order x*y, x*lo(y), lo(x)*y with the operands exchanged
         for (int i = 0; i < 3; ++i) { p2.qsel[i] = ds[i]; p2.dsel[i] = qs[i]; }
         p2.q = (int)n; p2.n = (int)q;

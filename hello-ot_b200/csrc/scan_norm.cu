@@ -125,27 +125,45 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
             __syncthreads();
             if (rvalid) {
                 const int cb0 = half * 64;
+                const int live = min(64, ncols - cb0);  // valid columns of this half
+                const double tv = top.v[KK - 1];
+                const int ti = top.i[KK - 1];
+                uint64_t mask = 0;
                 double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
-                for (int c4 = cb0; c4 < cb0 + 64; c4 += 4) {
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const int c = c4 + jj;
-                        if (c < ncols) {
-                            const double cost = (double)s.dist[er][c];
-                            const double cbias = s.dbias[c];
-                            const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
-                            if (STATS) {
-                                den4[jj] += cost * cost;
-                                acc[3] = fmax(acc[3], fabs(cost));
-                                if (sc > 0.0) { num4[jj] += sc * sc; acc[2] = fmax(acc[2], sc); acc[4] += 1.0; }
-                            }
-                            if (K > 0) top.offer(sc, c0 + c);
-                        }
+                double mpos = 0.0, mcost = 0.0;
+                int cnt = 0;
+                // phase 1, branch-free: scores, certificate terms, candidate mask
+#pragma unroll 16
+                for (int j = 0; j < 64; ++j) {
+                    const bool ok = j < live;
+                    const double cost = (double)s.dist[er][cb0 + j];
+                    const double cbias = s.dbias[cb0 + j];
+                    const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
+                    if (STATS) {
+                        den4[j & 3] += ok ? cost * cost : 0.0;
+                        mcost = fmax(mcost, ok ? fabs(cost) : 0.0);
+                        const bool pos = ok && sc > 0.0;
+                        num4[j & 3] += pos ? sc * sc : 0.0;
+                        mpos = fmax(mpos, pos ? sc : 0.0);
+                        cnt += pos ? 1 : 0;
                     }
+                    if (K > 0) mask |= (ok && better(sc, c0 + cb0 + j, tv, ti)) ? (1ull << j) : 0ull;
                 }
                 if (STATS) {
                     acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
                     acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
+                    acc[2] = fmax(acc[2], mpos);
+                    acc[3] = fmax(acc[3], mcost);
+                    acc[4] += (double)cnt;
+                }
+                // phase 2: insert the masked columns (rare once the list has filled)
+                while (K > 0 && mask) {
+                    const int j = __ffsll(mask) - 1;
+                    mask &= mask - 1;
+                    const double cost = (double)s.dist[er][cb0 + j];
+                    const double cbias = s.dbias[cb0 + j];
+                    const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
+                    top.offer(sc, c0 + cb0 + j);
                 }
             }
             __syncthreads();
@@ -197,7 +215,10 @@ cudaError_t norm_launch(const norm::Params& p, int grid, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
+    timing_mark(st);
     fn<<<grid, norm::THREADS, sizeof(norm::Smem), st>>>(p);
+    timing_mark(st);
+    count_launches(1);
     return cudaGetLastError();
 }
 
@@ -278,7 +299,7 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     cudaError_t e = want_stats ? norm_kind<true, false>(kind, K, p, L.p1.grid, st)
                                : norm_kind<false, false>(kind, K, p, L.p1.grid, st);
     if (e != cudaSuccess) { err = std::string("norm pass 1: ") + cudaGetErrorString(e); return 6; }
-    if (want_stats) finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5);
+    if (want_stats) { finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5); count_launches(1); }
     if (K > 0) {
         e = merge_any(K, L.pv1, L.pi1, L.p1.groups * 2, q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }

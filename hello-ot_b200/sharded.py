@@ -1,0 +1,135 @@
+"""Source-row-sharded pricing scan over several GPUs (one process per GPU).
+
+The reference is single-GPU (src/hello_ot/refinement/dual_feasibility.py:146,172).
+Here rank r owns a contiguous block of source rows (x, a, f) and a replica of
+the target cloud (y, b, g; y is broadcast once per solve, g per scan).  Each
+rank runs the fused bidirectional scan on its block; the exchange steps are
+
+  * certificate: all-reduce of (sum s+^2, sum c^2, count) and (max s+, max |c|);
+  * column top-k: all-gather of the per-rank column lists (n x k scores + global
+    source indices) and a merge with the scan's order and tie rule;
+  * candidates: all-gather of the row-side candidate pairs to assemble the
+    reference's candidate order (source rows ascending, then target columns).
+
+All collectives go through torch.distributed (NCCL over NVLink on the GPU box,
+gloo in the CPU tests); kernel inputs are always local HBM.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from ._lib import check, lib, ptr, stream_handle
+
+
+def row_partition(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous balanced block [start, stop) of `total` rows for `rank`."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("invalid world/rank")
+    base, extra = divmod(int(total), int(world))
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def merge_topk(vals: torch.Tensor, idx: torch.Tensor, k: int):
+    """Merge `parts` top-k lists per row on the GPU: vals/idx (parts, rows, width)."""
+    parts, rows, width = vals.shape
+    out_v = torch.empty((rows, k), dtype=torch.float64, device=vals.device)
+    out_i = torch.empty((rows, k), dtype=torch.int32, device=vals.device)
+    L = lib()
+    with torch.cuda.device(vals.device):
+        rc = L.hb_merge_topk(ptr(vals.contiguous()), ptr(idx.to(torch.int32).contiguous()), parts, rows, width, k,
+                             ptr(out_v), ptr(out_i), stream_handle(vals.device))
+    check(rc)
+    return out_v, out_i
+
+
+@dataclass
+class ShardedScanResult:
+    rows: Optional[torch.Tensor]   # candidate pairs (rank 0 only when gathered)
+    cols: Optional[torch.Tensor]
+    stats: torch.Tensor            # [sum s+^2, sum c^2, max s+, max |c|, count], global
+    col_vals: torch.Tensor         # merged column top-k (n x k), every rank
+    col_idx: torch.Tensor
+    row_vals: torch.Tensor         # this rank's rows (local block)
+    row_idx: torch.Tensor
+
+
+def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
+    """(world, *t.shape) concatenation of every rank's t."""
+    if world == 1:
+        return t.unsqueeze(0)
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world, *t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+        return out
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    return torch.stack(parts)
+
+
+class ShardedPricingScan:
+    """Bidirectional ℓ2² pricing scan with source rows sharded across ranks.
+
+    ``local_scan(x, y, a, b, qb, dbb, k)`` -> (row_vals, row_idx, col_vals, col_idx,
+    stats5) and ``merge(vals, idx, k)`` default to the CUDA kernels; tests inject
+    CPU versions to exercise the exchange logic under gloo.
+    """
+
+    def __init__(self, group=None, *, local_scan: Optional[Callable] = None, merge: Optional[Callable] = None,
+                 dot_scale: float = 2.0, precision: str = "fp32"):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if local_scan is None:
+            from .scan import l2sq_scan
+
+            def local_scan(x, y, a, b, qb, dbb, k):
+                return l2sq_scan(x, y, a, b, qb, dbb, k, dot_scale=dot_scale, precision=precision)
+        self.local_scan = local_scan
+        self.merge = merge or merge_topk
+
+    def scan(self, x_block, y, a_block, b, f_block, g, k: int, *, row_offset: int, theta: float = 0.0,
+             gather_candidates: bool = True) -> ShardedScanResult:
+        world, group = self.world, self.group
+        rv, ri, cv, ci, stats = self.local_scan(x_block, y, a_block, b, f_block - a_block, g - b, k)
+        ci = torch.where(ci >= 0, ci + int(row_offset), ci)
+        # certificate
+        sums = stats[[0, 1, 4]].contiguous()
+        maxs = stats[[2, 3]].contiguous()
+        if world > 1:
+            dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+            dist.all_reduce(maxs, op=dist.ReduceOp.MAX, group=group)
+        total = torch.stack((sums[0], sums[1], maxs[0], maxs[1], sums[2]))
+        # column lists
+        if world > 1:
+            gv = _all_gather(cv.contiguous(), world, group)
+            gi = _all_gather(ci.to(torch.int32).contiguous(), world, group)
+            cv_m, ci_m = self.merge(gv, gi, k)
+        else:
+            cv_m, ci_m = cv, ci
+        rows = cols = None
+        if gather_candidates:
+            rmask = (rv > float(theta)) & (ri >= 0)
+            local_rows = torch.nonzero(rmask, as_tuple=False)[:, 0] + int(row_offset)
+            local_cols = ri[rmask].to(torch.int64)
+            pairs = torch.stack((local_rows.to(torch.int64), local_cols))
+            if world > 1:
+                count = torch.tensor([pairs.shape[1]], dtype=torch.int64, device=pairs.device)
+                counts = _all_gather(count, world, group).view(-1)
+                width = int(counts.max().item())
+                padded = torch.full((2, width), -1, dtype=torch.int64, device=pairs.device)
+                padded[:, :pairs.shape[1]] = pairs
+                allp = _all_gather(padded, world, group)
+                pairs = torch.cat([allp[r, :, :int(counts[r])] for r in range(world)], dim=1)
+            if self.rank == 0:
+                cmask = (cv_m > float(theta)) & (ci_m >= 0)
+                d_local = torch.nonzero(cmask, as_tuple=False)[:, 0]
+                d_match = ci_m[cmask].to(torch.int64)
+                rows = torch.cat((pairs[0], d_match))
+                cols = torch.cat((pairs[1], d_local.to(torch.int64)))
+        return ShardedScanResult(rows=rows, cols=cols, stats=total, col_vals=cv_m, col_idx=ci_m, row_vals=rv,
+                                 row_idx=ri)

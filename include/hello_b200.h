@@ -39,6 +39,16 @@ enum {
 int hb_abi_version(void);
 const char* hb_last_error(void);
 
+/* Instrumentation (no counterpart in the reference, which has no kernel timers,
+ * docs/generic_scan.md:68-70).  hb_kernel_launch_count: kernels launched by this
+ * library in this process so far.  hb_set_kernel_timing(1) makes the calling
+ * thread's next calls bracket their main kernels with CUDA events;
+ * hb_last_kernel_times then returns their device times in ms (scans: pass 1,
+ * pass 2; pair costs: the pair kernel; PDHG: one iteration block average). */
+unsigned long long hb_kernel_launch_count(void);
+void hb_set_kernel_timing(int enable);
+int hb_last_kernel_times(double* ms, int capacity);
+
 /* ---------------------------------------------------------------------------
  * ℓ2² (bilinear) full-space pricing scan, bidirectional top-k + certificate.
  *
@@ -83,6 +93,17 @@ size_t hb_norm_scan_workspace(int64_t q, int64_t n, int k);
 int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
                  int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
                  int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Merge of top-k lists: for each of `rows` rows, the best k (score, index)
+ * entries over `parts` lists of `width` entries (vals/idx laid out
+ * [parts][rows][width], index -1 = empty), same order and tie rule as the scans.
+ * Replaces the cross-tile merges of the reference (generic_scan.py:131-147
+ * _merge, pricing.cu:164-180 reduce_columns, pricing_small.cu:270-277
+ * merge_raw_tile) and merges per-GPU column lists of a row-sharded scan.
+ * ------------------------------------------------------------------------- */
+int hb_merge_topk(const double* vals, const int32_t* idx, int parts, int64_t rows, int width, int k,
+                  double* out_vals, int32_t* out_idx, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Active-support pair costs (SDDMM), fp64 output in input order.

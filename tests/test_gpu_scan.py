@@ -67,8 +67,9 @@ def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0,
     ev, ei = _pad(ev, ei, k + 1)
     fv, fi = _pad(fv, fi, k + 1)
 
-    def score(r, c):
-        return oracle.pair_scores("raw", x, y, qb, dbb, a, b, r, c, dot_scale=dot_scale)[0]
+    def score(r, c, with_cost=False):
+        out = oracle.pair_scores("raw", x, y, qb, dbb, a, b, r, c, dot_scale=dot_scale)
+        return out if with_cost else out[0]
 
     def eps(r, c):
         return _bound(x, y, r, c, dot_scale, (a[r], b[c], qb[r], dbb[c]), precision)
@@ -77,9 +78,8 @@ def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0,
     check_topk(cv, ci, fv, fi, lambda r, c: score(c, r), lambda r, c: eps(c, r), min_clear=min_clear, label="cols")
     if q * n <= 4_000_000:
         rr, cc = np.divmod(np.arange(q * n), n)
-        e, s = eps(rr, cc), score(rr, cc)
-        check_stats(stats, es, float(np.sqrt(np.sum(2 * e * (np.abs(s) + e)))) + e.max(),
-                    int(np.sum(np.abs(s) <= e)), label="stats")
+        s, c = score(rr, cc, with_cost=True)
+        check_stats(stats, es, s, c, eps(rr, cc), label="stats")
     return rv, ri, cv, ci, stats
 
 
@@ -110,9 +110,10 @@ def test_l2sq_certificate_only_and_scale1(hb, cuda, oracle):
     out = hb.l2sq_scan(T(x, torch.float32), T(y, torch.float32), T(a, torch.float64), T(b, torch.float64),
                        T(f - a, torch.float64), T(g - b, torch.float64), 0, dot_scale=1.0)
     es = oracle.scan("raw", x, y, f - a, g - b, a, b, dot_scale=1.0, rk=0, ck=0)[4]
-    s = out[4].cpu().numpy()
-    np.testing.assert_allclose(s[[0, 1, 2, 3]], es[[0, 1, 2, 3]], rtol=1e-6)
-    assert abs(s[4] - es[4]) <= 1e-4 * 500 * 333
+    rr, cc = np.divmod(np.arange(500 * 333), 333)
+    s, c = oracle.pair_scores("raw", x, y, f - a, g - b, a, b, rr, cc, dot_scale=1.0)
+    e = _bound(x, y, rr, cc, 1.0, (a[rr], b[cc], (f - a)[rr], (g - b)[cc]), "fp32")
+    check_stats(out[4].cpu().numpy(), es, s, c, e, label="certificate")
 
 
 def test_l2sq_pass_symmetry(hb, cuda):

@@ -44,10 +44,8 @@ def test_l2sq_scan_oracle_matches_reference(oracle, path):
     check_topk(z["rv"], z["ri"], rv, ri, score, eps, label=path + ":rows")
     check_topk(z["cv"], z["ci"], cv, ci, lambda r, c: score(c, r), lambda r, c: eps(c, r), label=path + ":cols")
     all_r, all_c = np.divmod(np.arange(q * n), n)
-    e = eps(all_r, all_c)
-    s = score(all_r, all_c)
-    check_stats(z["stats"], stats, float(np.sqrt(np.sum((2 * e * (np.abs(s) + e)))) + e.max()),
-                int(np.sum(np.abs(s) <= e)), label=path)
+    s, c = oracle.pair_scores("raw", x, y, qb, dbb, a, b, all_r, all_c, dot_scale=2.0)
+    check_stats(z["stats"], stats, s, c, eps(all_r, all_c), label=path)
     # candidate flattening order of the reference CPU scan
     rows, cols = flatten(z["rv"], z["ri"], z["cv"], z["ci"])
     assert np.array_equal(rows, z["rows"]) and np.array_equal(cols, z["cols"])
@@ -75,10 +73,8 @@ def test_norm_scan_oracle_matches_reference(oracle, path):
             | (np.abs(s - full_c[diff[:, 1], ck - 1]) <= 2 * e)
         assert near.all(), f"{path}: {int((~near).sum())} unexplained candidate differences"
     all_r, all_c = np.divmod(np.arange(q * n), n)
-    s, _ = oracle.pair_scores(kind, x, y, f, g, None, None, all_r, all_c)
-    e = norm_error_bound(kind, x, y, all_r, all_c, f, g)
-    check_stats(z["stats"], stats, float(np.sqrt(np.sum(2 * e * (np.abs(s) + e)))) + e.max(),
-                int(np.sum(np.abs(s) <= e)), label=path)
+    s, c = oracle.pair_scores(kind, x, y, f, g, None, None, all_r, all_c)
+    check_stats(z["stats"], stats, s, c, norm_error_bound(kind, x, y, all_r, all_c, f, g), label=path)
 
 
 @pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pdlp_*.npz")))
