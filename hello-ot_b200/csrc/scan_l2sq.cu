@@ -30,7 +30,15 @@ namespace l2sq {
 
 constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192, EPI_FIRST = 64, EPI_THREADS = 128;
+constexpr int EPI_FIRST = 64;  // warps 0-1: TMA producer, MMA issuer; then EW epilogue warps
+constexpr int MAX_EW = 8;
+// Epilogue warps per CTA: 8 (two per TMEM lane quarter, each on half the
+// columns) when the row list is small enough for the register budget, else 4.
+template <int K>
+struct Epi {
+    static constexpr int EW = K <= 8 ? 8 : 4;
+    static constexpr int THREADS = EPI_FIRST + 32 * EW;
+};
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 
@@ -54,9 +62,12 @@ struct Params {
 
 struct __align__(1024) Smem {
     uint8_t stage[STAGES][STAGE_BYTES];
-    double dbias[4][BN];  // per epilogue warp: database bias of the current tile
-    double dcost[4][BN];  // per epilogue warp: database |y|^2 of the current tile
-    double red[4 * 5];
+    // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all):
+    double dbias[4 * BN];  // database bias
+    double dcost[4 * BN];  // database |y|^2
+    float fbias[4 * BN];   // fp32 copy of the bias for the screened (certificate-free) pass
+    float fmarg[4 * BN];   // 2^-21 |bias|, the bias part of the fp32 screening margin
+    double red[MAX_EW * 5];
     uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
     uint32_t tmem_base;
     int abort;
@@ -110,14 +121,79 @@ __device__ __forceinline__ void mma_issuer(const Params& p, Smem& s, uint32_t tm
     }
 }
 
-template <int K, bool STATS, bool SWAP>
+// Certificate terms computed by a pass (bit mask): score terms need the fp64
+// score of every pair, cost terms the fp64 cost.  The row pass takes the score
+// terms and the column pass the cost terms, so both passes share the fp64 work.
+enum : int { kScoreStats = 1, kCostStats = 2 };
+
+// Phase 1 of one 32-column chunk (branch-free).  FULL: all 32 columns valid for
+// the whole warp, so no per-column masking.  Returns the candidate mask.
+template <int K, int SM, bool SWAP, bool FULL>
+__device__ __forceinline__ uint32_t chunk_exact(const float (&v)[32], float scale, const double* wbias,
+                                                const double* wcost, double rbias, double rcost, int live,
+                                                double tv, bool list_open, double (&acc)[5]) {
+    constexpr bool MASKED = K > 0 && (SM & kScoreStats);  // otherwise the fp32 screen makes the mask
+    uint32_t mask = 0;
+    double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0}, mpos4[4] = {0, 0, 0, 0}, mcost4[4] = {0, 0, 0, 0};
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const bool ok = FULL || j < live;
+        const double dot = (double)(scale * v[j]);
+        if (SM & kScoreStats) {
+            const double cbias = wbias[j];
+            const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
+            if (SM & kScoreStats) {
+                const bool pos = ok && sc > 0.0;
+                num4[j & 3] = fma(sc, pos ? sc : 0.0, num4[j & 3]);
+                mpos4[j & 3] = fmax(mpos4[j & 3], FULL ? sc : (ok ? sc : 0.0));
+                cnt += pos ? 1 : 0;
+            }
+            // columns arrive in increasing index order, so a tie with a filled
+            // slot never wins; an open list admits everything (phase 2 decides)
+            if (MASKED) mask |= (ok && (sc > tv || list_open)) ? (1u << j) : 0u;
+        }
+        if (SM & kCostStats) {
+            const double co = (rcost + wcost[j]) - dot;
+            den4[j & 3] = fma(co, ok ? co : 0.0, den4[j & 3]);
+            mcost4[j & 3] = fmax(mcost4[j & 3], ok ? fabs(co) : 0.0);
+        }
+    }
+    if (SM & kScoreStats) {
+        acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
+        acc[2] = fmax(acc[2], fmax(fmax(mpos4[0], mpos4[1]), fmax(mpos4[2], mpos4[3])));
+        acc[4] += (double)cnt;
+    }
+    if (SM & kCostStats) {
+        acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
+        acc[3] = fmax(acc[3], fmax(fmax(mcost4[0], mcost4[1]), fmax(mcost4[2], mcost4[3])));
+    }
+    return mask;
+}
+
+// Epilogue.  Thread = one tile row (TMEM lane) in one column slice.  Per 32
+// columns: phase 1 is branch-free (scores, certificate terms, a mask of the
+// columns that may beat the row's k-th entry), phase 2 inserts the masked
+// columns with exact fp64 scores (rare once the list has filled).  A pass that
+// needs no fp64 score takes its mask from an fp32 screen: |fp32 score - fp64
+// score| <= 2^-23 (|dot| + |biases|) for the same dot, so adding the 2^-21 (...)
+// margin and comparing with the k-th score rounded down never drops a candidate.
+template <int K, int SM, bool SWAP>
 __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem, double (&acc)[5]) {
     constexpr int KK = K > 0 ? K : 1;
+    constexpr int EW = Epi<K>::EW;
+    constexpr int SLICES = EW / 4;
+    constexpr int SLICE = BN / SLICES;
+    constexpr bool SCREEN = !(SM & kScoreStats) && K > 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int quarter = warp & 3;          // TMEM lanes this warp may read
-    const int r = quarter * 32 + lane;     // tile row owned by this thread
-    double* wbias = s.dbias[quarter];
-    double* wcost = s.dcost[quarter];
+    const int ew = warp - EPI_FIRST / 32;
+    const int quarter = warp & 3;           // TMEM lanes this warp may read
+    const int slice = ew / 4;
+    const int r = quarter * 32 + lane;      // tile row owned by this thread
+    double* wbias = s.dbias + ew * SLICE;
+    double* wcost = s.dcost + ew * SLICE;
+    float* wfb = s.fbias + ew * SLICE;
+    float* wfm = s.fmarg + ew * SLICE;
     TopK<KK> top;
     uint32_t t = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
@@ -126,61 +202,56 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
         const int row = rb * BM + r;
         const bool rvalid = row < p.q;
         const double rbias = rvalid ? p.q_bias[row] : 0.0;
-        const double rcost = (STATS && rvalid) ? p.q_cost[row] : 0.0;
+        const double rcost = ((SM & kCostStats) && rvalid) ? p.q_cost[row] : 0.0;
+        const float rbias_f = (float)rbias;
+        const float rmarg_f = 0x1p-21f * fabsf(rbias_f);
         top.reset();
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
             const uint32_t buf = t & 1, aph = (t >> 1) & 1;
-            const int c0 = ct * BN;
-            const int ncols = min(BN, p.n - c0);
+            const int c0 = ct * BN + slice * SLICE;
+            const int ncols = min(SLICE, p.n - c0);  // may be <= 0 for the last tile's upper slice
             __syncwarp();  // the warp is done reading the previous tile's staging
-            for (int c = lane; c < BN; c += 32) {
+            for (int c = lane; c < SLICE; c += 32) {
                 const bool ok = c < ncols;
-                wbias[c] = ok ? p.d_bias[c0 + c] : 0.0;
-                if (STATS) wcost[c] = ok ? p.d_cost[c0 + c] : 0.0;
+                const double bv = ok ? p.d_bias[c0 + c] : 0.0;
+                wbias[c] = bv;
+                if (SM & kCostStats) wcost[c] = ok ? p.d_cost[c0 + c] : 0.0;
+                if (SCREEN) { wfb[c] = (float)bv; wfm[c] = 0x1p-21f * fabsf((float)bv); }
             }
             __syncwarp();
             if (!mbar_wait(&s.tfull[buf], aph, &s.abort, p.status)) return;
             tc_fence_after();
-            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + buf * BN;
-            for (int ch = 0; ch < BN / 32 && ch * 32 < ncols; ++ch) {
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + buf * BN + slice * SLICE;
+            for (int ch = 0; ch < SLICE / 32 && ch * 32 < ncols; ++ch) {
                 float v[32];
                 tmem_ld32(taddr + ch * 32, v);
                 tmem_wait_ld(v);
                 const int cb = ch * 32;
                 const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
-                // phase 1, branch-free: scores, certificate terms and a mask of the
-                // columns that beat the row's k-th entry as it stood at chunk start
                 const double tv = top.v[KK - 1];
-                const int ti = top.i[KK - 1];
+                const bool list_open = top.i[KK - 1] == INT32_MAX;
                 uint32_t mask = 0;
-                double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
-                double mpos = 0.0, mcost = 0.0;
-                int cnt = 0;
+                if (SM) {
+                    if (__all_sync(0xffffffffu, live == 32))
+                        mask = chunk_exact<K, SM, SWAP, true>(v, p.scale, wbias + cb, wcost + cb, rbias, rcost, live,
+                                                              tv, list_open, acc);
+                    else
+                        mask = chunk_exact<K, SM, SWAP, false>(v, p.scale, wbias + cb, wcost + cb, rbias, rcost, live,
+                                                               tv, list_open, acc);
+                }
+                if (SCREEN) {
+                    const float thr = list_open ? -INFINITY : __double2float_rd(tv);
+                    uint32_t sm = 0;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const bool ok = j < live;
-                    const double dot = (double)(p.scale * v[j]);
-                    const double cbias = wbias[cb + j];
-                    const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
-                    if (STATS) {
-                        const double co = (rcost + wcost[cb + j]) - dot;
-                        den4[j & 3] += ok ? co * co : 0.0;
-                        mcost = fmax(mcost, ok ? fabs(co) : 0.0);
-                        const bool pos = ok && sc > 0.0;
-                        num4[j & 3] += pos ? sc * sc : 0.0;
-                        mpos = fmax(mpos, pos ? sc : 0.0);
-                        cnt += pos ? 1 : 0;
+                    for (int j = 0; j < 32; ++j) {
+                        const float dotf = p.scale * v[j];
+                        const float sf = SWAP ? ((dotf + wfb[cb + j]) + rbias_f) : ((dotf + rbias_f) + wfb[cb + j]);
+                        const float m = fmaf(fabsf(dotf), 0x1p-21f, wfm[cb + j] + rmarg_f);
+                        sm |= (j < live && sf + m >= thr) ? (1u << j) : 0u;
                     }
-                    if (K > 0) mask |= (ok && better(sc, c0 + cb + j, tv, ti)) ? (1u << j) : 0u;
+                    mask = sm;
                 }
-                if (STATS) {
-                    acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
-                    acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
-                    acc[2] = fmax(acc[2], mpos);
-                    acc[3] = fmax(acc[3], mcost);
-                    acc[4] += (double)cnt;
-                }
-                // phase 2 (rare once the list has filled): insert the masked columns
+                // phase 2: exact fp64 scores of the masked columns into the row list
                 while (K > 0 && mask) {
                     const int j = __ffs(mask) - 1;
                     mask &= mask - 1;
@@ -197,22 +268,24 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
             mbar_arrive(&s.tempty[buf]);
         }
         if (K > 0 && rvalid) {
-            double* pv = p.part_v + ((int64_t)g * p.q + row) * KK;
-            int* pi = p.part_i + ((int64_t)g * p.q + row) * KK;
+            const int part = g * SLICES + slice;
+            double* pv = p.part_v + ((int64_t)part * p.q + row) * KK;
+            int* pi = p.part_i + ((int64_t)part * p.q + row) * KK;
 #pragma unroll
             for (int j = 0; j < KK; ++j) { pv[j] = top.v[j]; pi[j] = top.i[j]; }
         }
     }
 }
 
-template <int K, bool STATS, bool SWAP>
-__global__ void __launch_bounds__(THREADS, 1) scan_kernel(const __grid_constant__ Params p) {
+template <int K, int SM, bool SWAP>
+__global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_constant__ Params p) {
+    constexpr int EW = Epi<K>::EW;
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], EPI_THREADS); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], 32 * EW); }
         s.abort = 0;
         fence_barrier_init();
     }
@@ -231,8 +304,8 @@ __global__ void __launch_bounds__(THREADS, 1) scan_kernel(const __grid_constant_
         if (lane == 0) mma_issuer(p, s, tmem);
     } else {
         double acc[5] = {0, 0, 0, 0, 0};
-        epilogue<K, STATS, SWAP>(p, s, tmem, acc);
-        if (STATS) {  // warp totals in a fixed shuffle order
+        epilogue<K, SM, SWAP>(p, s, tmem, acc);
+        if (SM) {  // warp totals in a fixed shuffle order
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) {
                 const double o0 = __shfl_down_sync(0xffffffffu, acc[0], off);
@@ -243,7 +316,7 @@ __global__ void __launch_bounds__(THREADS, 1) scan_kernel(const __grid_constant_
                 acc[0] += o0; acc[1] += o1; acc[2] = fmax(acc[2], o2); acc[3] = fmax(acc[3], o3); acc[4] += o4;
             }
             if (lane == 0)
-                for (int j = 0; j < 5; ++j) s.red[(warp & 3) * 5 + j] = acc[j];
+                for (int j = 0; j < 5; ++j) s.red[(warp - EPI_FIRST / 32) * 5 + j] = acc[j];
         }
     }
     tc_fence_before();
@@ -252,9 +325,9 @@ __global__ void __launch_bounds__(THREADS, 1) scan_kernel(const __grid_constant_
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
-    if (STATS && threadIdx.x == EPI_FIRST) {
+    if (SM && threadIdx.x == EPI_FIRST) {
         double a[5] = {0, 0, 0, 0, 0};
-        for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < EW; ++w) {
             a[0] += s.red[w * 5 + 0]; a[1] += s.red[w * 5 + 1];
             a[2] = fmax(a[2], s.red[w * 5 + 2]); a[3] = fmax(a[3], s.red[w * 5 + 3]);
             a[4] += s.red[w * 5 + 4];
@@ -314,9 +387,9 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int dp, int box_r
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int K, bool STATS, bool SWAP>
+template <int K, int SM, bool SWAP>
 cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
-    auto fn = l2sq::scan_kernel<K, STATS, SWAP>;
+    auto fn = l2sq::scan_kernel<K, SM, SWAP>;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)l2sq::SMEM_BYTES);
@@ -324,22 +397,21 @@ cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
         configured = true;
     }
     timing_mark(st);
-    fn<<<grid, l2sq::THREADS, l2sq::SMEM_BYTES, st>>>(p);
+    fn<<<grid, l2sq::Epi<K>::THREADS, l2sq::SMEM_BYTES, st>>>(p);
     timing_mark(st);
     count_launches(1);
     return cudaGetLastError();
 }
 
-template <bool STATS, bool SWAP>
+template <int SM, bool SWAP>
 cudaError_t launch_k(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
     switch (K) {
-        case 0: return launch_pass<0, STATS, SWAP>(p, grid, st);
-        case 1: return launch_pass<1, STATS, SWAP>(p, grid, st);
-        case 2: return launch_pass<2, STATS, SWAP>(p, grid, st);
-        case 4: return launch_pass<4, STATS, SWAP>(p, grid, st);
-        case 8: return launch_pass<8, STATS, SWAP>(p, grid, st);
-        case 16: return launch_pass<16, STATS, SWAP>(p, grid, st);
-        case 32: return launch_pass<32, STATS, SWAP>(p, grid, st);
+        case 1: return launch_pass<1, SM, SWAP>(p, grid, st);
+        case 2: return launch_pass<2, SM, SWAP>(p, grid, st);
+        case 4: return launch_pass<4, SM, SWAP>(p, grid, st);
+        case 8: return launch_pass<8, SM, SWAP>(p, grid, st);
+        case 16: return launch_pass<16, SM, SWAP>(p, grid, st);
+        case 32: return launch_pass<32, SM, SWAP>(p, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -379,6 +451,9 @@ cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64
     }
 }
 
+// Column slices per tile (= row partial lists per unit) of the bucket-K kernel.
+inline int l2sq_slices(int K) { return (K <= 8 ? 8 : 4) / 4; }
+
 // Scratch layout of one ℓ2² scan call.  With base == nullptr only sizes it.
 struct L2sqLayout {
     float *xpad = nullptr, *ypad = nullptr, *xlo = nullptr, *ylo = nullptr;
@@ -410,11 +485,12 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     const int wide = (int)(d / 1024) + 1;
     L.p1 = scan_plan(q, n, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
     L.p2 = scan_plan(n, q, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
-    need(K > 0, L.pv1, (size_t)L.p1.groups * q * K);
-    need(K > 0, L.pi1, (size_t)L.p1.groups * q * K);
-    need(K > 0, L.pv2, (size_t)L.p2.groups * n * K);
-    need(K > 0, L.pi2, (size_t)L.p2.groups * n * K);
-    need(true, L.cta, (size_t)(L.p1.grid > L.p2.grid ? L.p1.grid : L.p2.grid) * 5);
+    const int slices = K > 0 ? l2sq_slices(K) : 1;
+    need(K > 0, L.pv1, (size_t)L.p1.groups * slices * q * K);
+    need(K > 0, L.pi1, (size_t)L.p1.groups * slices * q * K);
+    need(K > 0, L.pv2, (size_t)L.p2.groups * slices * n * K);
+    need(K > 0, L.pi2, (size_t)L.p2.groups * slices * n * K);
+    need(true, L.cta, (size_t)(L.p1.grid + L.p2.grid) * 5);
     need(true, L.status, 1);
     L.bytes = ar.used + 256;
     return L;
@@ -462,14 +538,13 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
     p.q_cost = nx; p.d_cost = ny; p.q_bias = qb; p.d_bias = dbb;
     p.part_v = L.pv1; p.part_i = L.pi1;
-    e = want_stats ? launch_k<true, false>(K, p, L.p1.grid, st) : launch_k<false, false>(K, p, L.p1.grid, st);
+    // certificate: score terms in the row pass, cost terms in the column pass
+    // (a certificate-only call has no column pass and takes all terms here)
+    if (K == 0) e = launch_pass<0, l2sq::kScoreStats | l2sq::kCostStats, false>(p, L.p1.grid, st);
+    else e = want_stats ? launch_k<l2sq::kScoreStats, false>(K, p, L.p1.grid, st) : launch_k<0, false>(K, p, L.p1.grid, st);
     if (e != cudaSuccess) { err = std::string("l2sq pass 1: ") + cudaGetErrorString(e); return 6; }
-    if (want_stats) {
-        finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5);
-        count_launches(1);
-    }
     if (K > 0) {
-        e = merge_any(K, L.pv1, L.pi1, L.p1.groups, q, k, rv, ri, st);
+        e = merge_any(K, L.pv1, L.pi1, L.p1.groups * l2sq_slices(K), q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
         // pass 2: y rows are the queries, same products in the same order
         // pass 2: y rows are the queries, same products in the same order;
@@ -486,10 +561,15 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
         p2.q_cost = ny; p2.d_cost = nx; p2.q_bias = dbb; p2.d_bias = qb;
         p2.part_v = L.pv2; p2.part_i = L.pi2;
-        e = launch_k<false, true>(K, p2, L.p2.grid, st);
+        p2.cta_stats = L.cta + (size_t)L.p1.grid * 5;
+        e = want_stats ? launch_k<l2sq::kCostStats, true>(K, p2, L.p2.grid, st) : launch_k<0, true>(K, p2, L.p2.grid, st);
         if (e != cudaSuccess) { err = std::string("l2sq pass 2: ") + cudaGetErrorString(e); return 6; }
-        e = merge_any(K, L.pv2, L.pi2, L.p2.groups, n, k, cv, ci, st);
+        e = merge_any(K, L.pv2, L.pi2, L.p2.groups * l2sq_slices(K), n, k, cv, ci, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+    }
+    if (want_stats) {  // per-CTA partials of both passes, unused terms are zero
+        finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid + (K > 0 ? L.p2.grid : 0), stats5);
+        count_launches(1);
     }
     if (status_out) cudaMemcpyAsync(status_out, L.status, sizeof(int), cudaMemcpyDeviceToHost, st);
     return 0;
