@@ -64,9 +64,9 @@ struct __align__(1024) Smem {
     uint8_t stage[STAGES][STAGE_BYTES];
     // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all):
     double dbias[4 * BN];  // database bias
-    double dcost[4 * BN];  // database |y|^2
-    float fbias[4 * BN];   // fp32 copy of the bias for the screened (certificate-free) pass
+    float fbias[4 * BN];   // fp32 copy of the bias
     float fmarg[4 * BN];   // 2^-21 |bias|, the bias part of the fp32 screening margin
+    float fcost[4 * BN];   // fp32 copy of |y|^2
     double red[MAX_EW * 5];
     uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
     uint32_t tmem_base;
@@ -121,79 +121,79 @@ __device__ __forceinline__ void mma_issuer(const Params& p, Smem& s, uint32_t tm
     }
 }
 
-// Certificate terms computed by a pass (bit mask): score terms need the fp64
-// score of every pair, cost terms the fp64 cost.  The row pass takes the score
-// terms and the column pass the cost terms, so both passes share the fp64 work.
+// Certificate terms computed by a pass (bit mask): score terms (sum s+^2,
+// max s+, count) and cost terms (sum c^2, max |c|).  The row pass takes the
+// score terms and the column pass the cost terms.
 enum : int { kScoreStats = 1, kCostStats = 2 };
 
-// Phase 1 of one 32-column chunk (branch-free).  FULL: all 32 columns valid for
-// the whole warp, so no per-column masking.  Returns the candidate mask.
+// Phase 1 of one 32-column chunk, branch-free and in fp32: fp32 score / cost
+// of every pair (within 2^-22 (|dot| + |a| + |b| + |biases|) of the fp64
+// values for the same dot), certificate partials (fp32 over 8 terms, then
+// fp64), and the candidate mask: columns whose fp32 score plus the rounding
+// margin 2^-21 (|dot| + |biases|) reaches the row's k-th score rounded down.
+// FULL: all 32 columns are valid for the whole warp (no per-column masking).
 template <int K, int SM, bool SWAP, bool FULL>
-__device__ __forceinline__ uint32_t chunk_exact(const float (&v)[32], float scale, const double* wbias,
-                                                const double* wcost, double rbias, double rcost, int live,
-                                                double tv, bool list_open, double (&acc)[5]) {
-    constexpr bool MASKED = K > 0 && (SM & kScoreStats);  // otherwise the fp32 screen makes the mask
+__device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float scale, const float* fb, const float* fm,
+                                                 const float* fc, float rbias_f, float rmarg_f, float rcost_f, int live,
+                                                 float thr, double (&acc)[5]) {
     uint32_t mask = 0;
-    double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0}, mpos4[4] = {0, 0, 0, 0}, mcost4[4] = {0, 0, 0, 0};
+    float num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
+    float mpos = 0.0f, mcost = 0.0f;
     int cnt = 0;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const bool ok = FULL || j < live;
-        const double dot = (double)(scale * v[j]);
-        if (SM & kScoreStats) {
-            const double cbias = wbias[j];
-            const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
+        const float dotf = scale * v[j];
+        if (K > 0 || (SM & kScoreStats)) {
+            const float sf = SWAP ? ((dotf + fb[j]) + rbias_f) : ((dotf + rbias_f) + fb[j]);
             if (SM & kScoreStats) {
-                const bool pos = ok && sc > 0.0;
-                num4[j & 3] = fma(sc, pos ? sc : 0.0, num4[j & 3]);
-                mpos4[j & 3] = fmax(mpos4[j & 3], FULL ? sc : (ok ? sc : 0.0));
+                const bool pos = ok && sf > 0.0f;
+                num4[j & 3] = fmaf(sf, pos ? sf : 0.0f, num4[j & 3]);
+                mpos = fmaxf(mpos, FULL ? sf : (ok ? sf : 0.0f));
                 cnt += pos ? 1 : 0;
             }
-            // columns arrive in increasing index order, so a tie with a filled
-            // slot never wins; an open list admits everything (phase 2 decides)
-            if (MASKED) mask |= (ok && (sc > tv || list_open)) ? (1u << j) : 0u;
+            if (K > 0) {
+                const float m = fmaf(fabsf(dotf), 0x1p-21f, fm[j] + rmarg_f);
+                mask |= (ok && sf + m >= thr) ? (1u << j) : 0u;
+            }
         }
         if (SM & kCostStats) {
-            const double co = (rcost + wcost[j]) - dot;
-            den4[j & 3] = fma(co, ok ? co : 0.0, den4[j & 3]);
-            mcost4[j & 3] = fmax(mcost4[j & 3], ok ? fabs(co) : 0.0);
+            const float cf = (rcost_f + fc[j]) - dotf;
+            den4[j & 3] = fmaf(cf, ok ? cf : 0.0f, den4[j & 3]);
+            mcost = fmaxf(mcost, ok ? fabsf(cf) : 0.0f);
         }
     }
     if (SM & kScoreStats) {
-        acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
-        acc[2] = fmax(acc[2], fmax(fmax(mpos4[0], mpos4[1]), fmax(mpos4[2], mpos4[3])));
+        acc[0] += ((double)num4[0] + (double)num4[1]) + ((double)num4[2] + (double)num4[3]);
+        acc[2] = fmax(acc[2], (double)mpos);
         acc[4] += (double)cnt;
     }
     if (SM & kCostStats) {
-        acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
-        acc[3] = fmax(acc[3], fmax(fmax(mcost4[0], mcost4[1]), fmax(mcost4[2], mcost4[3])));
+        acc[1] += ((double)den4[0] + (double)den4[1]) + ((double)den4[2] + (double)den4[3]);
+        acc[3] = fmax(acc[3], (double)mcost);
     }
     return mask;
 }
 
 // Epilogue.  Thread = one tile row (TMEM lane) in one column slice.  Per 32
-// columns: phase 1 is branch-free (scores, certificate terms, a mask of the
-// columns that may beat the row's k-th entry), phase 2 inserts the masked
-// columns with exact fp64 scores (rare once the list has filled).  A pass that
-// needs no fp64 score takes its mask from an fp32 screen: |fp32 score - fp64
-// score| <= 2^-23 (|dot| + |biases|) for the same dot, so adding the 2^-21 (...)
-// margin and comparing with the k-th score rounded down never drops a candidate.
+// columns: phase 1 (above), then phase 2 inserts the masked columns into the
+// row's k-list with exact fp64 scores (rare once the list has filled), so
+// reported scores follow the reference arithmetic (dot + qb) + dbb in fp64.
 template <int K, int SM, bool SWAP>
 __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem, double (&acc)[5]) {
     constexpr int KK = K > 0 ? K : 1;
     constexpr int EW = Epi<K>::EW;
     constexpr int SLICES = EW / 4;
     constexpr int SLICE = BN / SLICES;
-    constexpr bool SCREEN = !(SM & kScoreStats) && K > 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ew = warp - EPI_FIRST / 32;
     const int quarter = warp & 3;           // TMEM lanes this warp may read
     const int slice = ew / 4;
     const int r = quarter * 32 + lane;      // tile row owned by this thread
     double* wbias = s.dbias + ew * SLICE;
-    double* wcost = s.dcost + ew * SLICE;
     float* wfb = s.fbias + ew * SLICE;
     float* wfm = s.fmarg + ew * SLICE;
+    float* wfc = s.fcost + ew * SLICE;
     TopK<KK> top;
     uint32_t t = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
@@ -202,9 +202,9 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
         const int row = rb * BM + r;
         const bool rvalid = row < p.q;
         const double rbias = rvalid ? p.q_bias[row] : 0.0;
-        const double rcost = ((SM & kCostStats) && rvalid) ? p.q_cost[row] : 0.0;
         const float rbias_f = (float)rbias;
         const float rmarg_f = 0x1p-21f * fabsf(rbias_f);
+        const float rcost_f = ((SM & kCostStats) && rvalid) ? (float)p.q_cost[row] : 0.0f;
         top.reset();
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
             const uint32_t buf = t & 1, aph = (t >> 1) & 1;
@@ -215,8 +215,9 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
                 const bool ok = c < ncols;
                 const double bv = ok ? p.d_bias[c0 + c] : 0.0;
                 wbias[c] = bv;
-                if (SM & kCostStats) wcost[c] = ok ? p.d_cost[c0 + c] : 0.0;
-                if (SCREEN) { wfb[c] = (float)bv; wfm[c] = 0x1p-21f * fabsf((float)bv); }
+                wfb[c] = (float)bv;
+                wfm[c] = 0x1p-21f * fabsf((float)bv);
+                if (SM & kCostStats) wfc[c] = ok ? (float)p.d_cost[c0 + c] : 0.0f;
             }
             __syncwarp();
             if (!mbar_wait(&s.tfull[buf], aph, &s.abort, p.status)) return;
@@ -228,29 +229,14 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
                 tmem_wait_ld(v);
                 const int cb = ch * 32;
                 const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
-                const double tv = top.v[KK - 1];
-                const bool list_open = top.i[KK - 1] == INT32_MAX;
-                uint32_t mask = 0;
-                if (SM) {
-                    if (__all_sync(0xffffffffu, live == 32))
-                        mask = chunk_exact<K, SM, SWAP, true>(v, p.scale, wbias + cb, wcost + cb, rbias, rcost, live,
-                                                              tv, list_open, acc);
-                    else
-                        mask = chunk_exact<K, SM, SWAP, false>(v, p.scale, wbias + cb, wcost + cb, rbias, rcost, live,
-                                                               tv, list_open, acc);
-                }
-                if (SCREEN) {
-                    const float thr = list_open ? -INFINITY : __double2float_rd(tv);
-                    uint32_t sm = 0;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float dotf = p.scale * v[j];
-                        const float sf = SWAP ? ((dotf + wfb[cb + j]) + rbias_f) : ((dotf + rbias_f) + wfb[cb + j]);
-                        const float m = fmaf(fabsf(dotf), 0x1p-21f, wfm[cb + j] + rmarg_f);
-                        sm |= (j < live && sf + m >= thr) ? (1u << j) : 0u;
-                    }
-                    mask = sm;
-                }
+                const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY : __double2float_rd(top.v[KK - 1]);
+                uint32_t mask;
+                if (__all_sync(0xffffffffu, live == 32))
+                    mask = chunk_phase1<K, SM, SWAP, true>(v, p.scale, wfb + cb, wfm + cb, wfc + cb, rbias_f, rmarg_f,
+                                                           rcost_f, live, thr, acc);
+                else
+                    mask = chunk_phase1<K, SM, SWAP, false>(v, p.scale, wfb + cb, wfm + cb, wfc + cb, rbias_f,
+                                                            rmarg_f, rcost_f, live, thr, acc);
                 // phase 2: exact fp64 scores of the masked columns into the row list
                 while (K > 0 && mask) {
                     const int j = __ffs(mask) - 1;

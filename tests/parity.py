@@ -106,19 +106,22 @@ def flatten(rv, ri, cv, ci, theta=0.0):
     return rows, cols
 
 
-def check_stats(test, exact, score, cost, eps, label=""):
-    """test/exact: [num, den, max_pos, max_abs_cost, count]; score/cost/eps: exact
-    fp64 score, exact cost and error bound of every pair.  Each sum may move by at
-    most the sum of its terms' bounds; the count by the pairs within eps of 0."""
+def check_stats(test, exact, score, cost, eps, eps_cost=None, rel=0.0, label=""):
+    """test/exact: [num, den, max_pos, max_abs_cost, count]; score/cost: exact fp64
+    score and cost of every pair; eps / eps_cost: per-pair error bounds of the
+    score / cost as the implementation under test evaluates them; rel: relative
+    rounding of its partial sums.  Each sum may move by the sum of its terms'
+    bounds, the count by the pairs within eps of 0."""
     test = np.asarray(test, np.float64)
     exact = np.asarray(exact, np.float64)
     s, c, e = (np.asarray(v, np.float64) for v in (score, cost, eps))
+    ec = e if eps_cost is None else np.asarray(eps_cost, np.float64)
     tiny = 1e-12 * (1 + abs(exact[1]))
     pos = s > -e
-    num_tol = float(np.sum((2 * np.abs(s) * e + e * e)[pos])) + tiny
-    den_tol = float(np.sum(2 * np.abs(c) * e + e * e)) + 1e-12 * exact[1] + tiny
+    num_tol = float(np.sum((2 * np.abs(s) * e + e * e)[pos])) + rel * float(np.sum(np.maximum(s, 0) ** 2)) + tiny
+    den_tol = float(np.sum(2 * np.abs(c) * ec + ec * ec)) + rel * exact[1] + 1e-12 * exact[1] + tiny
     assert abs(test[1] - exact[1]) <= den_tol, f"{label}: den {test[1]} vs {exact[1]} (tol {den_tol})"
     assert abs(test[0] - exact[0]) <= num_tol, f"{label}: num {test[0]} vs {exact[0]} (tol {num_tol})"
     assert abs(test[2] - exact[2]) <= e.max() + tiny, f"{label}: max+ {test[2]} vs {exact[2]}"
-    assert abs(test[3] - exact[3]) <= e.max() + tiny, f"{label}: max|c| {test[3]} vs {exact[3]}"
+    assert abs(test[3] - exact[3]) <= ec.max() + tiny, f"{label}: max|c| {test[3]} vs {exact[3]}"
     assert abs(test[4] - exact[4]) <= int(np.sum(np.abs(s) <= e)), f"{label}: count {test[4]} vs {exact[4]}"

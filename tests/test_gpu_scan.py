@@ -47,6 +47,18 @@ def _bound(x, y, r, c, scale, biases, precision):
     return scale * (prod + 2 * (d + 2) * U32) * absdot + 16 * 2.0 ** -53 * mag
 
 
+def _cert_bounds(x, y, r, c, scale, a, b, qb, dbb, precision):
+    """Error bounds of the certificate terms: the kernel evaluates scores and
+    costs in fp32 from the tensor-core dot (2^-22 of the magnitudes it adds)."""
+    x64, y64 = np.asarray(x, np.float64), np.asarray(y, np.float64)
+    e = _bound(x, y, r, c, scale, (a[r], b[c], qb[r], dbb[c]), precision)
+    dot = scale * np.abs(np.einsum("ij,ij->i", x64[r], y64[c]))
+    return e + 2.0 ** -22 * (dot + np.abs(qb[r]) + np.abs(dbb[c])), e + 2.0 ** -22 * (dot + np.abs(a[r]) + np.abs(b[c]))
+
+
+CERT_REL = 2.0 ** -20  # fp32 partial sums over 8 terms
+
+
 def _pad(v, i, width):
     if v.shape[1] < width:
         v = np.pad(v, ((0, 0), (0, width - v.shape[1])), constant_values=-np.inf)
@@ -79,7 +91,8 @@ def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0,
     if q * n <= 4_000_000:
         rr, cc = np.divmod(np.arange(q * n), n)
         s, c = score(rr, cc, with_cost=True)
-        check_stats(stats, es, s, c, eps(rr, cc), label="stats")
+        es_, ec_ = _cert_bounds(x, y, rr, cc, dot_scale, a, b, qb, dbb, precision)
+        check_stats(stats, es, s, c, es_, ec_, rel=CERT_REL, label="stats")
     return rv, ri, cv, ci, stats
 
 
@@ -112,8 +125,8 @@ def test_l2sq_certificate_only_and_scale1(hb, cuda, oracle):
     es = oracle.scan("raw", x, y, f - a, g - b, a, b, dot_scale=1.0, rk=0, ck=0)[4]
     rr, cc = np.divmod(np.arange(500 * 333), 333)
     s, c = oracle.pair_scores("raw", x, y, f - a, g - b, a, b, rr, cc, dot_scale=1.0)
-    e = _bound(x, y, rr, cc, 1.0, (a[rr], b[cc], (f - a)[rr], (g - b)[cc]), "fp32")
-    check_stats(out[4].cpu().numpy(), es, s, c, e, label="certificate")
+    es_, ec_ = _cert_bounds(x, y, rr, cc, 1.0, a, b, f - a, g - b, "fp32")
+    check_stats(out[4].cpu().numpy(), es, s, c, es_, ec_, rel=CERT_REL, label="certificate")
 
 
 def test_l2sq_pass_symmetry(hb, cuda):
