@@ -65,6 +65,8 @@ bool valid_k(int k) { return k >= 0 && k <= 32; }
 }  // namespace
 
 namespace hb {
+int abi_fail(int code, const std::string& msg) { return fail(code, msg); }
+int abi_finish(cudaStream_t st, const char* what) { return finish(st, nullptr, what); }
 void count_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 void timing_mark(cudaStream_t st) {
     Timing& t = g_timing;

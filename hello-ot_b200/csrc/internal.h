@@ -10,6 +10,11 @@ namespace hb {
 // Instrumentation: a process-wide count of kernel launches issued by this
 // library, and optional CUDA-event timing of the main kernels of a call.
 void count_launches(int n);
+// Error reporting of the C ABI for entry points defined outside abi.cu:
+// abi_fail records the message for hb_last_error and returns code;
+// abi_finish synchronises the stream and maps a CUDA error to HB_CUDA.
+int abi_fail(int code, const std::string& msg);
+int abi_finish(cudaStream_t st, const char* what);
 void timing_mark(cudaStream_t st);  // no-op unless timing is enabled on this thread
 
 // ℓ2² scan (scan_l2sq.cu)

@@ -14,8 +14,10 @@
 // register block from k-major shared-memory slabs; the distance tile is then
 // handed through shared memory to a row-per-thread epilogue (two threads per
 // row, one per half of the columns) that keeps the row top-k in registers.
+#include <mutex>
 #include <string>
 
+#include "../../include/hello_b200.h"
 #include "common.cuh"
 #include "internal.h"
 #include "scan_common.cuh"
@@ -317,3 +319,65 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
 }
 
 }  // namespace hb
+
+// ---------------------------------------------------------------------------
+// Allocation-free norm scan.  The scratch (partial top-k lists and per-CTA
+// certificate partials) lives in this file-scope device array instead of a
+// caller-provided workspace; every GPU that loads the library holds it until
+// the process exits.  In host code `g_norm_scratch` is only a host-side stand-in
+// for the symbol, so its device address is looked up once per device (with that
+// device current) and passed to the kernels.
+static __device__ __align__(256) unsigned char g_norm_scratch[HB_NORM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_norm_scratch_mutex;
+void* g_norm_scratch_ptr[256] = {};
+
+// Device address of g_norm_scratch on the current device (looked up on first use).
+cudaError_t norm_scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 256) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_norm_scratch_mutex);
+    if (!g_norm_scratch_ptr[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_norm_scratch);
+        if (e != cudaSuccess) return e;
+        g_norm_scratch_ptr[dev] = ptr;
+    }
+    *out = g_norm_scratch_ptr[dev];
+    return cudaSuccess;
+}
+}  // namespace
+
+extern "C" int hb_norm_scan_noalloc(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f,
+                                    const double* g, int cost_type, int k, int compute_stats, double* row_vals,
+                                    int32_t* row_idx, double* col_vals, int32_t* col_idx, double* stats5,
+                                    void* stream) {
+    using namespace hb;
+    if (!x || !y || !f || !g) return abi_fail(HB_BAD_ARGUMENT, "null input pointer");
+    if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
+        return abi_fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
+    if (cost_type < 0 || cost_type > 2) return abi_fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2)");
+    if (k < 0 || k > 32) return abi_fail(HB_BAD_ARGUMENT, "k must be in 0..32");
+    if (k > 0 && (!row_vals || !row_idx || !col_vals || !col_idx)) return abi_fail(HB_BAD_ARGUMENT, "null output pointer");
+    if (compute_stats && !stats5) return abi_fail(HB_BAD_ARGUMENT, "null stats pointer");
+    const size_t need = norm_bytes(q, n, k);
+    if (need > (size_t)HB_NORM_NOALLOC_SCRATCH_BYTES)
+        return abi_fail(HB_WORKSPACE, "hb_norm_scan_noalloc: this problem needs " + std::to_string(need) +
+                                          " bytes of scratch but the static buffer holds " +
+                                          std::to_string((size_t)HB_NORM_NOALLOC_SCRATCH_BYTES) +
+                                          "; use hb_norm_scan with a workspace");
+    void* scratch = nullptr;
+    cudaError_t e = norm_scratch_address(&scratch);
+    if (e != cudaSuccess)
+        return abi_fail(HB_CUDA, std::string("hb_norm_scan_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::string err;
+    int rc = norm_scan(x, y, q, n, d, f, g, cost_type, k, compute_stats, row_vals, row_idx, col_vals, col_idx, stats5,
+                       scratch, (size_t)HB_NORM_NOALLOC_SCRATCH_BYTES, st, err);
+    if (rc) return abi_fail(rc == 3 ? HB_WORKSPACE : HB_LAUNCH, err);
+    return abi_finish(st, "norm scan (no alloc)");
+}
+

@@ -95,6 +95,29 @@ int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
                  int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Allocation-free variant of hb_norm_scan (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory themselves: a host runtime
+ * reached through an FFI that has no CUDA allocator binding, a caller running
+ * under a fixed memory budget that forbids new device allocations, or one that
+ * must not grow the process footprint in the middle of a solve.  It takes no
+ * workspace: its scratch is a static device array of
+ * HB_NORM_NOALLOC_SCRATCH_BYTES inside libhello_b200.so, which every GPU that
+ * loads the library holds until the process exits.  Problems whose scratch
+ * (hb_norm_scan_workspace(q, n, k)) exceeds that size are rejected with
+ * HB_WORKSPACE and a message; use hb_norm_scan for them.  It calls no
+ * cudaMalloc/cudaFree or other allocating routine.  The first call on a device
+ * looks up the array's device address and should come before any stream
+ * capture.  All calls on a device share the one array, so calls that overlap
+ * on the GPU (other streams, other host threads) race; serialise them.
+ * Arguments and results as hb_norm_scan; the stream is synchronised.
+ * ------------------------------------------------------------------------- */
+#define HB_NORM_NOALLOC_SCRATCH_BYTES (16u << 20)
+int hb_norm_scan_noalloc(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f,
+                         const double* g, int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx,
+                         double* col_vals, int32_t* col_idx, double* stats5, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Merge of top-k lists: for each of `rows` rows, the best k (score, index)
  * entries over `parts` lists of `width` entries (vals/idx laid out
  * [parts][rows][width], index -1 = empty), same order and tie rule as the scans.
