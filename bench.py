@@ -56,6 +56,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp"],
+                   help="scan (default, the headline): l2sq pricing scan; norm: l1 scan (config 3 shape); "
+                        "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
     p.add_argument("--n", type=int, default=1_048_576)
     p.add_argument("--d", type=int, default=256)
@@ -405,9 +408,172 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ other rows of the path
+def _line(args, metric, value, unit, sec, config, extra):
+    out = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "data": "synthetic (seeded)", "config": config}
+    out.update(extra)
+    print(json.dumps(out))
+
+
+def _timed(fn, args, dev):
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        fn()
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    return ev0.elapsed_time(ev1) / 1e3 / args.steps
+
+
+def support_problem(n, m, beta, seed):
+    """A feasible restricted-OT support: each source and target gets edges, about
+    beta (n + m) edges in all (the reference's support budget factor, 10 by default)."""
+    rng = np.random.default_rng(seed)
+    e_rand = int(beta * (n + m)) - n - m
+    rows = np.concatenate([np.arange(n), rng.integers(0, n, m), rng.integers(0, n, e_rand)])
+    cols = np.concatenate([rng.integers(0, m, n), np.arange(m), rng.integers(0, m, e_rand)])
+    key = np.unique(rows.astype(np.int64) * m + cols)
+    rows, cols = key // m, key % m
+    perm = rng.permutation(rows.size)
+    cost = rng.random(rows.size) * 4.0
+    return rows[perm], cols[perm], cost[perm], np.full(n, 1.0 / n), np.full(m, 1.0 / m)
+
+
+def run_pdlp(args, hb, dev, peaks):
+    """Restricted-OT PDHG: a step is `iters` iterations (evaluation every 200) on a
+    support of 10 (n + m) edges; metric iterations/s; roofline HBM bytes/iteration."""
+    n = m = args.n
+    iters = 1000
+    rows, cols, cost, a, b = support_problem(n, m, 10.0, 42)
+    e = rows.size
+    R, C, W = (torch.as_tensor(v, device=dev) for v in (rows, cols, cost))
+    A, B = torch.as_tensor(a, device=dev), torch.as_tensor(b, device=dev)
+    solver = hb.NativeRestrictedOTPDLP(device=dev, evaluation_frequency=200, iteration_limit=iters)
+    hb.set_kernel_timing(True)
+    sec = _timed(lambda: solver.solve_restricted(rows=R, cols=C, costs=W, source_mass=A, target_mass=B, tolerance=0.0),
+                 args, dev)
+    block_ms = hb.last_kernel_times()
+    hb.set_kernel_timing(False)
+    per_iter = (block_ms[0] / 200 / 1e3) if block_ms else sec / iters
+    bytes_iter = 44 * e + 32 * (n + m)
+    achieved = bytes_iter / per_iter / 1e9
+    extra = {"dtype": "f64", "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                                          "kernel": "hb::pdlp::source_pass + target_pass (one iteration)",
+                                          "bytes_per_iteration": bytes_iter}}
+    if not args.no_cpu:
+        import oracle
+        lp = oracle.load_ref("lp")
+        threads = os.cpu_count() or 1
+        cpu_iters = 40
+        masses = np.concatenate((a, b))
+        t0 = time.perf_counter()
+        lp.solve_once(rows, cols, cost, masses, np.zeros(e), np.zeros(n + m), n, threads, 200, 3600.0, cpu_iters,
+                      0.0, 0.0, 0.0, False, False)
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": cpu_iters / dt, "unit": "iterations/s", "cores": threads,
+                                 "kind": "reference", "sample": f"{cpu_iters} iterations of the reference C++ "
+                                                                 f"solve_once (solver.cpp) on the same support"}
+    _line(args, "restricted-OT PDHG iterations/s", iters / sec, "iterations/s", sec,
+          {"workload": f"restricted OT, n=m={n}, E={e} (10 (n+m)), {iters} iterations per step", "n": n, "m": m,
+           "edges": e}, extra)
+
+
+def run_pairs(args, hb, dev, peaks):
+    """Active-support pair costs: a step evaluates E = 8 (n + m) candidate edges
+    (k = 8 per row and column) of an n x n, d-dim problem; metric Gedges/s."""
+    n, d = args.n, args.d
+    e = 8 * 2 * n
+    g = torch.Generator(device=dev)
+    g.manual_seed(42)
+    x = torch.randn(n, d, device=dev, generator=g)
+    y = torch.randn(n, d, device=dev, generator=g)
+    a, b = (x.double() ** 2).sum(1), (y.double() ** 2).sum(1)
+    rows = torch.randint(0, n, (e,), device=dev, generator=g)
+    cols = torch.randint(0, n, (e,), device=dev, generator=g)
+    hb.set_kernel_timing(True)
+    sec = _timed(lambda: hb.pair_costs(3, x, y, rows, cols, a, b, 2.0), args, dev)
+    kms = hb.last_kernel_times()
+    hb.set_kernel_timing(False)
+    bytes_call = e * (8 + 8 + 8 + 2 * 4 * d + 16)
+    achieved = bytes_call / (kms[0] / 1e3) / 1e9 if kms else bytes_call / sec / 1e9
+    extra = {"dtype": "f32 in, f64 accumulate", "roofline": {
+        "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "hb::pairs::pair_kernel<3,...>",
+        "bytes_per_edge": bytes_call / e}}
+    if not args.no_cpu:  # the reference's CPU branch: a[r] + b[c] - s * einsum (pairs.py:296-307)
+        xs, ys = x.cpu().numpy(), y.cpu().numpy()
+        asub, bsub = a.cpu().numpy().astype(np.float32), b.cpu().numpy().astype(np.float32)
+        rs, cs = rows[:200000].cpu().numpy(), cols[:200000].cpu().numpy()
+        t0 = time.perf_counter()
+        _ = (asub[rs] + bsub[cs]) - 2.0 * np.einsum("nd,nd->n", xs[rs], ys[cs])
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": rs.size / dt / 1e9, "unit": "Gedges/s", "cores": 1, "kind": "port",
+                                 "sample": f"{rs.size} edges with the reference's numpy CPU branch"}
+    _line(args, "pair costs Gedges/s", e / sec / 1e9, "Gedges/s", sec,
+          {"workload": f"l2sq pair costs, E={e} random edges of a {n} x {n} problem, d={d}", "edges": e, "d": d},
+          extra)
+
+
+def run_norm(args, hb, dev, peaks):
+    """ℓ1 pricing scan, config 3 shape (n = m = 262144, d = 128, k = 8)."""
+    n, d, k = args.n, args.d, args.k
+    g = torch.Generator(device=dev)
+    g.manual_seed(42)
+    x = torch.randn(n, d, device=dev, generator=g)
+    y = torch.randn(n, d, device=dev, generator=g)
+    f = torch.randn(n, device=dev, dtype=torch.float64, generator=g) * d
+    gg = torch.randn(n, device=dev, dtype=torch.float64, generator=g) * d
+    hb.set_kernel_timing(True)
+    sec = _timed(lambda: hb.norm_scan(x, y, f, gg, k, "l1"), args, dev)
+    kms = hb.last_kernel_times()
+    hb.set_kernel_timing(False)
+    # FP32-pipe roofline: 2 d instructions per pair; peak = 148 SMs x 128 lanes x max clock
+    sm, mhz = torch.cuda.get_device_properties(dev).multi_processor_count, peaks.get("sm_max_mhz", 1965.0)
+    peak = sm * 128 * mhz * 1e6 / 1e12
+    achieved = 2 * d * n * n / (kms[0] / 1e3) / 1e12 if kms else float("nan")
+    extra = {"dtype": "f32 distance, f64 score", "roofline": {
+        "bound": "fp32 pipe", "achieved": achieved, "peak": peak, "unit": "Tinst/s", "frac": achieved / peak,
+        "traffic": None, "kernel": "hb::norm::scan_kernel<0,8,1,0> (pass 1)",
+        "peak_source": "nominal: SMs x 128 fp32 lanes x max SM clock"}}
+    if not args.no_cpu:
+        import oracle
+        rows = 64
+        xs, ys = x[:rows].cpu().numpy(), y.cpu().numpy()
+        t0 = time.perf_counter()
+        oracle.scan("l1", xs, ys, f[:rows].cpu().numpy(), gg.cpu().numpy(), rk=k, ck=0, exact=False,
+                    threads=os.cpu_count() or 1)
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": rows * n / dt / 1e9, "unit": "Gpairs/s", "cores": os.cpu_count() or 1,
+                                 "kind": "port", "sample": f"{rows} source rows x {n} targets, oracle fp32 model"}
+    _line(args, "l1 pricing-scan Gpairs/s (m·n)", n * n / sec / 1e9, "Gpairs/s", sec,
+          {"workload": f"l1 pricing scan, n=m={n}, d={d}, k={k}", "n": n, "d": d, "topk": k}, extra)
+
+
+def run_other(args):
+    import __graft_entry__ as entry
+
+    hb = entry.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, _ = load_peaks()
+    {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm}[args.path](args, hb, dev, peaks)
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.path != "scan":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is defined for the default "
+                                                                  "scan path; other paths report cpu_baseline"}))
+            return
+        run_other(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

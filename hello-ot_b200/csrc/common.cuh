@@ -170,6 +170,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return d;
 }
 
+// Same for a tile stored with the 64-byte swizzle (rows of 64 B, 8-row atoms of 512 B).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);          // start address
+    d |= (uint64_t)1 << 16;                           // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32;                  // stride byte offset: one 8-row atom
+    d |= (uint64_t)1 << 46;                           // descriptor version (sm_100)
+    d |= (uint64_t)4 << 61;                           // layout: 64-byte swizzle
+    return d;
+}
+
 // Instruction descriptor: fp32 accumulate, A/B tf32, both K-major, MxN tile.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);

@@ -8,10 +8,10 @@
 //
 // Layout in HBM: edges sorted by (source row, original index), so a source
 // row's edges are contiguous; a target's incident edges are kept as a list of
-// positions in that order, sorted by original edge index.  Per iteration two
-// kernels run: the source pass (primal update, reflection, Halpern averaging
-// and the source dual update, a warp per source row) and the target pass
-// (the target dual update, a warp per target).  Each node's incident sum is
+// positions in that order, sorted by original edge index.  Per iteration three
+// kernels run: the edge pass (primal update, reflection, Halpern averaging,
+// thread per edge), the source pass (source dual update, thread per row) and
+// the target pass (target dual update, thread per target).  Each node's incident sum is
 // accumulated sequentially in the reference's edge order and this file is
 // compiled without fma contraction, so with the same step sizes one block of
 // iterations reproduces the reference arithmetic bit for bit.
@@ -48,6 +48,7 @@ struct Dev {
     int* t_pos;     // sorted-edge positions of each target's edges, by original index
     double *cost, *cs, *ax, *x, *px, *rx, *dx;  // per sorted edge
     double *mass, *scale, *bs, *ns, *ay, *y, *py, *dy, *td;
+    double* sd;     // [n] source dual / node scale, the value every edge of the row uses
     double* red;    // [RED_BLOCKS][8]
     double* scal;   // [16] reduced scalars
     int* status;
@@ -153,6 +154,7 @@ __global__ void init_state(Dev D, const double* masses, const double* y0, const 
         const double a = (y0 ? y0[i] : 0.0) * D.scale[i] * objective;
         D.ay[i] = a; D.y[i] = a; D.py[i] = a;
         if (i >= D.n) D.td[i - D.n] = a / D.ns[i];
+        else D.sd[i] = a / D.ns[i];
     }
 }
 
@@ -162,64 +164,67 @@ struct Step {
     int checkpoint, major;
 };
 
-// Source pass: primal update of every edge and the source dual update
-// (solver.cpp:255-271).  One warp per source row.
-__global__ void __launch_bounds__(256) source_pass(Dev D, Step s) {
-    const int lane = threadIdx.x & 31;
-    const int warps = (gridDim.x * blockDim.x) >> 5;
-    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < D.n; i += warps) {
-        const double sdual = D.y[i] / D.ns[i];
-        const int b0 = D.s_off[i], b1 = D.s_off[i + 1];
-        double sum = 0.0;
-        for (int base = b0; base < b1; base += 32) {
-            const int p = base + lane;
-            double r = 0.0;
-            if (p < b1) {
-                const double at = sdual + D.td[D.e_col[p]];
-                const double xv = D.x[p];
-                const double pxv = max0(xv - s.primal_step * (D.cs[p] - at));
-                r = 2.0 * pxv - xv;
-                if (s.checkpoint) D.dx[p] = r - xv;
-                D.x[p] = s.halpern * r + (1.0 - s.halpern) * D.ax[p];
-                D.rx[p] = r;
-                if (s.major) D.px[p] = pxv;
-            }
-            sum = ordered_warp_sum(sum, r, min(32, b1 - base));
-        }
-        if (lane == 0) {
-            const double yv = D.y[i];
-            const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
-            const double refl = 2.0 * pyv - yv;
-            if (s.checkpoint) D.dy[i] = refl - yv;
-            D.y[i] = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
-            if (s.major) D.py[i] = pyv;
-        }
+// One PDHG iteration runs as three kernels (solver.cpp:255-281):
+//  edge_pass   : thread per edge, primal update, reflection, Halpern averaging
+//                (coalesced over the source-sorted edges, perfectly balanced);
+//  source_pass : thread per source row, ordered sum of its reflected primal and
+//                the source dual update;
+//  target_pass : thread per target, ordered gather-sum and the target dual update.
+// Each node sums its edges sequentially in the reference's edge order.
+__global__ void __launch_bounds__(256) edge_pass(Dev D, Step s) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
+        const double at = D.sd[D.e_row[p]] + D.td[D.e_col[p]];
+        const double xv = D.x[p];
+        const double pxv = max0(xv - s.primal_step * (D.cs[p] - at));
+        const double r = 2.0 * pxv - xv;
+        if (s.checkpoint) D.dx[p] = r - xv;
+        D.x[p] = s.halpern * r + (1.0 - s.halpern) * D.ax[p];
+        D.rx[p] = r;
+        if (s.major) D.px[p] = pxv;
     }
 }
 
-// Target pass: target dual update from the reflected primal (solver.cpp:273-281).
+__global__ void __launch_bounds__(256) source_pass(Dev D, Step s) {
+    const int stride = gridDim.x * blockDim.x;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D.n; i += stride) {
+        const int b0 = D.s_off[i], b1 = D.s_off[i + 1];
+        double sum = 0.0;
+        const double* rx = D.rx;
+#pragma unroll 4
+        for (int p = b0; p < b1; ++p) sum += __ldg(rx + p);
+        const double yv = D.y[i];
+        const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+        const double refl = 2.0 * pyv - yv;
+        if (s.checkpoint) D.dy[i] = refl - yv;
+        const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+        D.y[i] = ynew;
+        D.sd[i] = ynew / D.ns[i];
+        if (s.major) D.py[i] = pyv;
+    }
+}
+
 __global__ void __launch_bounds__(256) target_pass(Dev D, Step s) {
-    const int lane = threadIdx.x & 31;
-    const int warps = (gridDim.x * blockDim.x) >> 5;
-    for (int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < D.m; j += warps) {
+    const int stride = gridDim.x * blockDim.x;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < D.m; j += stride) {
         const int b0 = D.t_off[j], b1 = D.t_off[j + 1];
         double sum = 0.0;
-        for (int base = b0; base < b1; base += 32) {
-            const int sl = base + lane;
-            const double r = sl < b1 ? D.rx[D.t_pos[sl]] : 0.0;
-            sum = ordered_warp_sum(sum, r, min(32, b1 - base));
+        int sl = b0;
+        for (; sl + 4 <= b1; sl += 4) {  // four independent gathers in flight, summed in order
+            const double r0 = D.rx[D.t_pos[sl]], r1 = D.rx[D.t_pos[sl + 1]];
+            const double r2 = D.rx[D.t_pos[sl + 2]], r3 = D.rx[D.t_pos[sl + 3]];
+            sum += r0; sum += r1; sum += r2; sum += r3;
         }
-        if (lane == 0) {
-            const int i = D.n + j;
-            const double yv = D.y[i];
-            const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
-            const double refl = 2.0 * pyv - yv;
-            if (s.checkpoint) D.dy[i] = refl - yv;
-            const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
-            D.y[i] = ynew;
-            if (s.major) D.py[i] = pyv;
-            D.td[j] = ynew / D.ns[i];
-        }
+        for (; sl < b1; ++sl) sum += D.rx[D.t_pos[sl]];
+        const int i = D.n + j;
+        const double yv = D.y[i];
+        const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+        const double refl = 2.0 * pyv - yv;
+        if (s.checkpoint) D.dy[i] = refl - yv;
+        const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+        D.y[i] = ynew;
+        if (s.major) D.py[i] = pyv;
+        D.td[j] = ynew / D.ns[i];
     }
 }
 
@@ -300,6 +305,7 @@ __global__ void restart_kernel(Dev D) {
         const double v = D.py[i];
         D.ay[i] = v; D.y[i] = v;
         if (i >= D.n) D.td[i - D.n] = v / D.ns[i];
+        else D.sd[i] = v / D.ns[i];
     }
 }
 
@@ -352,7 +358,7 @@ PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e)
     take_d(D.cost, e); take_d(D.cs, e); take_d(D.ax, e); take_d(D.x, e); take_d(D.px, e); take_d(D.rx, e);
     take_d(D.dx, e);
     take_d(D.mass, nodes); take_d(D.scale, nodes); take_d(D.bs, nodes); take_d(D.ns, nodes); take_d(D.ay, nodes);
-    take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m);
+    take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m); take_d(D.sd, n);
     take_d(D.red, (size_t)pdlp::RED_BLOCKS * 8); take_d(D.scal, 16);
     take_i(D.status, 1);
     take_i(L.r32, e); take_i(L.c32, e); take_i(L.iota, e); take_i(L.keys_out, e); take_i(L.t_orig, e);
@@ -538,9 +544,11 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             s.major = ((count + 1) % F) == 0;
             const bool is_restart = t == 0 && restart;
             s.checkpoint = s.major || is_restart;
-            pdlp::source_pass<<<gb, 256, 0, st>>>(D, s);
+            pdlp::edge_pass<<<gb, 256, 0, st>>>(D, s);
             HB_LAUNCHED(1);
-            pdlp::target_pass<<<gb, 256, 0, st>>>(D, s);
+            pdlp::source_pass<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(D, s);
+            HB_LAUNCHED(1);
+            pdlp::target_pass<<<(unsigned)((m + 255) / 256), 256, 0, st>>>(D, s);
             HB_LAUNCHED(1);
             if (s.checkpoint) {
                 pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);

@@ -28,8 +28,13 @@
 namespace hb {
 namespace l2sq {
 
-constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+// K slab of 16 fp32 (64-byte rows, 64-byte swizzle).  A stage holds the query
+// and database tiles and, for the 3xTF32 split, their low parts, so all three
+// products of a slab come from one fetch: [A | A_lo | B | B_lo] = 8+8+16+16 KB.
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
+constexpr int OFF_ALO = A_BYTES, OFF_B = 2 * A_BYTES, OFF_BLO = 2 * A_BYTES + B_BYTES;
+constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
 constexpr int EPI_FIRST = 64;  // warps 0-1: TMA producer, MMA issuer; then EW epilogue warps
 constexpr int MAX_EW = 8;
 // Epilogue warps per CTA: 8 (two per TMEM lane quarter, each on half the
@@ -43,10 +48,10 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 
 struct Params {
-    CUtensorMap qmap[2];  // query operand: [0] features, [1] low parts
+    CUtensorMap qmap[2];  // query operand: [0] features (read as tf32 = hi part), [1] low parts
     CUtensorMap dmap[2];  // database operand
-    int qsel[3], dsel[3]; // map used by each product term
-    int nseg, kslabs;
+    int terms;            // 1: x*y (TF32); 3: x*y + x*lo(y) + lo(x)*y (3xTF32)
+    int kslabs;
     int q, n;
     int groups, tpg, ct, units;
     const double* q_cost;  // a_i  (certificate only)
@@ -76,22 +81,30 @@ constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
 
 __device__ __forceinline__ void producer(const Params& p, Smem& s) {
     uint32_t stage = 0, phase = 0;
+    const uint32_t bytes = p.terms == 3 ? STAGE_BYTES : A_BYTES + B_BYTES;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
         const int rb = u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         for (int ct = g * p.tpg; ct < ct1; ++ct)
-            for (int sg = 0; sg < p.nseg; ++sg)
-                for (int ks = 0; ks < p.kslabs; ++ks) {
-                    if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.abort, p.status)) return;
-                    uint8_t* a = s.stage[stage];
-                    mbar_arrive_expect_tx(&s.full[stage], STAGE_BYTES);
-                    tma_load_2d(a, &p.qmap[p.qsel[sg]], &s.full[stage], ks * BK, rb * BM);
-                    tma_load_2d(a + A_BYTES, &p.dmap[p.dsel[sg]], &s.full[stage], ks * BK, ct * BN);
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            for (int ks = 0; ks < p.kslabs; ++ks) {
+                if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.abort, p.status)) return;
+                uint8_t* a = s.stage[stage];
+                mbar_arrive_expect_tx(&s.full[stage], bytes);
+                tma_load_2d(a, &p.qmap[0], &s.full[stage], ks * BK, rb * BM);
+                tma_load_2d(a + OFF_B, &p.dmap[0], &s.full[stage], ks * BK, ct * BN);
+                if (p.terms == 3) {
+                    tma_load_2d(a + OFF_ALO, &p.qmap[1], &s.full[stage], ks * BK, rb * BM);
+                    tma_load_2d(a + OFF_BLO, &p.dmap[1], &s.full[stage], ks * BK, ct * BN);
                 }
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
     }
 }
 
+// Products per K step of 8: pass 1 (query = x): x*y, x*lo(y), lo(x)*y; pass 2
+// (query = y) issues the same three products with the operands exchanged and
+// in the same order, so both passes accumulate bit-identical dots.
+template <bool SWAP>
 __device__ __forceinline__ void mma_issuer(const Params& p, Smem& s, uint32_t tmem) {
     uint32_t stage = 0, phase = 0, t = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
@@ -103,19 +116,25 @@ __device__ __forceinline__ void mma_issuer(const Params& p, Smem& s, uint32_t tm
             tc_fence_after();
             const uint32_t d = tmem + acc * BN;
             uint32_t accumulate = 0;
-            for (int sg = 0; sg < p.nseg; ++sg)
-                for (int ks = 0; ks < p.kslabs; ++ks) {
-                    if (!mbar_wait(&s.full[stage], phase, &s.abort, p.status)) return;
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(s.stage[stage]), b0 = a0 + A_BYTES;
+            for (int ks = 0; ks < p.kslabs; ++ks) {
+                if (!mbar_wait(&s.full[stage], phase, &s.abort, p.status)) return;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(s.stage[stage]);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        mma_tf32(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), IDESC, accumulate);
-                        accumulate = 1;
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint32_t o = kk * 32;
+                    const uint64_t ah = smem_desc_sw64(a0 + o), bh = smem_desc_sw64(a0 + OFF_B + o);
+                    mma_tf32(d, ah, bh, IDESC, accumulate);
+                    accumulate = 1;
+                    if (p.terms == 3) {
+                        const uint64_t al = smem_desc_sw64(a0 + OFF_ALO + o), bl = smem_desc_sw64(a0 + OFF_BLO + o);
+                        if (!SWAP) { mma_tf32(d, ah, bl, IDESC, 1); mma_tf32(d, al, bh, IDESC, 1); }
+                        else { mma_tf32(d, al, bh, IDESC, 1); mma_tf32(d, ah, bl, IDESC, 1); }
                     }
-                    mma_commit(&s.empty[stage]);
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
+                mma_commit(&s.empty[stage]);
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
             mma_commit(&s.tfull[acc]);
         }
     }
@@ -287,7 +306,7 @@ __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_c
     if (warp == 0) {
         if (lane == 0) producer(p, s);
     } else if (warp == 1) {
-        if (lane == 0) mma_issuer(p, s, tmem);
+        if (lane == 0) mma_issuer<SWAP>(p, s, tmem);
     } else {
         double acc[5] = {0, 0, 0, 0, 0};
         epilogue<K, SM, SWAP>(p, s, tmem, acc);
@@ -366,10 +385,10 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int dp, int box_r
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)dp * sizeof(float)};
-    cuuint32_t box[2] = {(cuuint32_t)l2sq::BK, (cuuint32_t)box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)l2sq::BK, (cuuint32_t)box_rows};  // 64-byte rows
     cuuint32_t estr[2] = {1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -511,15 +530,12 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (precision == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, l2sq::BN);
     else { p.qmap[1] = p.qmap[0]; p.dmap[1] = p.dmap[0]; }
     if (!maps) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
-    // product terms in a fixed order: x*y, x*lo(y), lo(x)*y
-    const int qs[3] = {0, 0, 1}, ds[3] = {0, 1, 0};
-    p.nseg = precision == 3 ? 3 : 1;
+    p.terms = precision == 3 ? 3 : 1;
     p.kslabs = (dp + l2sq::BK - 1) / l2sq::BK;
     p.scale = (float)dot_scale;
     p.status = L.status;
     p.cta_stats = L.cta;
     // pass 1: x rows are the queries (row top-k + certificate)
-    for (int i = 0; i < 3; ++i) { p.qsel[i] = qs[i]; p.dsel[i] = ds[i]; }
     p.q = (int)q; p.n = (int)n;
     p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
     p.q_cost = nx; p.d_cost = ny; p.q_bias = qb; p.d_bias = dbb;
@@ -541,8 +557,6 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
             maps2 = maps2 && make_map(&p2.qmap[1], L.ylo, n, dp, l2sq::BM) && make_map(&p2.dmap[1], L.xlo, q, dp, l2sq::BN);
         else { p2.qmap[1] = p2.qmap[0]; p2.dmap[1] = p2.dmap[0]; }
         if (!maps2) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
-        // keep the product order x*y, x*lo(y), lo(x)*y with the operands exchanged
-        for (int i = 0; i < 3; ++i) { p2.qsel[i] = ds[i]; p2.dsel[i] = qs[i]; }
         p2.q = (int)n; p2.n = (int)q;
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
         p2.q_cost = ny; p2.d_cost = nx; p2.q_bias = dbb; p2.d_bias = qb;
