@@ -47,7 +47,7 @@ sys.path.insert(0, str(REPO))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per pair of one pass-1 launch, from an ncu capture of the
 # scan kernel scaled by the pairs it processed (see profiles/ for the capture and command).
-DRAM_BYTES_PER_PAIR = {(256, "fp32"): 0.1282}  # profiles/l2sq_scan_kernel_c5_d256.md
+DRAM_BYTES_PER_PAIR = {(256, "fp32"): 0.1357}  # profiles/l2sq_scan_kernel_c5_d256.md
 
 
 def parse_args():
