@@ -47,7 +47,8 @@ sys.path.insert(0, str(REPO))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per pair of one pass-1 launch, from an ncu capture of the
 # scan kernel scaled by the pairs it processed (see profiles/ for the capture and command).
-DRAM_BYTES_PER_PAIR = {(256, "fp32"): 0.1357}  # profiles/l2sq_scan_kernel_c5_d256.md
+# DRAM bytes per pair of the scan kernel from an ncu capture (profiles/l2sq_scan_kernel_c5_d256.md)
+DRAM_BYTES_PER_PAIR = {(256, "fp32", "two-pass"): 0.1357}
 
 
 def parse_args():
@@ -64,6 +65,8 @@ def parse_args():
     p.add_argument("--d", type=int, default=256)
     p.add_argument("--k", type=int, default=8)
     p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
+    p.add_argument("--two-pass", action="store_true",
+                   help="scan with two passes (roles exchanged) instead of the one-pass default for k <= 8")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
@@ -249,10 +252,15 @@ def run_reference(args):
     }))
 
 
+def scan_mode(args):
+    return "two-pass" if (args.two_pass or args.k > 8) else "one-pass"
+
+
 def workload_config(args):
     return {"workload": f"C5 isolated pricing scan, l2sq, m=n={args.n}, d={args.d}, k={args.k}",
             "n": args.n, "m": args.n, "d": args.d, "topk": args.k, "cost": "l2sq", "dot_scale": 2.0,
             "precision": {"fp32": "3xTF32 (fp32-class dot)", "tf32": "1xTF32"}[args.precision],
+            "scan_mode": scan_mode(args),
             "parallelism": f"source-row shards x{args.gpus}",
             "l2_policy": "inputs (2 GB clouds) larger than L2; no flush"}
 
@@ -280,7 +288,7 @@ def run_ours(args):
     if world > 1:  # the target cloud is replicated from rank 0 (once per solve)
         dist.broadcast(y, 0)
         dist.broadcast(b, 0)
-    sharded = ShardedPricingScan(precision=args.precision)
+    sharded = ShardedPricingScan(precision=args.precision, two_pass=args.two_pass)
     g_step = g.clone()
 
     def step():
@@ -305,7 +313,7 @@ def run_ours(args):
         start.record()
         for _ in range(args.steps):
             step()
-            pass_ms.append(hb.last_kernel_times()[:2])
+            pass_ms.append(hb.last_kernel_times())
         stop.record()
         torch.cuda.synchronize()
         if world > 1:
@@ -319,17 +327,19 @@ def run_ours(args):
     sec = float(t.item()) / args.steps
     value = n * n / sec / 1e9
 
-    times = [sum(p[j] for p in pass_ms) / len(pass_ms) for j in range(2)] if all(len(p) == 2 for p in pass_ms) \
-        else []
+    nk = len(pass_ms[0]) if pass_ms else 0
+    times = [sum(p[j] for p in pass_ms) / len(pass_ms) for j in range(nk)] \
+        if nk and all(len(p) == nk for p in pass_ms) else []
     out = None
     if rank == 0:
         peaks, peak_kind = load_peaks()
         rows_local = hi - lo
+        mode = scan_mode(args)
         pass1_ms = times[0] if times else float("nan")
-        flops = 2.0 * d * rows_local * n  # algorithmic flops of one pass: one dot product per pair
+        flops = 2.0 * d * rows_local * n  # algorithmic flops of one launch: one dot product per pair
         achieved = flops / (pass1_ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
-        per_pair = DRAM_BYTES_PER_PAIR.get((d, args.precision))
+        per_pair = DRAM_BYTES_PER_PAIR.get((d, args.precision, mode))
         traffic = per_pair * rows_local * n if per_pair else None
         out = {
             "metric": "pricing-scan Gpairs/s (m·n)", "value": value, "unit": "Gpairs/s", "n_gpus": world,
@@ -340,8 +350,10 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "hb::l2sq::scan_kernel (pass 1: source rows, certificate)",
-                         "pass_ms": times[:2], "peak_source": f"{peak_kind} bf16 dense (sustained)",
+                         "kernel": ("hb::l2sq::scan_kernel (one pass: row and column top-k, certificate)"
+                                    if mode == "one-pass" else
+                                    "hb::l2sq::scan_kernel (pass 1 of 2: source rows, score terms)"),
+                         "pass_ms": times, "peak_source": f"{peak_kind} bf16 dense (sustained)",
                          "note": ("algorithmic flops 2*d per pair; the 3xTF32 split issues 3 tf32 products "
                                   "per pair on a pipe with half the bf16 rate")},
             "clocks": clocks.summary(),

@@ -115,11 +115,13 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
         return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
     if (!valid_k(k)) return fail(HB_BAD_ARGUMENT, "k must be in 0..32");
     if (dot_scale != 1.0 && dot_scale != 2.0) return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
-    if (precision != 1 && precision != 3) return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32)");
+    if ((precision & ~HB_L2SQ_TWO_PASS) != 1 && (precision & ~HB_L2SQ_TWO_PASS) != 3)
+        return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32), optionally | HB_L2SQ_TWO_PASS");
     if (k > 0 && (!row_vals || !row_idx || !col_vals || !col_idx)) return fail(HB_BAD_ARGUMENT, "null output pointer");
     if (compute_stats && !stats5) return fail(HB_BAD_ARGUMENT, "null stats pointer");
     if (workspace_bytes < hb::l2sq_bytes(q, n, d, k, precision, min_groups))
         return fail(HB_WORKSPACE, "workspace smaller than hb_l2sq_scan_workspace()");
+    if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(HB_BAD_ARGUMENT, "workspace must be 256-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     std::string err;
     int status_host = 0;

@@ -4,11 +4,12 @@
 // (src/hello_ot/_native/generic_scan/pricing_small.cu:230-304, pricing.cu,
 // matrix_selection.cuh) with one fused persistent kernel per pass:
 //
-//   TMA (128B-swizzled fp32 slabs, local HBM only, no multicast)
+//   TMA (64B-swizzled fp32 slabs, local HBM only, no multicast)
 //     -> tcgen05.mma kind::tf32, 128x256 tile, fp32 accumulator in TMEM
 //        (two accumulators: the MMA of tile t+1 overlaps the epilogue of t)
 //     -> epilogue warps: tcgen05.ld, score, certificate sums, row top-k in
-//        registers.  No cost tile is ever written to HBM.
+//        registers and (one-pass mode) column top-k in per-warp HBM lists.
+//   No cost tile is ever written to HBM.
 //
 // Score arithmetic follows the reference raw path (matrix_selection.cuh:20-26):
 //   dot = fp32(s * <x,y>);  cost = (a_i + b_j) - dot;  score = (dot + qb_i) + dbb_j
@@ -16,11 +17,24 @@
 // 3-term split hi*hi + hi*lo + lo*hi ("3xtf32"), hi = x with the low 13
 // mantissa bits dropped and lo = x - hi (exact), which gives an fp32-class dot.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2-5 epilogue (thread = tile row = TMEM lane).
+// Warp roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, 4 or 8
+// epilogue warps (thread = tile row = TMEM lane).
+//
+// Column top-k.  One-pass mode (k <= 8): each CTA owns a fixed rectangle of
+// the pair space (a row group x a column group); every epilogue warp keeps, in
+// HBM, the top-k list of each of its columns over the rows it sees (one list
+// per row group and TMEM lane quarter, so each list has exactly one writer).
+// Pairs are screened in fp32 against a per-column threshold shared by all of
+// the column's lists (the largest k-th score among them); chunks with a
+// candidate are transposed through shared memory and each lane inserts its
+// column's candidates with exact fp64 scores.  A merge combines the lists.
+// Two-pass mode: a second pass with the clouds' roles exchanged computes the
+// column lists as row lists (same products, same order, same scores).
+#include <algorithm>
 #include <cstring>
 #include <string>
 
+#include "../../include/hello_b200.h"
 #include "common.cuh"
 #include "internal.h"
 #include "scan_common.cuh"
@@ -31,7 +45,7 @@ namespace l2sq {
 // K slab of 16 fp32 (64-byte rows, 64-byte swizzle).  A stage holds the query
 // and database tiles and, for the 3xTF32 split, their low parts, so all three
 // products of a slab come from one fetch: [A | A_lo | B | B_lo] = 8+8+16+16 KB.
-constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 16;
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
 constexpr int OFF_ALO = A_BYTES, OFF_B = 2 * A_BYTES, OFF_BLO = 2 * A_BYTES + B_BYTES;
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
@@ -55,37 +69,79 @@ struct Params {
     int q, n;
     int groups, tpg, ct, units;
     const double* q_cost;  // a_i  (certificate only)
-    const double* d_cost;  // b_j
+    const double* d_cost;  // b_j, padded to whole column tiles (null: no cost terms in this pass)
     const double* q_bias;  // query-side bias
-    const double* d_bias;  // database-side bias
+    const double* d_bias;  // database-side bias, padded to whole column tiles
     float scale;
     double* part_v;
     int* part_i;
     double* cta_stats;
     int* status;
+    // one-pass mode: CTA b owns row group b / groups (rbg row blocks) x column group b % groups
+    int rb, rbg;
+    int* ckey;     // [ct * BN] screening threshold of each column (ordered-int fp32 image), see below
+    double* cval;  // [row groups * 4][n][K]
+    int* cidx;
 };
 
-struct __align__(1024) Smem {
-    uint8_t stage[STAGES][STAGE_BYTES];
-    // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all):
-    double dbias[4 * BN];  // database bias
-    float fbias[4 * BN];   // fp32 copy of the bias
-    float fmarg[4 * BN];   // 2^-21 |bias|, the bias part of the fp32 screening margin
-    float fcost[4 * BN];   // fp32 copy of |y|^2
+// Column vectors of a tile (bias, cost, threshold) are bulk-copied by the
+// producer into a ring of CS slots, ahead of the tile's epilogue.
+template <int NST, int NCS, bool ONE>
+struct __align__(1024) SmemT {
+    static constexpr int STAGES = NST, CS = NCS;
+    uint8_t stage[NST][STAGE_BYTES];
+    double cbias[NCS][BN];                     // the tile's column biases
+    double ccost[NCS][BN];                     // the tile's column costs (cost terms)
+    int ckey[ONE ? NCS : 1][ONE ? BN : 4];     // the tile's column thresholds (one pass)
+    // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all), fp32
+    // constants read once per pair: x = bias, y = 2^-21 |bias| (the bias part of the
+    // screening margin), z = |y|^2, w = column threshold (one pass)
+    float4 col[4 * BN];
+    float trans[ONE ? MAX_EW * 32 * 33 : 1];   // per warp: 32 x 32 chunk, transposed
+    double rbx[ONE ? MAX_EW * 32 : 1];         // per warp: the chunk rows' biases
     double red[MAX_EW * 5];
-    uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+    uint64_t full[NST], empty[NST], tfull[2], tempty[2], cfull[NCS], cempty[NCS];
     uint32_t tmem_base;
     int abort;
 };
-constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+template <bool ONE>
+using Smem = SmemT<ONE ? 3 : 4, 4, ONE>;
+template <bool ONE>
+constexpr size_t smem_bytes() { return sizeof(Smem<ONE>) + 1024; }
+static_assert(smem_bytes<false>() <= 227 * 1024 && smem_bytes<true>() <= 227 * 1024,
+              "dynamic shared memory above the 227 KB a CTA may use");
 
-__device__ __forceinline__ void producer(const Params& p, Smem& s) {
+// Tile schedule of a CTA: units u = rb * groups + g in [u0, uend) by ustep.
+struct Sched {
+    int u0, ustep, uend;
+};
+template <bool ONE>
+__device__ __forceinline__ Sched schedule(const Params& p) {
+    if (!ONE) return {(int)blockIdx.x, (int)gridDim.x, p.units};
+    const int rg = blockIdx.x / p.groups, g = blockIdx.x % p.groups;
+    const int rb0 = rg * p.rbg, rb1 = min(p.rb, rb0 + p.rbg);
+    return {rb0 * p.groups + g, p.groups, rb1 > rb0 ? rb1 * p.groups : 0};
+}
+
+template <bool ONE>
+__device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
+    constexpr int STAGES = Smem<ONE>::STAGES, CSLOTS = Smem<ONE>::CS;
     uint32_t stage = 0, phase = 0;
     const uint32_t bytes = p.terms == 3 ? STAGE_BYTES : A_BYTES + B_BYTES;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    const uint32_t cbytes = BN * 8 + (p.d_cost ? BN * 8 : 0) + (ONE ? BN * 4 : 0);
+    uint32_t t = 0;
+    const Sched sc = schedule<ONE>(p);
+    for (int u = sc.u0; u < sc.uend; u += sc.ustep) {
         const int rb = u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
-        for (int ct = g * p.tpg; ct < ct1; ++ct)
+        for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
+            // the tile's column vectors (the slot was released CSLOTS tiles ago)
+            const uint32_t cs = t % CSLOTS;
+            if (!mbar_wait(&s.cempty[cs], ((t / CSLOTS) & 1) ^ 1, &s.abort, p.status)) return;
+            mbar_arrive_expect_tx(&s.cfull[cs], cbytes);
+            bulk_load_1d(s.cbias[cs], p.d_bias + (size_t)ct * BN, BN * 8, &s.cfull[cs]);
+            if (p.d_cost) bulk_load_1d(s.ccost[cs], p.d_cost + (size_t)ct * BN, BN * 8, &s.cfull[cs]);
+            if (ONE) bulk_load_1d(s.ckey[cs], p.ckey + (size_t)ct * BN, BN * 4, &s.cfull[cs]);
             for (int ks = 0; ks < p.kslabs; ++ks) {
                 if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.abort, p.status)) return;
                 uint8_t* a = s.stage[stage];
@@ -98,16 +154,19 @@ __device__ __forceinline__ void producer(const Params& p, Smem& s) {
                 }
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }
             }
+        }
     }
 }
 
 // Products per K step of 8: pass 1 (query = x): x*y, x*lo(y), lo(x)*y; pass 2
 // (query = y) issues the same three products with the operands exchanged and
 // in the same order, so both passes accumulate bit-identical dots.
-template <bool SWAP>
-__device__ __forceinline__ void mma_issuer(const Params& p, Smem& s, uint32_t tmem) {
+template <bool SWAP, bool ONE>
+__device__ __forceinline__ void mma_issuer(const Params& p, Smem<ONE>& s, uint32_t tmem) {
+    constexpr int STAGES = Smem<ONE>::STAGES;
     uint32_t stage = 0, phase = 0, t = 0;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    const Sched sc = schedule<ONE>(p);
+    for (int u = sc.u0; u < sc.uend; u += sc.ustep) {
         const int g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
@@ -151,11 +210,11 @@ enum : int { kScoreStats = 1, kCostStats = 2 };
 // fp64), and the candidate mask: columns whose fp32 score plus the rounding
 // margin 2^-21 (|dot| + |biases|) reaches the row's k-th score rounded down.
 // FULL: all 32 columns are valid for the whole warp (no per-column masking).
-template <int K, int SM, bool SWAP, bool FULL>
-__device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float scale, const float* fb, const float* fm,
-                                                 const float* fc, float rbias_f, float rmarg_f, float rcost_f, int live,
-                                                 float thr, double (&acc)[5]) {
-    uint32_t mask = 0;
+template <int K, int SM, bool SWAP, bool FULL, bool ONE>
+__device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float scale, const float4* col,
+                                                 float rbias_f, float rmarg_f, float rcost_f, int live, float thr,
+                                                 uint32_t& cmask, double (&acc)[5]) {
+    uint32_t mask = 0, cm = 0;
     float num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
     float mpos = 0.0f, mcost = 0.0f;
     int cnt = 0;
@@ -163,8 +222,9 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
     for (int j = 0; j < 32; ++j) {
         const bool ok = FULL || j < live;
         const float dotf = scale * v[j];
+        const float4 cc = col[j];  // broadcast
         if (K > 0 || (SM & kScoreStats)) {
-            const float sf = SWAP ? ((dotf + fb[j]) + rbias_f) : ((dotf + rbias_f) + fb[j]);
+            const float sf = SWAP ? ((dotf + cc.x) + rbias_f) : ((dotf + rbias_f) + cc.x);
             if (SM & kScoreStats) {
                 const bool pos = ok && sf > 0.0f;
                 num4[j & 3] = fmaf(sf, pos ? sf : 0.0f, num4[j & 3]);
@@ -172,12 +232,13 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
                 cnt += pos ? 1 : 0;
             }
             if (K > 0) {
-                const float m = fmaf(fabsf(dotf), 0x1p-21f, fm[j] + rmarg_f);
+                const float m = fmaf(fabsf(dotf), 0x1p-21f, cc.y + rmarg_f);
                 mask |= (ok && sf + m >= thr) ? (1u << j) : 0u;
+                if (ONE) cm |= (ok && sf + m >= cc.w) ? (1u << j) : 0u;
             }
         }
         if (SM & kCostStats) {
-            const float cf = (rcost_f + fc[j]) - dotf;
+            const float cf = (rcost_f + cc.z) - dotf;
             den4[j & 3] = fmaf(cf, ok ? cf : 0.0f, den4[j & 3]);
             mcost = fmaxf(mcost, ok ? fabsf(cf) : 0.0f);
         }
@@ -191,31 +252,135 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
         acc[1] += ((double)den4[0] + (double)den4[1]) + ((double)den4[2] + (double)den4[3]);
         acc[3] = fmax(acc[3], (double)mcost);
     }
+    cmask = cm;
     return mask;
+}
+
+// Column thresholds.  Every full column list's k-th score is a lower bound on
+// the k-th best score of that column over all rows, so the largest of them is
+// too: a pair below it is in no final column list and need not be offered.
+// Lists of all row groups raise one shared threshold per column (atomicMax on
+// an order-preserving integer image of the fp32 value, rounded down); a stale
+// read only screens less.  The threshold array (4 bytes per column) stays in L2.
+__device__ __forceinline__ int order_key(float f) {
+    const int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float order_value(int key) { return __int_as_float(key >= 0 ? key : key ^ 0x7FFFFFFF); }
+
+// One-pass column update of a 32 x 32 chunk (all lanes of the warp), in two
+// steps so the chunk's registers are free during the list insertions:
+// column_stage transposes the fp32 dots (and the rows' biases) through shared
+// memory; column_update then has lane c insert the candidate rows of column c
+// (the bits c of the rows' masks) into that column's list with exact fp64
+// scores (dot + qb_row) + dbb_col.  The list is read from and written back to
+// HBM only when the lane has a candidate, and a full list raises the column
+// threshold.
+// A column list (K scores, K indices) in HBM, moved with 16-byte accesses.
+template <int KK>
+__device__ __forceinline__ void load_list(const Params& p, int64_t base, TopK<KK>& ct) {
+    if constexpr (KK % 2 == 0) {
+#pragma unroll
+        for (int t = 0; t < KK; t += 2) {
+            const double2 w = *reinterpret_cast<const double2*>(p.cval + base + t);
+            ct.v[t] = w.x; ct.v[t + 1] = w.y;
+        }
+    } else {
+        ct.v[0] = p.cval[base];
+    }
+    if constexpr (KK % 4 == 0) {
+#pragma unroll
+        for (int t = 0; t < KK; t += 4) {
+            const int4 w = *reinterpret_cast<const int4*>(p.cidx + base + t);
+            ct.i[t] = w.x; ct.i[t + 1] = w.y; ct.i[t + 2] = w.z; ct.i[t + 3] = w.w;
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < KK; ++t) ct.i[t] = p.cidx[base + t];
+    }
+}
+template <int KK>
+__device__ __forceinline__ void store_list(const Params& p, int64_t base, const TopK<KK>& ct) {
+    if constexpr (KK % 2 == 0) {
+#pragma unroll
+        for (int t = 0; t < KK; t += 2)
+            *reinterpret_cast<double2*>(p.cval + base + t) = make_double2(ct.v[t], ct.v[t + 1]);
+    } else {
+        p.cval[base] = ct.v[0];
+    }
+    if constexpr (KK % 4 == 0) {
+#pragma unroll
+        for (int t = 0; t < KK; t += 4)
+            *reinterpret_cast<int4*>(p.cidx + base + t) = make_int4(ct.i[t], ct.i[t + 1], ct.i[t + 2], ct.i[t + 3]);
+    } else {
+#pragma unroll
+        for (int t = 0; t < KK; ++t) p.cidx[base + t] = ct.i[t];
+    }
+}
+
+template <bool ONE>
+__device__ __forceinline__ void column_stage(Smem<ONE>& s, const float (&v)[32], int ew, int lane, double rbias) {
+    float* T = s.trans + ew * 32 * 33;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) T[lane * 33 + j] = v[j];
+    s.rbx[ew * 32 + lane] = rbias;
+    __syncwarp();
+}
+
+template <int K, bool ONE>
+__device__ __forceinline__ void column_update(const Params& p, Smem<ONE>& s, uint32_t cmask, int ew, int lane,
+                                              int row0, int col0, double cbias, int64_t list_base) {
+    constexpr int KK = K > 0 ? K : 1;
+    const float* T = s.trans + ew * 32 * 33;
+    const double* RB = s.rbx + ew * 32;
+    // rows with a candidate (few once the lists have filled); lane c collects the
+    // rows whose candidate mask has bit c
+    uint32_t rows = __ballot_sync(0xffffffffu, cmask != 0u), mine = 0;
+    while (rows) {
+        const int r = __ffs(rows) - 1;
+        rows &= rows - 1;
+        const uint32_t m = __shfl_sync(0xffffffffu, cmask, r);
+        mine |= ((m >> lane) & 1u) << r;
+    }
+    if (mine) {
+        const int64_t base = (list_base + col0 + lane) * KK;
+        TopK<KK> ct;
+        load_list<KK>(p, base, ct);
+        while (mine) {
+            const int r = __ffs(mine) - 1;
+            mine &= mine - 1;
+            const double dot = (double)(p.scale * T[r * 33 + lane]);
+            ct.offer((dot + RB[r]) + cbias, row0 + r);
+        }
+        store_list<KK>(p, base, ct);
+        if (ct.i[KK - 1] != INT32_MAX) atomicMax(p.ckey + col0 + lane, order_key(__double2float_rd(ct.v[KK - 1])));
+    }
+    __syncwarp();
 }
 
 // Epilogue.  Thread = one tile row (TMEM lane) in one column slice.  Per 32
 // columns: phase 1 (above), then phase 2 inserts the masked columns into the
 // row's k-list with exact fp64 scores (rare once the list has filled), so
 // reported scores follow the reference arithmetic (dot + qb) + dbb in fp64.
-template <int K, int SM, bool SWAP>
-__device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem, double (&acc)[5]) {
+template <int K, int SM, bool SWAP, bool ONE>
+__device__ __forceinline__ void epilogue(const Params& p, Smem<ONE>& s, uint32_t tmem, double (&acc)[5]) {
     constexpr int KK = K > 0 ? K : 1;
     constexpr int EW = Epi<K>::EW;
     constexpr int SLICES = EW / 4;
     constexpr int SLICE = BN / SLICES;
+    constexpr int CSLOTS = Smem<ONE>::CS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ew = warp - EPI_FIRST / 32;
     const int quarter = warp & 3;           // TMEM lanes this warp may read
     const int slice = ew / 4;
     const int r = quarter * 32 + lane;      // tile row owned by this thread
-    double* wbias = s.dbias + ew * SLICE;
-    float* wfb = s.fbias + ew * SLICE;
-    float* wfm = s.fmarg + ew * SLICE;
-    float* wfc = s.fcost + ew * SLICE;
+    float4* wcol = s.col + ew * SLICE;
+    // one-pass: this warp's column lists (row group of the CTA, TMEM lane quarter)
+    const int64_t list_base = ONE ? (int64_t)((blockIdx.x / p.groups) * 4 + quarter) * p.n : 0;
     TopK<KK> top;
     uint32_t t = 0;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    const Sched sched = schedule<ONE>(p);
+    for (int u = sched.u0; u < sched.uend; u += sched.ustep) {
         const int rb = u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         const int row = rb * BM + r;
@@ -229,14 +394,17 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
             const uint32_t buf = t & 1, aph = (t >> 1) & 1;
             const int c0 = ct * BN + slice * SLICE;
             const int ncols = min(SLICE, p.n - c0);  // may be <= 0 for the last tile's upper slice
-            __syncwarp();  // the warp is done reading the previous tile's staging
+            const uint32_t cs = t % CSLOTS;
+            if (!mbar_wait(&s.cfull[cs], (t / CSLOTS) & 1, &s.abort, p.status)) return;
+            const double* wbias = s.cbias[cs] + slice * SLICE;  // exact column biases of the slice
+            __syncwarp();  // the warp is done reading the previous tile's constants
             for (int c = lane; c < SLICE; c += 32) {
                 const bool ok = c < ncols;
-                const double bv = ok ? p.d_bias[c0 + c] : 0.0;
-                wbias[c] = bv;
-                wfb[c] = (float)bv;
-                wfm[c] = 0x1p-21f * fabsf((float)bv);
-                if (SM & kCostStats) wfc[c] = ok ? (float)p.d_cost[c0 + c] : 0.0f;
+                const float bf = ok ? (float)wbias[c] : 0.0f;
+                float cf = 0.0f, th = 0.0f;
+                if constexpr ((SM & kCostStats) != 0) cf = ok ? (float)s.ccost[cs][slice * SLICE + c] : 0.0f;
+                if constexpr (ONE) th = ok ? order_value(s.ckey[cs][slice * SLICE + c]) : INFINITY;
+                wcol[c] = make_float4(bf, 0x1p-21f * fabsf(bf), cf, th);
             }
             __syncwarp();
             if (!mbar_wait(&s.tfull[buf], aph, &s.abort, p.status)) return;
@@ -249,13 +417,15 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
                 const int cb = ch * 32;
                 const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
                 const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY : __double2float_rd(top.v[KK - 1]);
-                uint32_t mask;
+                uint32_t mask, cmask;
                 if (__all_sync(0xffffffffu, live == 32))
-                    mask = chunk_phase1<K, SM, SWAP, true>(v, p.scale, wfb + cb, wfm + cb, wfc + cb, rbias_f, rmarg_f,
-                                                           rcost_f, live, thr, acc);
+                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, p.scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
+                                                                live, thr, cmask, acc);
                 else
-                    mask = chunk_phase1<K, SM, SWAP, false>(v, p.scale, wfb + cb, wfm + cb, wfc + cb, rbias_f,
-                                                            rmarg_f, rcost_f, live, thr, acc);
+                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, p.scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
+                                                                 live, thr, cmask, acc);
+                const bool colwork = ONE && K > 0 && __any_sync(0xffffffffu, cmask != 0u);
+                if (colwork) column_stage<ONE>(s, v, ew, lane, rbias);
                 // phase 2: exact fp64 scores of the masked columns into the row list
                 while (K > 0 && mask) {
                     const int j = __ffs(mask) - 1;
@@ -268,9 +438,14 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
                     const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
                     top.offer(sc, c0 + cb + j);
                 }
+                if (colwork)
+                    column_update<K, ONE>(p, s, cmask, ew, lane, rb * BM + quarter * 32, c0 + cb, wbias[cb + lane],
+                                          list_base);
             }
             tc_fence_before();
             mbar_arrive(&s.tempty[buf]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.cempty[cs]);  // the warp is done with the tile's column slot
         }
         if (K > 0 && rvalid) {
             const int part = g * SLICES + slice;
@@ -282,15 +457,17 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem& s, uint32_t tmem
     }
 }
 
-template <int K, int SM, bool SWAP>
+template <int K, int SM, bool SWAP, bool ONE>
 __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_constant__ Params p) {
     constexpr int EW = Epi<K>::EW;
+    constexpr int STAGES = Smem<ONE>::STAGES;
     extern __shared__ uint8_t smem_raw[];
-    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<ONE>& s = *reinterpret_cast<Smem<ONE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], 32 * EW); }
+        for (int i = 0; i < Smem<ONE>::CS; ++i) { mbar_init(&s.cfull[i], 1); mbar_init(&s.cempty[i], EW); }
         s.abort = 0;
         fence_barrier_init();
     }
@@ -304,12 +481,12 @@ __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_c
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
     if (warp == 0) {
-        if (lane == 0) producer(p, s);
+        if (lane == 0) producer<ONE>(p, s);
     } else if (warp == 1) {
-        if (lane == 0) mma_issuer<SWAP>(p, s, tmem);
+        if (lane == 0) mma_issuer<SWAP, ONE>(p, s, tmem);
     } else {
         double acc[5] = {0, 0, 0, 0, 0};
-        epilogue<K, SM, SWAP>(p, s, tmem, acc);
+        epilogue<K, SM, SWAP, ONE>(p, s, tmem, acc);
         if (SM) {  // warp totals in a fixed shuffle order
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) {
@@ -338,6 +515,32 @@ __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_c
             a[4] += s.red[w * 5 + 4];
         }
         for (int j = 0; j < 5; ++j) p.cta_stats[blockIdx.x * 5 + j] = a[j];
+    }
+}
+
+// Column vectors padded with zeros to whole column tiles (bulk copies read
+// whole tiles): dst[i] = i < n ? src[i] : 0 for up to four vectors.
+struct PadJob {
+    const double* src[4];
+    double* dst[4];
+    int64_t n[4], npad[4];
+};
+__global__ void pad_columns(const PadJob job) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int v = 0; v < 4; ++v) {
+        if (!job.dst[v]) continue;
+        for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < job.npad[v]; e += stride)
+            job.dst[v][e] = e < job.n[v] ? job.src[v][e] : 0.0;
+    }
+}
+
+// Empty one-pass column lists: (-inf, no index), thresholds -inf.
+__global__ void init_columns(double* cval, int* cidx, int* ckey, int64_t lists, int64_t n, int K) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t total = lists * K > n ? lists * K : n;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        if (e < lists * K) { cval[e] = -INFINITY; cidx[e] = INT32_MAX; }
+        if (e < n) ckey[e] = order_key(-INFINITY);
     }
 }
 
@@ -392,17 +595,18 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int dp, int box_r
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int K, int SM, bool SWAP>
+template <int K, int SM, bool SWAP, bool ONE = false>
 cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
-    auto fn = l2sq::scan_kernel<K, SM, SWAP>;
+    auto fn = l2sq::scan_kernel<K, SM, SWAP, ONE>;
+    constexpr size_t smem = l2sq::smem_bytes<ONE>();
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)l2sq::SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     timing_mark(st);
-    fn<<<grid, l2sq::Epi<K>::THREADS, l2sq::SMEM_BYTES, st>>>(p);
+    fn<<<grid, l2sq::Epi<K>::THREADS, smem, st>>>(p);
     timing_mark(st);
     count_launches(1);
     return cudaGetLastError();
@@ -417,6 +621,17 @@ cudaError_t launch_k(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
         case 8: return launch_pass<8, SM, SWAP>(p, grid, st);
         case 16: return launch_pass<16, SM, SWAP>(p, grid, st);
         case 32: return launch_pass<32, SM, SWAP>(p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int SM>
+cudaError_t launch_one(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
+    switch (K) {
+        case 1: return launch_pass<1, SM, false, true>(p, grid, st);
+        case 2: return launch_pass<2, SM, false, true>(p, grid, st);
+        case 4: return launch_pass<4, SM, false, true>(p, grid, st);
+        case 8: return launch_pass<8, SM, false, true>(p, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -459,12 +674,43 @@ cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64
 // Column slices per tile (= row partial lists per unit) of the bucket-K kernel.
 inline int l2sq_slices(int K) { return (K <= 8 ? 8 : 4) / 4; }
 
+// One-pass rectangle plan: GR row groups x GC column groups, one CTA each.
+// Few row groups keep the number of column partial lists (4 GR per column)
+// and their insertions small; each row group re-reads its column groups'
+// features once per row block, which costs HBM bandwidth (not the bound).
+constexpr int ONE_PASS_ROW_GROUPS = 8;
+inline bool use_one_pass(int K, int precision) { return K > 0 && K <= 8 && !(precision & HB_L2SQ_TWO_PASS); }
+
+struct OnePlan {
+    int rb, ct, gr, rbg, gc, tpg, grid;
+};
+inline OnePlan one_plan(int64_t q, int64_t n, int sms, int min_groups) {
+    OnePlan o{};
+    o.rb = (int)((q + l2sq::BM - 1) / l2sq::BM);
+    o.ct = (int)((n + l2sq::BN - 1) / l2sq::BN);
+    o.gr = std::min(ONE_PASS_ROW_GROUPS, o.rb);
+    o.rbg = (o.rb + o.gr - 1) / o.gr;
+    o.gr = (o.rb + o.rbg - 1) / o.rbg;
+    int gc = std::max(1, std::max(sms / o.gr, min_groups));
+    gc = std::min(gc, o.ct);
+    o.tpg = (o.ct + gc - 1) / gc;
+    o.gc = (o.ct + o.tpg - 1) / o.tpg;
+    o.grid = o.gr * o.gc;
+    return o;
+}
+
 // Scratch layout of one ℓ2² scan call.  With base == nullptr only sizes it.
 struct L2sqLayout {
     float *xpad = nullptr, *ypad = nullptr, *xlo = nullptr, *ylo = nullptr;
     double *pv1 = nullptr, *pv2 = nullptr, *cta = nullptr;
     int *pi1 = nullptr, *pi2 = nullptr, *status = nullptr;
+    int* ckey = nullptr;  // one-pass column lists and thresholds
+    double *ybp = nullptr, *ycp = nullptr, *xbp = nullptr, *xcp = nullptr;  // padded column vectors
+    double* cval = nullptr;
+    int* cidx = nullptr;
     ScanPlan p1{}, p2{};
+    OnePlan one{};
+    bool one_pass = false;
     size_t bytes = 0;
     bool ok = true;
 };
@@ -473,6 +719,7 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     L2sqLayout L;
     const int sms = device_sms();
     const int K = k > 0 ? bucket_of(k) : 0;
+    const int prec = precision & 0xF;
     const int dp = (int)((d + 3) / 4 * 4);
     const bool pad = dp != d;
     Arena ar{static_cast<char*>(base), size, 0};
@@ -484,18 +731,36 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     };
     need(pad, L.xpad, (size_t)q * dp);
     need(pad, L.ypad, (size_t)n * dp);
-    need(precision == 3, L.xlo, (size_t)q * dp);
-    need(precision == 3, L.ylo, (size_t)n * dp);
-    // features wider than ~1k keep more column groups so the row-block slabs in flight fit in L2
-    const int wide = (int)(d / 1024) + 1;
-    L.p1 = scan_plan(q, n, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
-    L.p2 = scan_plan(n, q, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
+    need(prec == 3, L.xlo, (size_t)q * dp);
+    need(prec == 3, L.ylo, (size_t)n * dp);
     const int slices = K > 0 ? l2sq_slices(K) : 1;
-    need(K > 0, L.pv1, (size_t)L.p1.groups * slices * q * K);
-    need(K > 0, L.pi1, (size_t)L.p1.groups * slices * q * K);
-    need(K > 0, L.pv2, (size_t)L.p2.groups * slices * n * K);
-    need(K > 0, L.pi2, (size_t)L.p2.groups * slices * n * K);
-    need(true, L.cta, (size_t)(L.p1.grid + L.p2.grid) * 5);
+    const size_t npad = (size_t)(n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
+    const size_t qpad = (size_t)(q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
+    L.one_pass = use_one_pass(K, precision);
+    need(true, L.ybp, npad);
+    need(true, L.ycp, npad);
+    need(!L.one_pass && K > 0, L.xbp, qpad);
+    need(!L.one_pass && K > 0, L.xcp, qpad);
+    if (L.one_pass) {
+        L.one = one_plan(q, n, sms, min_groups);
+        const size_t lists = (size_t)L.one.gr * 4 * n;
+        need(true, L.pv1, (size_t)L.one.gc * slices * q * K);
+        need(true, L.pi1, (size_t)L.one.gc * slices * q * K);
+        need(true, L.cval, lists * K);
+        need(true, L.cidx, lists * K);
+        need(true, L.ckey, npad);
+        need(true, L.cta, (size_t)L.one.grid * 5);
+    } else {
+        // features wider than ~1k keep more column groups so the row-block slabs in flight fit in L2
+        const int wide = (int)(d / 1024) + 1;
+        L.p1 = scan_plan(q, n, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
+        L.p2 = scan_plan(n, q, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
+        need(K > 0, L.pv1, (size_t)L.p1.groups * slices * q * K);
+        need(K > 0, L.pi1, (size_t)L.p1.groups * slices * q * K);
+        need(K > 0, L.pv2, (size_t)L.p2.groups * slices * n * K);
+        need(K > 0, L.pi2, (size_t)L.p2.groups * slices * n * K);
+        need(true, L.cta, (size_t)(L.p1.grid + L.p2.grid) * 5);
+    }
     need(true, L.status, 1);
     L.bytes = ar.used + 256;
     return L;
@@ -512,6 +777,7 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     L2sqLayout L = l2sq_layout(ws, ws_bytes, q, n, d, k, precision, min_groups);
     if (!L.ok) { err = "workspace too small for the l2sq scan"; return 3; }
     const int K = k > 0 ? bucket_of(k) : 0;
+    const int prec = precision & 0xF;
     const int dp = (int)((d + 3) / 4 * 4);
     cudaError_t e = cudaMemsetAsync(L.status, 0, sizeof(int), st);
     if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
@@ -524,22 +790,57 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         count_launches(2);
         if (L.xpad) { xs = L.xpad; ys = L.ypad; }
     }
+    const int64_t npad = (n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
+    const int64_t qpad = (q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
+    {
+        l2sq::PadJob job{};
+        job.src[0] = dbb; job.dst[0] = L.ybp; job.n[0] = n; job.npad[0] = npad;
+        job.src[1] = ny; job.dst[1] = L.ycp; job.n[1] = n; job.npad[1] = npad;
+        job.src[2] = qb; job.dst[2] = L.xbp; job.n[2] = q; job.npad[2] = qpad;
+        job.src[3] = nx; job.dst[3] = L.xcp; job.n[3] = q; job.npad[3] = qpad;
+        l2sq::pad_columns<<<prep_blocks, 256, 0, st>>>(job);
+        count_launches(1);
+    }
     l2sq::Params p;
     std::memset(&p, 0, sizeof(p));
     bool maps = make_map(&p.qmap[0], xs, q, dp, l2sq::BM) && make_map(&p.dmap[0], ys, n, dp, l2sq::BN);
-    if (precision == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, l2sq::BN);
+    if (prec == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, l2sq::BN);
     else { p.qmap[1] = p.qmap[0]; p.dmap[1] = p.dmap[0]; }
     if (!maps) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
-    p.terms = precision == 3 ? 3 : 1;
+    p.terms = prec == 3 ? 3 : 1;
     p.kslabs = (dp + l2sq::BK - 1) / l2sq::BK;
     p.scale = (float)dot_scale;
     p.status = L.status;
     p.cta_stats = L.cta;
-    // pass 1: x rows are the queries (row top-k + certificate)
     p.q = (int)q; p.n = (int)n;
-    p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
-    p.q_cost = nx; p.d_cost = ny; p.q_bias = qb; p.d_bias = dbb;
+    p.q_cost = nx; p.d_cost = L.ycp; p.q_bias = qb; p.d_bias = L.ybp;
     p.part_v = L.pv1; p.part_i = L.pi1;
+    if (L.one_pass) {
+        // one pass: row lists in registers, column lists per (row group, lane quarter) in HBM
+        const OnePlan& o = L.one;
+        const int64_t lists = (int64_t)o.gr * 4 * n;
+        l2sq::init_columns<<<prep_blocks, 256, 0, st>>>(L.cval, L.cidx, L.ckey, lists, npad, K);
+        count_launches(1);
+        p.groups = o.gc; p.tpg = o.tpg; p.ct = o.ct; p.units = o.rb * o.gc;
+        p.rb = o.rb; p.rbg = o.rbg;
+        p.ckey = L.ckey; p.cval = L.cval; p.cidx = L.cidx;
+        if (!want_stats) p.d_cost = nullptr;  // the cost vector is staged only for the cost terms
+        e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats>(K, p, o.grid, st)
+                       : launch_one<0>(K, p, o.grid, st);
+        if (e != cudaSuccess) { err = std::string("l2sq scan: ") + cudaGetErrorString(e); return 6; }
+        e = merge_any(K, L.pv1, L.pi1, o.gc * l2sq_slices(K), q, k, rv, ri, st);
+        if (e == cudaSuccess) e = merge_any(K, L.cval, L.cidx, o.gr * 4, n, k, cv, ci, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        if (want_stats) {
+            finalize_stats<<<1, 32, 0, st>>>(L.cta, o.grid, stats5);
+            count_launches(1);
+        }
+        if (status_out) cudaMemcpyAsync(status_out, L.status, sizeof(int), cudaMemcpyDeviceToHost, st);
+        return 0;
+    }
+    // pass 1: x rows are the queries (row top-k + certificate)
+    p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
+    if (K != 0) p.d_cost = nullptr;  // cost terms are in pass 2 (a certificate-only pass takes all terms)
     // certificate: score terms in the row pass, cost terms in the column pass
     // (a certificate-only call has no column pass and takes all terms here)
     if (K == 0) e = launch_pass<0, l2sq::kScoreStats | l2sq::kCostStats, false>(p, L.p1.grid, st);
@@ -548,18 +849,17 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (K > 0) {
         e = merge_any(K, L.pv1, L.pi1, L.p1.groups * l2sq_slices(K), q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
-        // pass 2: y rows are the queries, same products in the same order
         // pass 2: y rows are the queries, same products in the same order;
         // the maps are rebuilt because a map fixes its box height (A 128 rows, B 256 rows)
         l2sq::Params p2 = p;
         bool maps2 = make_map(&p2.qmap[0], ys, n, dp, l2sq::BM) && make_map(&p2.dmap[0], xs, q, dp, l2sq::BN);
-        if (precision == 3)
+        if (prec == 3)
             maps2 = maps2 && make_map(&p2.qmap[1], L.ylo, n, dp, l2sq::BM) && make_map(&p2.dmap[1], L.xlo, q, dp, l2sq::BN);
         else { p2.qmap[1] = p2.qmap[0]; p2.dmap[1] = p2.dmap[0]; }
         if (!maps2) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
         p2.q = (int)n; p2.n = (int)q;
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
-        p2.q_cost = ny; p2.d_cost = nx; p2.q_bias = dbb; p2.d_bias = qb;
+        p2.q_cost = ny; p2.d_cost = want_stats ? L.xcp : nullptr; p2.q_bias = dbb; p2.d_bias = L.xbp;
         p2.part_v = L.pv2; p2.part_i = L.pi2;
         p2.cta_stats = L.cta + (size_t)L.p1.grid * 5;
         e = want_stats ? launch_k<l2sq::kCostStats, true>(K, p2, L.p2.grid, st) : launch_k<0, true>(K, p2, L.p2.grid, st);

@@ -68,17 +68,24 @@ def _c(t):
     return t.contiguous()
 
 
+L2SQ_TWO_PASS = 0x10
+
+
 def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute_stats=True, precision="fp32",
-              min_groups=0):
+              min_groups=0, two_pass=False):
     """Bidirectional ℓ2² scan on the tensor cores.
 
-    Returns (row_vals q x k fp64, row_idx q x k int32, col_vals n x k, col_idx n x k,
-    stats [sum s+^2, sum c^2, max s+, max |c|, count] fp64 on the device)."""
+    k <= 8 makes one pass over the pairs unless two_pass is set (both modes give
+    the same lists bit for bit).  Returns (row_vals q x k fp64, row_idx q x k int32,
+    col_vals n x k, col_idx n x k, stats [sum s+^2, sum c^2, max s+, max |c|, count]
+    fp64 on the device)."""
     x, y = _c(x), _c(y)
     x_cost, y_cost, x_bias, y_bias = map(_c, (x_cost, y_cost, x_bias, y_bias))
     q, d = x.shape
     n = y.shape[0]
     prec = PRECISION[precision] if isinstance(precision, str) else int(precision)
+    if two_pass:
+        prec |= L2SQ_TWO_PASS
     L = lib()
     dev = x.device
     kk = int(k)

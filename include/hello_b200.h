@@ -7,7 +7,8 @@
  * and a nonzero HB_* code on failure; hb_last_error() then holds a message
  * (per calling thread).  No entry point allocates device memory: callers
  * provide scratch through `workspace`, sized by the matching *_workspace()
- * query for the same shapes on the same device.  Calls that report device
+ * query for the same shapes on the same device, 256-byte aligned (as returned
+ * by cudaMalloc or a caching allocator).  Calls that report device
  * status (scans, pair costs, the PDHG solve) synchronise `stream` before
  * returning.
  *
@@ -67,9 +68,14 @@ int hb_last_kernel_times(double* ms, int capacity);
  * missing slots (-inf, -1).  k in 0..32 (0: certificate only, outputs unused).
  * stats5 (device, 5 doubles): [sum max(s,0)^2, sum cost^2, max s+, max |cost|,
  * count s>0] over all q*n pairs; written when compute_stats != 0.
- * precision: 1 = one TF32 tensor-core product, 3 = 3xTF32 split (fp32-class).
- * min_groups: column groups per row block (0 = automatic).
+ * precision: 1 = one TF32 tensor-core product, 3 = 3xTF32 split (fp32-class),
+ * optionally OR HB_L2SQ_TWO_PASS.  For k <= 8 the scan makes one pass over the
+ * pairs (row lists in registers, column lists in the workspace); with the flag,
+ * or k > 8, it makes two passes with the clouds' roles exchanged.  Both give the
+ * same lists bit for bit (the certificate sums differ in summation order only).
+ * min_groups: column groups (0 = automatic).
  * ------------------------------------------------------------------------- */
+#define HB_L2SQ_TWO_PASS 0x10
 size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
 int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_cost,
                  const double* y_cost, const double* x_bias, const double* y_bias, int k, double dot_scale,

@@ -143,6 +143,39 @@ def test_l2sq_pass_symmetry(hb, cuda):
     assert ci[j, 0] == i and cv[j, 0] == rv[i, 0]
 
 
+# (q, n, d, k, min_groups): one row group, several row blocks per row group (q > 8 * 128),
+# ragged last blocks, k > rows, forced column groups, tf32
+ONE_PASS_CASES = [(37, 53, 8, 3, 0, "fp32"), (2048, 1500, 64, 4, 0, "fp32"), (3001, 777, 20, 8, 0, "fp32"),
+                  (5, 3, 4, 8, 0, "fp32"), (1300, 2600, 33, 1, 7, "fp32"), (2500, 900, 48, 2, 3, "tf32"),
+                  (4096, 4096, 256, 8, 0, "fp32")]
+
+
+@pytest.mark.parametrize("q,n,d,k,groups,precision", ONE_PASS_CASES)
+def test_l2sq_one_pass_equals_two_pass(hb, cuda, q, n, d, k, groups, precision):
+    """The one-pass scan (column lists kept per row group in the workspace) and the
+    two-pass scan (roles exchanged) report the same lists bit for bit: both insert
+    the same fp32 tensor-core dots with the same fp64 score arithmetic and tie rule.
+    The certificate differs only in the order of its fp32 partial sums."""
+    x, y, a, b, f, g = _cloud(q, n, d, seed=q + 3 * n + d)
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    args = (T(x, torch.float32), T(y, torch.float32), T(a, torch.float64), T(b, torch.float64),
+            T(f - a, torch.float64), T(g - b, torch.float64), k)
+    hb.set_kernel_timing(True)
+    try:
+        one = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups)]
+        assert len(hb.last_kernel_times()) == 1  # one scan kernel launch
+        two = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups, two_pass=True)]
+        assert len(hb.last_kernel_times()) == 2
+    finally:
+        hb.set_kernel_timing(False)
+    for u, v in zip(one[:4], two[:4]):
+        assert torch.equal(u, v)
+    s1, s2 = one[4].cpu().numpy(), two[4].cpu().numpy()
+    # maxima and the count are order-free; (a + b) - dot and (b + a) - dot agree in fp32
+    assert s1[2] == s2[2] and s1[3] == s2[3] and s1[4] == s2[4]
+    assert s1[0] == pytest.approx(s2[0], rel=4 * CERT_REL) and s1[1] == pytest.approx(s2[1], rel=4 * CERT_REL)
+
+
 NORM_CASES = [(41, 29, 3, 2), (64, 80, 20, 8), (129, 257, 1, 1), (300, 200, 128, 4), (1000, 1200, 3, 16),
               (5, 3, 2, 8), (513, 260, 9, 32)]
 
