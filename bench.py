@@ -47,8 +47,9 @@ sys.path.insert(0, str(REPO))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per pair of one pass-1 launch, from an ncu capture of the
 # scan kernel scaled by the pairs it processed (see profiles/ for the capture and command).
-# DRAM bytes per pair of the scan kernel from an ncu capture (profiles/l2sq_scan_kernel_c5_d256.md)
-DRAM_BYTES_PER_PAIR = {(256, "fp32", "two-pass"): 0.1357}
+# DRAM bytes (read + write) per pair of the scan kernel from ncu captures (profiles/l2sq_scan_kernel_c5_d256.md):
+# one-pass measured on the full C5 launch, two-pass (pass 1) on a 131072^2 launch
+DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 2.379, (256, "fp32", "two-pass"): 0.1357}
 
 
 def parse_args():
@@ -65,8 +66,8 @@ def parse_args():
     p.add_argument("--d", type=int, default=256)
     p.add_argument("--k", type=int, default=8)
     p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
-    p.add_argument("--two-pass", action="store_true",
-                   help="scan with two passes (roles exchanged) instead of the one-pass default for k <= 8")
+    p.add_argument("--passes", type=int, choices=[1, 2], default=None,
+                   help="force a one-pass (k <= 8) or two-pass scan (default: the library's choice)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
@@ -253,7 +254,10 @@ def run_reference(args):
 
 
 def scan_mode(args):
-    return "two-pass" if (args.two_pass or args.k > 8) else "one-pass"
+    if args.passes is not None:
+        return "one-pass" if args.passes == 1 else "two-pass"
+    one = args.k <= 8 and (args.d >= 128 or (args.d >= 64 and args.n >= 1 << 19))  # the library's rule
+    return "one-pass" if one else "two-pass"
 
 
 def workload_config(args):
@@ -288,7 +292,7 @@ def run_ours(args):
     if world > 1:  # the target cloud is replicated from rank 0 (once per solve)
         dist.broadcast(y, 0)
         dist.broadcast(b, 0)
-    sharded = ShardedPricingScan(precision=args.precision, two_pass=args.two_pass)
+    sharded = ShardedPricingScan(precision=args.precision, passes=args.passes)
     g_step = g.clone()
 
     def step():

@@ -79,6 +79,7 @@ struct Params {
     int* status;
     // one-pass mode: CTA b owns row group b / groups (rbg row blocks) x column group b % groups
     int rb, rbg;
+    int* progress;  // [grid] tiles started by each CTA (pacing of a column group's CTAs)
     int* ckey;     // [ct * BN] screening threshold of each column (ordered-int fp32 image), see below
     double* cval;  // [row groups * 4][n][K]
     int* cidx;
@@ -123,6 +124,26 @@ __device__ __forceinline__ Sched schedule(const Params& p) {
     return {rb0 * p.groups + g, p.groups, rb1 > rb0 ? rb1 * p.groups : 0};
 }
 
+// One pass: the CTAs of a column group (one per row group) stream the same
+// column tiles.  Each keeps within PACE tiles of the slowest of them, so a tile
+// one of them brings from HBM is still in L2 for the others; unpaced they
+// drift apart and every one of them reads the whole target cloud from HBM.
+// The wait is bounded (PACE_SPINS sleeps, then it proceeds): no CTA ever
+// depends on another one making progress.
+constexpr int PACE = 2, PACE_SPINS = 64;
+
+__device__ __forceinline__ void pace(const Params& p, int t) {
+    volatile int* prog = p.progress;
+    prog[blockIdx.x] = t;
+    const int g = blockIdx.x % p.groups, gr = gridDim.x / p.groups;
+    for (int spin = 0; spin < PACE_SPINS; ++spin) {
+        int slow = INT32_MAX;
+        for (int r = 0; r < gr; ++r) slow = min(slow, prog[r * p.groups + g]);
+        if (t - slow <= PACE) return;
+        __nanosleep(500);
+    }
+}
+
 template <bool ONE>
 __device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
     constexpr int STAGES = Smem<ONE>::STAGES, CSLOTS = Smem<ONE>::CS;
@@ -135,6 +156,7 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
         const int rb = u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
+            if (ONE) pace(p, (int)t);
             // the tile's column vectors (the slot was released CSLOTS tiles ago)
             const uint32_t cs = t % CSLOTS;
             if (!mbar_wait(&s.cempty[cs], ((t / CSLOTS) & 1) ^ 1, &s.abort, p.status)) return;
@@ -156,6 +178,7 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
             }
         }
     }
+    if (ONE) *(volatile int*)(p.progress + blockIdx.x) = INT32_MAX;  // done: never wait for this CTA
 }
 
 // Products per K step of 8: pass 1 (query = x): x*y, x*lo(y), lo(x)*y; pass 2
@@ -679,7 +702,14 @@ inline int l2sq_slices(int K) { return (K <= 8 ? 8 : 4) / 4; }
 // and their insertions small; each row group re-reads its column groups'
 // features once per row block, which costs HBM bandwidth (not the bound).
 constexpr int ONE_PASS_ROW_GROUPS = 8;
-inline bool use_one_pass(int K, int precision) { return K > 0 && K <= 8 && !(precision & HB_L2SQ_TWO_PASS); }
+// Automatic choice: the one-pass epilogue costs about the same per pair at any
+// d (list upkeep), the tensor-core work grows with d, and the column lists see
+// more rows (fewer insertions) as q grows.
+inline bool use_one_pass(int K, int precision, int64_t q, int64_t d) {
+    if (K < 1 || K > 8 || (precision & HB_L2SQ_TWO_PASS)) return false;
+    if (precision & HB_L2SQ_ONE_PASS) return true;
+    return d >= 128 || (d >= 64 && q >= (int64_t(1) << 19));
+}
 
 struct OnePlan {
     int rb, ct, gr, rbg, gc, tpg, grid;
@@ -705,6 +735,7 @@ struct L2sqLayout {
     double *pv1 = nullptr, *pv2 = nullptr, *cta = nullptr;
     int *pi1 = nullptr, *pi2 = nullptr, *status = nullptr;
     int* ckey = nullptr;  // one-pass column lists and thresholds
+    int* progress = nullptr;
     double *ybp = nullptr, *ycp = nullptr, *xbp = nullptr, *xcp = nullptr;  // padded column vectors
     double* cval = nullptr;
     int* cidx = nullptr;
@@ -736,7 +767,7 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     const int slices = K > 0 ? l2sq_slices(K) : 1;
     const size_t npad = (size_t)(n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     const size_t qpad = (size_t)(q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
-    L.one_pass = use_one_pass(K, precision);
+    L.one_pass = use_one_pass(K, precision, q, d);
     need(true, L.ybp, npad);
     need(true, L.ycp, npad);
     need(!L.one_pass && K > 0, L.xbp, qpad);
@@ -749,6 +780,7 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
         need(true, L.cval, lists * K);
         need(true, L.cidx, lists * K);
         need(true, L.ckey, npad);
+        need(true, L.progress, (size_t)L.one.grid);
         need(true, L.cta, (size_t)L.one.grid * 5);
     } else {
         // features wider than ~1k keep more column groups so the row-block slabs in flight fit in L2
@@ -824,6 +856,9 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         p.groups = o.gc; p.tpg = o.tpg; p.ct = o.ct; p.units = o.rb * o.gc;
         p.rb = o.rb; p.rbg = o.rbg;
         p.ckey = L.ckey; p.cval = L.cval; p.cidx = L.cidx;
+        p.progress = L.progress;
+        e = cudaMemsetAsync(L.progress, 0, sizeof(int) * o.grid, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
         if (!want_stats) p.d_cost = nullptr;  // the cost vector is staged only for the cost terms
         e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats>(K, p, o.grid, st)
                        : launch_one<0>(K, p, o.grid, st);

@@ -68,15 +68,15 @@ def _c(t):
     return t.contiguous()
 
 
-L2SQ_TWO_PASS = 0x10
+L2SQ_PASS_FLAGS = {None: 0, 2: 0x10, 1: 0x20}
 
 
 def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute_stats=True, precision="fp32",
-              min_groups=0, two_pass=False):
+              min_groups=0, passes=None):
     """Bidirectional ℓ2² scan on the tensor cores.
 
-    k <= 8 makes one pass over the pairs unless two_pass is set (both modes give
-    the same lists bit for bit).  Returns (row_vals q x k fp64, row_idx q x k int32,
+    passes: 1 (k <= 8 only), 2, or None to let the library choose; both give the
+    same lists bit for bit.  Returns (row_vals q x k fp64, row_idx q x k int32,
     col_vals n x k, col_idx n x k, stats [sum s+^2, sum c^2, max s+, max |c|, count]
     fp64 on the device)."""
     x, y = _c(x), _c(y)
@@ -84,8 +84,7 @@ def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute
     q, d = x.shape
     n = y.shape[0]
     prec = PRECISION[precision] if isinstance(precision, str) else int(precision)
-    if two_pass:
-        prec |= L2SQ_TWO_PASS
+    prec |= L2SQ_PASS_FLAGS[passes]
     L = lib()
     dev = x.device
     kk = int(k)

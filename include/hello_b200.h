@@ -69,13 +69,17 @@ int hb_last_kernel_times(double* ms, int capacity);
  * stats5 (device, 5 doubles): [sum max(s,0)^2, sum cost^2, max s+, max |cost|,
  * count s>0] over all q*n pairs; written when compute_stats != 0.
  * precision: 1 = one TF32 tensor-core product, 3 = 3xTF32 split (fp32-class),
- * optionally OR HB_L2SQ_TWO_PASS.  For k <= 8 the scan makes one pass over the
- * pairs (row lists in registers, column lists in the workspace); with the flag,
- * or k > 8, it makes two passes with the clouds' roles exchanged.  Both give the
- * same lists bit for bit (the certificate sums differ in summation order only).
+ * optionally OR one of HB_L2SQ_ONE_PASS / HB_L2SQ_TWO_PASS.  A one-pass scan
+ * (k <= 8) keeps row lists in registers and column lists in the workspace; a
+ * two-pass scan runs the row pass again with the clouds' roles exchanged.  Both
+ * give the same lists bit for bit (the certificate sums differ in summation
+ * order only).  Without a flag the scan picks one pass when k <= 8 and the
+ * tensor-core work per pair dominates the list upkeep (d >= 128, or d >= 64
+ * with q >= 2^19), else two.
  * min_groups: column groups (0 = automatic).
  * ------------------------------------------------------------------------- */
 #define HB_L2SQ_TWO_PASS 0x10
+#define HB_L2SQ_ONE_PASS 0x20
 size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
 int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_cost,
                  const double* y_cost, const double* x_bias, const double* y_bias, int k, double dot_scale,

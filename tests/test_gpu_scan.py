@@ -66,13 +66,13 @@ def _pad(v, i, width):
     return v, i
 
 
-def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0, min_clear=0.5):
+def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0, min_clear=0.5, passes=None):
     q, n = len(x), len(y)
     T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
     qb, dbb = f - a, g - b
     rv, ri, cv, ci, stats = hb.l2sq_scan(T(x, torch.float32), T(y, torch.float32), T(a, torch.float64),
                                          T(b, torch.float64), T(qb, torch.float64), T(dbb, torch.float64), k,
-                                         dot_scale=dot_scale, precision=precision)
+                                         dot_scale=dot_scale, precision=precision, passes=passes)
     rv, ri, cv, ci, stats = (t.cpu().numpy() for t in (rv, ri, cv, ci, stats))
     ev, ei, fv, fi, es = oracle.scan("raw", x, y, qb, dbb, a, b, dot_scale=dot_scale, rk=min(k + 1, n),
                                      ck=min(k + 1, q))
@@ -98,10 +98,13 @@ def _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision, dot_scale=2.0,
 
 @pytest.mark.parametrize("q,n,d,k", L2SQ_CASES)
 @pytest.mark.parametrize("precision", ["fp32", "tf32"])
-def test_l2sq_scan_matches_oracle(hb, cuda, oracle, q, n, d, k, precision):
+@pytest.mark.parametrize("passes", [1, 2])
+def test_l2sq_scan_matches_oracle(hb, cuda, oracle, q, n, d, k, precision, passes):
+    if passes == 1 and k > 8:
+        pytest.skip("the one-pass scan keeps k <= 8 column lists")
     x, y, a, b, f, g = _cloud(q, n, d, seed=q * 7 + n + d)
     _check_l2sq(hb, oracle, cuda, x, y, a, b, f, g, k, precision,
-                min_clear=0.5 if precision == "fp32" else 0.05)
+                min_clear=0.5 if precision == "fp32" else 0.05, passes=passes)
 
 
 @pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("scan_l2sq_*.npz")))
@@ -162,9 +165,9 @@ def test_l2sq_one_pass_equals_two_pass(hb, cuda, q, n, d, k, groups, precision):
             T(f - a, torch.float64), T(g - b, torch.float64), k)
     hb.set_kernel_timing(True)
     try:
-        one = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups)]
+        one = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups, passes=1)]
         assert len(hb.last_kernel_times()) == 1  # one scan kernel launch
-        two = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups, two_pass=True)]
+        two = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups, passes=2)]
         assert len(hb.last_kernel_times()) == 2
     finally:
         hb.set_kernel_timing(False)

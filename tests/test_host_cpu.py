@@ -87,3 +87,22 @@ def test_pdlp_validates_controls(hb):
         hb.NativeRestrictedOTPDLP(device="cpu")
     with pytest.raises(ValueError):
         hb.NativeRestrictedOTPDLP(device="cuda:0", evaluation_frequency=0)
+
+
+def test_l2sq_pass_flags_are_validated_before_launch(hb):
+    """Bad precision / pass-flag combinations are refused before any device work."""
+    lib = hb.load_library()
+    fake = 256  # never dereferenced: the argument checks come first
+    base = [fake, fake, 100, 100, 8, fake, fake, fake, fake]
+
+    def call(k, precision):
+        return lib.hb_l2sq_scan(*base, k, 2.0, 1, precision, 0, fake, fake, fake, fake, fake, fake, 1 << 20, None)
+
+    one, two = 0x20, 0x10
+    assert call(8, 2) == hb._lib.HB_BAD_ARGUMENT
+    assert "precision must be 1" in lib.hb_last_error().decode()
+    assert call(8, 3 | one | two) == hb._lib.HB_BAD_ARGUMENT
+    assert "exclusive" in lib.hb_last_error().decode()
+    assert call(16, 3 | one) == hb._lib.HB_BAD_ARGUMENT
+    assert "one-pass scan needs" in lib.hb_last_error().decode()
+    assert call(0, 1 | one) == hb._lib.HB_BAD_ARGUMENT
