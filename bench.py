@@ -52,18 +52,25 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 2.379, (256, "fp32", "two-pass"): 0.1357}
 
 
+# per-path default sizes: config 5 (m = n = 2^20, d = 256) for the l2sq scans, pair costs and
+# the PDHG; config 3 (n = m = 262144, d = 128) for the l1 scan
+PATH_SIZES = {"scan": (1_048_576, 256), "initial": (1_048_576, 256), "pairs": (1_048_576, 256),
+              "pdlp": (1_048_576, 256), "norm": (262_144, 128)}
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp"],
+    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial"],
                    help="scan (default, the headline): l2sq pricing scan; norm: l1 scan (config 3 shape); "
-                        "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations")
+                        "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations; "
+                        "initial: l2sq directional top-16 scan (config 5 shape)")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
-    p.add_argument("--n", type=int, default=1_048_576)
-    p.add_argument("--d", type=int, default=256)
+    p.add_argument("--n", type=int, default=None, help="points per side (default: the path's config)")
+    p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
     p.add_argument("--k", type=int, default=8)
     p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
     p.add_argument("--passes", type=int, choices=[1, 2], default=None,
@@ -71,7 +78,11 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    return p.parse_args()
+    args = p.parse_args()
+    n0, d0 = PATH_SIZES[args.path]
+    args.n = n0 if args.n is None else args.n
+    args.d = d0 if args.d is None else args.d
+    return args
 
 
 def load_peaks():
@@ -571,6 +582,39 @@ def run_norm(args, hb, dev, peaks):
           {"workload": f"l1 pricing scan, n=m={n}, d={d}, k={k}", "n": n, "d": d, "topk": k}, extra)
 
 
+def run_initial(args, hb, dev, peaks):
+    """ℓ2² directional (initial) scan: each source row's best kappa = 16 of (2<x,y> - a) + (g - b),
+    config 5 shape (m = n = 1,048,576, d = 256) unless --n/--d say otherwise."""
+    n, d, k = args.n, args.d, 16
+    x, y, a, b, f, g, med = make_workload(n, d, 42, dev, rows=(0, n))
+    qb, dbb = -a, g - b
+    hb.set_kernel_timing(True)
+    sec = _timed(lambda: hb.l2sq_topk(x, y, qb, dbb, k, dot_scale=2.0, precision=args.precision), args, dev)
+    kms = hb.last_kernel_times()
+    hb.set_kernel_timing(False)
+    peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
+    achieved = 2.0 * d * n * n / (kms[0] / 1e3) / 1e12 if kms else float("nan")
+    extra = {"dtype": "tf32x3/f64" if args.precision == "fp32" else "tf32/f64", "roofline": {
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+        "traffic": None, "kernel": "hb::l2sq::scan_kernel<16, 0, 0, 0> (row lists only)",
+        "peak_source": "measured bf16 dense (sustained)",
+        "note": "algorithmic flops 2*d per pair; 3xTF32 issues 3 tf32 products per pair at half the bf16 rate"}}
+    if not args.no_cpu:  # the reference's CPU directional scan is torch tiles + topk; the oracle port stands in
+        import oracle
+        rows = 32
+        xs, ys = x[:rows].cpu().numpy(), y.cpu().numpy()
+        t0 = time.perf_counter()
+        oracle.scan("raw", xs, ys, qb[:rows].cpu().numpy(), dbb.cpu().numpy(), a[:rows].cpu().numpy(),
+                    b.cpu().numpy(), dot_scale=2.0, rk=k, ck=0, threads=os.cpu_count() or 1)
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": rows * n / dt / 1e9, "unit": "Gpairs/s", "cores": os.cpu_count() or 1,
+                                 "kind": "port", "sample": f"{rows} source rows x {n} targets in {dt:.1f} s, "
+                                                           "oracle fp64 row scan"}
+    _line(args, "l2sq initial directional scan Gpairs/s (m·n)", n * n / sec / 1e9, "Gpairs/s", sec,
+          {"workload": f"l2sq directional top-{k} scan, n=m={n}, d={d}", "n": n, "d": d, "topk": k,
+           "median_pair_cost": med}, extra)
+
+
 def run_other(args):
     import __graft_entry__ as entry
 
@@ -578,7 +622,7 @@ def run_other(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks, _ = load_peaks()
-    {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm}[args.path](args, hb, dev, peaks)
+    {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm, "initial": run_initial}[args.path](args, hb, dev, peaks)
 
 
 def main():

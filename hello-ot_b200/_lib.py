@@ -19,7 +19,8 @@ HB_OK, HB_BAD_ARGUMENT, HB_BAD_INPUT, HB_WORKSPACE = 0, 1, 2, 3
 HB_CUDA, HB_TENSOR_MAP, HB_LAUNCH, HB_DEVICE_TIMEOUT = 4, 5, 6, 7
 
 EXPORTS = ("hb_abi_version", "hb_last_error", "hb_kernel_launch_count", "hb_set_kernel_timing",
-           "hb_last_kernel_times", "hb_l2sq_scan_workspace", "hb_l2sq_scan", "hb_norm_scan_workspace",
+           "hb_last_kernel_times", "hb_l2sq_scan_workspace", "hb_l2sq_scan", "hb_l2sq_topk_workspace",
+           "hb_l2sq_topk", "hb_norm_topk_workspace", "hb_norm_topk", "hb_norm_scan_workspace",
            "hb_norm_scan", "hb_norm_scan_noalloc", "hb_merge_topk", "hb_pair_costs_workspace", "hb_pair_costs", "hb_restricted_ot_workspace",
            "hb_restricted_ot_solve")
 
@@ -78,6 +79,14 @@ def load_library(path: Path | str = LIB_PATH):
     lib.hb_l2sq_scan.restype = c_int
     lib.hb_l2sq_scan.argtypes = [P, P, c_int64, c_int64, c_int64, P, P, P, P, c_int, c_double, c_int, c_int, c_int,
                                  P, P, P, P, P, P, c_size_t, P]
+    lib.hb_l2sq_topk_workspace.restype = c_size_t
+    lib.hb_l2sq_topk_workspace.argtypes = [c_int64, c_int64, c_int64, c_int, c_int]
+    lib.hb_l2sq_topk.restype = c_int
+    lib.hb_l2sq_topk.argtypes = [P, P, c_int64, c_int64, c_int64, P, P, c_int, c_double, c_int, P, P, P, c_size_t, P]
+    lib.hb_norm_topk_workspace.restype = c_size_t
+    lib.hb_norm_topk_workspace.argtypes = [c_int64, c_int64, c_int]
+    lib.hb_norm_topk.restype = c_int
+    lib.hb_norm_topk.argtypes = [P, P, c_int64, c_int64, c_int64, P, c_int, c_int, c_int, P, P, P, P, c_size_t, P]
     lib.hb_norm_scan_workspace.restype = c_size_t
     lib.hb_norm_scan_workspace.argtypes = [c_int64, c_int64, c_int]
     lib.hb_norm_scan.restype = c_int

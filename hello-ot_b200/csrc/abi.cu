@@ -168,6 +168,74 @@ int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     return finish(st, nullptr, "norm scan");
 }
 
+size_t hb_l2sq_topk_workspace(int64_t q, int64_t n, int64_t d, int k, int precision) {
+    if (q < 1 || n < 1 || d < 1 || k < 1 || k > 32) return 0;
+    return hb::l2sq_bytes(q, n, d, k, (precision & 0xF) | hb::L2SQ_ROWS_ONLY, 0);
+}
+
+int hb_l2sq_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_bias,
+                 const double* y_bias, int k, double dot_scale, int precision, double* row_vals, int32_t* row_idx,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+    if (!x || !y || !x_bias || !y_bias || !workspace) return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
+    if (!row_vals || !row_idx) return fail(HB_BAD_ARGUMENT, "null output pointer");
+    if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
+        return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
+    if (k < 1 || k > 32) return fail(HB_BAD_ARGUMENT, "k must be in 1..32");
+    if (dot_scale != 1.0 && dot_scale != 2.0) return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
+    if (precision != 1 && precision != 3) return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32)");
+    const int flags = precision | hb::L2SQ_ROWS_ONLY;
+    if (workspace_bytes < hb::l2sq_bytes(q, n, d, k, flags, 0))
+        return fail(HB_WORKSPACE, "workspace smaller than hb_l2sq_topk_workspace()");
+    if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(HB_BAD_ARGUMENT, "workspace must be 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::string err;
+    int status_host = 0;
+    int rc = hb::l2sq_scan(x, y, q, n, d, nullptr, nullptr, x_bias, y_bias, k, dot_scale, 0, flags, 0, row_vals,
+                           row_idx, nullptr, nullptr, nullptr, workspace, workspace_bytes, &status_host, st, err);
+    if (rc) return fail(rc == 3 ? HB_WORKSPACE : rc == 5 ? HB_TENSOR_MAP : HB_LAUNCH, err);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail(HB_CUDA, std::string("l2sq top-k: ") + cudaGetErrorString(e));
+    collect_timing();
+    if (status_host & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, "l2sq top-k: a device-side wait timed out");
+    g_error.clear();
+    return HB_OK;
+}
+
+// The norm top-k workspace is the norm scan's plus 64 bytes for the five certificate slots.
+size_t hb_norm_topk_workspace(int64_t q, int64_t n, int k) {
+    if (q < 1 || n < 1 || k < 1 || k > 32) return 0;
+    return ((hb::norm_bytes(q, n, k) + 7) & ~size_t(7)) + 64;
+}
+
+int hb_norm_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* g, int cost_type,
+                 int k, int compute_stats, double* row_vals, int32_t* row_idx, double* stats2, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+    if (!x || !y || !g || !workspace) return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
+    if (!row_vals || !row_idx) return fail(HB_BAD_ARGUMENT, "null output pointer");
+    if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
+        return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
+    if (cost_type < 0 || cost_type > 2) return fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2)");
+    if (k < 1 || k > 32) return fail(HB_BAD_ARGUMENT, "k must be in 1..32");
+    if (compute_stats && !stats2) return fail(HB_BAD_ARGUMENT, "null stats pointer");
+    if (workspace_bytes < hb_norm_topk_workspace(q, n, k))
+        return fail(HB_WORKSPACE, "workspace smaller than hb_norm_topk_workspace()");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    std::string err;
+    // the five certificate slots sit after the scan's scratch; [1] and [3] are the cost terms
+    double* stats5 = compute_stats ? reinterpret_cast<double*>(static_cast<char*>(workspace) +
+                                                              ((hb::norm_bytes(q, n, k) + 7) & ~size_t(7)))
+                                   : nullptr;
+    int rc = hb::norm_scan(x, y, q, n, d, nullptr, g, cost_type, k, compute_stats, row_vals, row_idx, nullptr, nullptr,
+                           stats5, workspace, workspace_bytes, st, err, true);
+    if (rc) return fail(rc == 3 ? HB_WORKSPACE : HB_LAUNCH, err);
+    if (compute_stats) {
+        cudaError_t e = cudaMemcpyAsync(stats2, stats5 + 1, sizeof(double), cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(stats2 + 1, stats5 + 3, sizeof(double), cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return fail(HB_CUDA, std::string("norm top-k: ") + cudaGetErrorString(e));
+    }
+    return finish(st, nullptr, "norm top-k");
+}
+
 int hb_merge_topk(const double* vals, const int32_t* idx, int parts, int64_t rows, int width, int k,
                   double* out_vals, int32_t* out_idx, void* stream) {
     if (!vals || !idx || !out_vals || !out_idx) return fail(HB_BAD_ARGUMENT, "null pointer");

@@ -17,18 +17,22 @@ int abi_fail(int code, const std::string& msg);
 int abi_finish(cudaStream_t st, const char* what);
 void timing_mark(cudaStream_t st);  // no-op unless timing is enabled on this thread
 
-// ℓ2² scan (scan_l2sq.cu)
+// ℓ2² scan (scan_l2sq.cu).  `precision` carries the public pass flags and, internally,
+// L2SQ_ROWS_ONLY: row lists only (no column lists, no certificate; the cost vectors
+// and column outputs may be null), the directional top-k.
+constexpr int L2SQ_ROWS_ONLY = 0x40;
 size_t l2sq_bytes(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
 int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* nx, const double* ny,
               const double* qb, const double* dbb, int k, double dot_scale, int want_stats, int precision,
               int min_groups, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws, size_t ws_bytes,
               int* status_out, cudaStream_t st, std::string& err);
 
-// norm scans (scan_norm.cu)
+// norm scans (scan_norm.cu).  f == nullptr: no query bias (the score is g - c
+// exactly); rows_only: no column lists (cv/ci unused).
 size_t norm_bytes(int64_t q, int64_t n, int k);
 int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
               int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
-              size_t ws_bytes, cudaStream_t st, std::string& err);
+              size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only = false);
 
 // partial top-k merge (scan_l2sq.cu): lists of `width` entries, bucket K >= width
 cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out,

@@ -706,7 +706,7 @@ constexpr int ONE_PASS_ROW_GROUPS = 8;
 // d (list upkeep), the tensor-core work grows with d, and the column lists see
 // more rows (fewer insertions) as q grows.
 inline bool use_one_pass(int K, int precision, int64_t q, int64_t d) {
-    if (K < 1 || K > 8 || (precision & HB_L2SQ_TWO_PASS)) return false;
+    if (K < 1 || K > 8 || (precision & (HB_L2SQ_TWO_PASS | L2SQ_ROWS_ONLY))) return false;
     if (precision & HB_L2SQ_ONE_PASS) return true;
     return d >= 128 || (d >= 64 && q >= (int64_t(1) << 19));
 }
@@ -768,10 +768,11 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     const size_t npad = (size_t)(n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     const size_t qpad = (size_t)(q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     L.one_pass = use_one_pass(K, precision, q, d);
+    const bool rows_only = (precision & L2SQ_ROWS_ONLY) != 0;
     need(true, L.ybp, npad);
-    need(true, L.ycp, npad);
-    need(!L.one_pass && K > 0, L.xbp, qpad);
-    need(!L.one_pass && K > 0, L.xcp, qpad);
+    need(!rows_only, L.ycp, npad);
+    need(!L.one_pass && !rows_only && K > 0, L.xbp, qpad);
+    need(!L.one_pass && !rows_only && K > 0, L.xcp, qpad);
     if (L.one_pass) {
         L.one = one_plan(q, n, sms, min_groups);
         const size_t lists = (size_t)L.one.gr * 4 * n;
@@ -789,8 +790,8 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
         L.p2 = scan_plan(n, q, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
         need(K > 0, L.pv1, (size_t)L.p1.groups * slices * q * K);
         need(K > 0, L.pi1, (size_t)L.p1.groups * slices * q * K);
-        need(K > 0, L.pv2, (size_t)L.p2.groups * slices * n * K);
-        need(K > 0, L.pi2, (size_t)L.p2.groups * slices * n * K);
+        need(K > 0 && !rows_only, L.pv2, (size_t)L.p2.groups * slices * n * K);
+        need(K > 0 && !rows_only, L.pi2, (size_t)L.p2.groups * slices * n * K);
         need(true, L.cta, (size_t)(L.p1.grid + L.p2.grid) * 5);
     }
     need(true, L.status, 1);
@@ -810,6 +811,8 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (!L.ok) { err = "workspace too small for the l2sq scan"; return 3; }
     const int K = k > 0 ? bucket_of(k) : 0;
     const int prec = precision & 0xF;
+    const bool rows_only = (precision & L2SQ_ROWS_ONLY) != 0;
+    if (rows_only) want_stats = 0;
     const int dp = (int)((d + 3) / 4 * 4);
     cudaError_t e = cudaMemsetAsync(L.status, 0, sizeof(int), st);
     if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
@@ -884,6 +887,8 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (K > 0) {
         e = merge_any(K, L.pv1, L.pi1, L.p1.groups * l2sq_slices(K), q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+    }
+    if (K > 0 && !rows_only) {
         // pass 2: y rows are the queries, same products in the same order;
         // the maps are rebuilt because a map fixes its box height (A 128 rows, B 256 rows)
         l2sq::Params p2 = p;

@@ -83,7 +83,8 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         const int row = rb * BM + er;
         const bool rvalid = row < p.q;
-        const double rbias = rvalid ? p.q_bias[row] : 0.0;
+        // no query bias: add -0.0, the exact identity (keeps g - c bit for bit, signed zeros included)
+        const double rbias = rvalid && p.q_bias ? p.q_bias[row] : -0.0;
         top.reset();
         for (int ct = g * p.tpg; ct < ct1; ++ct) {
             const int c0 = ct * BN;
@@ -289,7 +290,7 @@ size_t norm_bytes(int64_t q, int64_t n, int k) { return norm_layout(nullptr, 0, 
 
 int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
               int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
-              size_t ws_bytes, cudaStream_t st, std::string& err) {
+              size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only) {
     NormLayout L = norm_layout(ws, ws_bytes, q, n, k);
     if (!L.ok) { err = "workspace too small for the norm scan"; return 3; }
     const int K = k > 0 ? bucket_of(k) : 0;
@@ -305,6 +306,8 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (K > 0) {
         e = merge_any(K, L.pv1, L.pi1, L.p1.groups * 2, q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+    }
+    if (K > 0 && !rows_only) {
         norm::Params p2 = p;
         p2.x = y; p2.y = x; p2.q = (int)n; p2.n = (int)q;
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;

@@ -128,6 +128,46 @@ def norm_scan(x, y, f, g, k, cost_type, *, compute_stats=True):
     return rv[:, :kk], ri[:, :kk], cv[:, :kk], ci[:, :kk], stats
 
 
+def l2sq_topk(x, y, x_bias, y_bias, k, *, dot_scale=2.0, precision="fp32"):
+    """One-sided ℓ2² top-k on the tensor cores (the initial dual-assignment scan):
+    for every x row the best k of (fp32(s <x, y_j>) + x_bias) + y_bias_j, descending,
+    lower index on ties.  Returns (values q x k fp64, indices q x k int32)."""
+    x, y, x_bias, y_bias = map(_c, (x, y, x_bias, y_bias))
+    q, d = x.shape
+    n = y.shape[0]
+    prec = PRECISION[precision] if isinstance(precision, str) else int(precision)
+    L = lib()
+    dev = x.device
+    vals = torch.empty((q, int(k)), dtype=torch.float64, device=dev)
+    idx = torch.empty((q, int(k)), dtype=torch.int32, device=dev)
+    ws = Workspace.get(dev, L.hb_l2sq_topk_workspace(q, n, d, int(k), prec))
+    with torch.cuda.device(dev):
+        rc = L.hb_l2sq_topk(ptr(x), ptr(y), q, n, d, ptr(x_bias), ptr(y_bias), int(k), float(dot_scale), prec,
+                            ptr(vals), ptr(idx), ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc)
+    return vals, idx
+
+
+def norm_topk(x, y, g, k, cost_type, *, compute_stats=False):
+    """One-sided ℓ1/ℓ∞/ℓ2 top-k on the CUDA cores: for every x row the best k of
+    g_j - c_ij (fp64 score of the fp32 distance), descending, lower index on ties.
+    Returns (scores q x k fp64, indices q x k int32, stats [sum c^2, max |c|] or None)."""
+    x, y, g = map(_c, (x, y, g))
+    q, d = x.shape
+    n = y.shape[0]
+    L = lib()
+    dev = x.device
+    vals = torch.empty((q, int(k)), dtype=torch.float64, device=dev)
+    idx = torch.empty((q, int(k)), dtype=torch.int32, device=dev)
+    stats = torch.zeros(2, dtype=torch.float64, device=dev) if compute_stats else None
+    ws = Workspace.get(dev, L.hb_norm_topk_workspace(q, n, int(k)))
+    with torch.cuda.device(dev):
+        rc = L.hb_norm_topk(ptr(x), ptr(y), q, n, d, ptr(g), NORM_KIND[cost_type], int(k), int(bool(compute_stats)),
+                            ptr(vals), ptr(idx), ptr(stats), ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc)
+    return vals, idx, stats
+
+
 def _no_perturbation(sigma, query_global_index=None, database_global_index=None):
     if sigma is not None and float(sigma) != 0.0:
         raise NotImplementedError("hello_ot_b200 does not implement cost perturbation (sigma > 0); "
@@ -171,6 +211,42 @@ class ScanExtension:
         if not compute_stats:
             stats.zero_()
         return [rv, ri, cv, ci, stats, torch.zeros(4, dtype=torch.float64, device="cpu")]
+
+    def initialization_directional_topk_raw(self, query_feat, db_feat, query_bias, db_bias, query_tile, db_tile, k,
+                                            dot_scale):
+        """[values q x k fp64 descending, indices q x k int32] of (dot + query_bias) + db_bias
+        (generic_scan.py:560-575, cost.cu:248-348)."""
+        x, y, qb, dbb = query_feat, db_feat, query_bias, db_bias
+        if x.dtype != y.dtype:
+            raise RuntimeError("query/db feature dtypes must match")
+        _check(x, y, k, (qb, len(x)), (dbb, len(y)))
+        if query_tile <= 0 or db_tile <= 0 or dot_scale not in (1., 2.):
+            raise ValueError("invalid raw directional tile or scale")
+        self._record("raw_initial")
+        values, ids = l2sq_topk(x, y, qb, dbb, k, dot_scale=dot_scale, precision=self.precision)
+        return [values, ids]
+
+    def fused_directional_topk_raw(self, query_feat, db_feat, query_bias, db_bias, query_tile, db_tile, k, dot_scale):
+        """Compatibility name of initialization_directional_topk_raw (generic_scan.py:512-518)."""
+        self._record("raw_directional")
+        return self.initialization_directional_topk_raw(query_feat, db_feat, query_bias, db_bias, query_tile, db_tile,
+                                                        k, dot_scale)
+
+    def fused_gcost_topk(self, query, db, dual_db, k, cost_type, query_global_index=None, database_global_index=None,
+                         sigma=0., seed=0, perturb_mode=1, row_is_source=True, index_hash_coeffs=None,
+                         compute_precision=0, collect_statistics=False):
+        """[values q x k ascending c - g, indices int64 (, stats [sum c^2, max |c|])]
+        (generic_scan.py:520-531 -> directional(minimum=True), initial.cu:34-107)."""
+        _no_perturbation(sigma)
+        if compute_precision not in (0,):
+            raise NotImplementedError("hello_ot_b200 norm scans compute fp32 distances (compute_precision=0)")
+        _check(query, db, k, (dual_db, len(db)))
+        self._record("norm_initial")
+        scores, ids, stats = norm_topk(query, db, dual_db, k, cost_type, compute_stats=bool(collect_statistics))
+        out = [scores.neg_(), ids.long()]
+        if collect_statistics:
+            out.append(stats)
+        return out
 
     def raw_lowrank_stats_only(self, x, y, nx, ny, f, g, query_tile, db_tile, dot_scale):
         """Certificate of the bilinear scan without candidates (generic_scan.py:502-510):

@@ -88,6 +88,42 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
                  void* stream);
 
 /* ---------------------------------------------------------------------------
+ * ℓ2² directional top-k (one side only: the initial dual-assignment scan).
+ *
+ * Replaces ScanExtension.initialization_directional_topk_raw and its alias
+ * fused_directional_topk_raw (src/hello_ot/kernels/generic_scan.py:512-518,
+ * 560-575) and the kernel behind them, raw_initial
+ * (src/hello_ot/_native/generic_scan/cost.cu:248-348).
+ *
+ * For every x row the best k (score, j), score = (fp32(dot_scale <x_i, y_j>)
+ * + x_bias_i) + y_bias_j in fp64, descending, lower index on ties, missing
+ * slots (-inf, -1); k in 1..32.  Same kernel and arithmetic as the row side of
+ * hb_l2sq_scan, without the column lists and the certificate.
+ * ------------------------------------------------------------------------- */
+size_t hb_l2sq_topk_workspace(int64_t q, int64_t n, int64_t d, int k, int precision);
+int hb_l2sq_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_bias,
+                 const double* y_bias, int k, double dot_scale, int precision, double* row_vals, int32_t* row_idx,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * ℓ1 / ℓ∞ / ℓ2 directional top-k (the initial c-transform scan).
+ *
+ * Replaces ScanExtension.fused_gcost_topk (src/hello_ot/kernels/generic_scan.py:520-531)
+ * -> directional(minimum=True) (:219-306) and its kernels, queue_kernel
+ * (src/hello_ot/_native/generic_scan/initial.cu:34-107).
+ *
+ * For every x row the best k (score, j) with score = g_j - c_ij (fp64, c_ij the
+ * fp32 distance), descending, lower index on ties, missing slots (-inf, -1);
+ * the reference reports the values negated (c_ij - g_j ascending), which the
+ * host layer does.  stats2 (device, 2 doubles, when compute_stats != 0):
+ * [sum c^2, max |c|] over all q*n pairs.  k in 1..32.
+ * ------------------------------------------------------------------------- */
+size_t hb_norm_topk_workspace(int64_t q, int64_t n, int k);
+int hb_norm_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* g, int cost_type,
+                 int k, int compute_stats, double* row_vals, int32_t* row_idx, double* stats2, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * ℓ1 / ℓ∞ / ℓ2 full-space pricing scan (CUDA cores), bidirectional top-k +
  * certificate.  cost_type: 0 l1, 1 linf, 2 l2.
  *

@@ -18,6 +18,8 @@ Reference entry points recorded:
                (src/hello_ot/kernels/torch_scan.py:337)
   * PDLP:      CppRestrictedOTPDLP / TorchRestrictedOTPDLP
                (src/hello_ot/_internal/lp/{cpp,torch}_restricted_ot.py)
+  * directional (initial) scans: hello_ot.kernels.torch_scan.directional_assignment
+               (src/hello_ot/kernels/torch_scan.py:165-291), known side = target
   * pair costs: hello_ot.costs.pairs._cost_pairs_lowrank_batched (CPU branch,
                src/hello_ot/costs/pairs.py:296-307) and
                hello_ot.costs.metric.pair_costs_metric(compute_precision="fp64")
@@ -41,7 +43,7 @@ import torch  # noqa: E402
 torch.set_num_threads(1)
 
 from hello_ot.kernels.cpp_scan import cpp_violation_scan, fused_dot_tile  # noqa: E402
-from hello_ot.kernels.torch_scan import bidirectional_violation_scan  # noqa: E402
+from hello_ot.kernels.torch_scan import bidirectional_violation_scan, directional_assignment  # noqa: E402
 from hello_ot._internal.lp.cpp_restricted_ot import CppRestrictedOTPDLP  # noqa: E402
 from hello_ot._internal.lp.torch_restricted_ot import TorchRestrictedOTPDLP  # noqa: E402
 from hello_ot.costs.pairs import _cost_pairs_lowrank_batched  # noqa: E402
@@ -118,6 +120,36 @@ def norm_case(name, cost, q, n, d, k, seed):
                         dual_feasibility=res.dual_feasibility)
 
 
+DIRECTIONAL = [  # (name, family, cost, q, n, d, k, seed)
+    ("l2sq_a", "inner_product", "lowrank", 70, 90, 12, 8, 41),
+    ("l2sq_b", "inner_product", "lowrank", 33, 20, 40, 32, 42),   # k > n
+    ("l1_a", "norm_cost", "l1", 64, 75, 3, 16, 43),
+    ("l2_a", "norm_cost", "l2", 50, 41, 9, 4, 44),
+    ("linf_a", "norm_cost", "linf", 48, 66, 2, 1, 45),
+]
+
+
+def directional_case(name, family, cost, q, n, d, k, seed):
+    """Known side = target: each source row's best k of g_j - c_ij (the reference keeps
+    the candidate pairs and the top-1 value / index of each row)."""
+    from types import SimpleNamespace
+    rng = np.random.default_rng(seed)
+    x, y = _points(rng, q, n, d)
+    a = np.sum(x.astype(np.float64) ** 2, axis=1)
+    b = np.sum(y.astype(np.float64) ** 2, axis=1)
+    g = rng.normal(size=n) * (float(np.median(a)) if family == "inner_product" else 2.0)
+    f = np.zeros(q)
+    state = SimpleNamespace(rows=np.zeros(0, np.int32), cols=np.zeros(0, np.int32), x_prev=np.zeros(0),
+                            dual_uv=np.concatenate([f, g]), n_source=q, n_target=n)
+    aug, _, _, cand = directional_assignment(
+        state=state, source_points=x, target_points=y,
+        source_offset=a if family == "inner_product" else None, target_offset=b if family == "inner_product" else None,
+        score_family=family, cost_type=cost, dot_scale=2.0, known_side="target", topk=k, device="cpu")
+    np.savez_compressed(HERE / f"directional_{name}.npz", family=family, cost=cost, x=x, y=y, a=a, b=b, g=g, k=k,
+                        rows=np.asarray(aug.rows, np.int64), cols=np.asarray(aug.cols, np.int64),
+                        top1_values=cand.values.numpy(), top1_indices=cand.indices.numpy())
+
+
 def pdlp_cases():
     cases = []
     rng = np.random.default_rng(12)
@@ -183,6 +215,8 @@ if __name__ == "__main__":
         l2sq_case(*case)
     for case in SCAN_NORM:
         norm_case(*case)
+    for case in DIRECTIONAL:
+        directional_case(*case)
     pdlp_cases()
     pairs_cases()
     print("fixtures written to", HERE)

@@ -30,7 +30,8 @@ def test_library_exports_every_declared_symbol(hb):
 def test_header_cites_reference_interfaces():
     header = (REPO / "include" / "hello_b200.h").read_text()
     for cite in ("generic_scan.py:577-597", "generic_scan.py:533-558", "pairs.py:221-440",
-                 "norm_cost_scan_kernel.cu:249-275", "restricted_ot_pdlp.py:39-100", "solver.cpp:39-381"):
+                 "norm_cost_scan_kernel.cu:249-275", "restricted_ot_pdlp.py:39-100", "solver.cpp:39-381",
+                 "generic_scan.py:520-531", "initial.cu:34-107", "cost.cu:248-348"):
         assert cite in header
 
 

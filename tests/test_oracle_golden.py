@@ -113,3 +113,43 @@ def test_pair_costs_oracle_matches_reference(oracle, path):
     for kind in ("l1", "l2", "linf"):
         got = oracle.pair_costs(kind, x, y, rows, cols)
         np.testing.assert_allclose(got, z[kind], rtol=1e-13, atol=0)
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("directional_*.npz")))
+def test_directional_oracle_matches_reference(oracle, path):
+    """The reference's directional assignment (known side = target): each source row's
+    best k of g_j - c_ij.  The oracle's row lists (no source bias) give the same pairs
+    except inside the fp32 error band, and the same top-1 scores within it."""
+    z = _load(path)
+    x, y, g, k = z["x"], z["y"], z["g"], int(z["k"])
+    q, n = len(x), len(y)
+    rk = min(k, n)
+    if str(z["family"]) == "inner_product":
+        a, b = z["a"], z["b"]
+        rowb, colb, kind = -a, g - b, "raw"
+        rv, ri, _, _, _ = oracle.scan(kind, x, y, rowb, colb, a, b, dot_scale=2.0, rk=min(rk + 1, n), ck=0)
+        score = lambda r, c: oracle.pair_scores(kind, x, y, rowb, colb, a, b, r, c, dot_scale=2.0)[0]  # noqa: E731
+        # the reference evaluates g - ((a + b) - 2 fp32(x y^T)): fp32 dot error plus fp64 rounding
+        bound = lambda r, c: l2sq_error_bound(x, y, r, c, 2.0, (a[r], b[c], g[c])) + 1e-12 * (a[r] + b[c])  # noqa: E731
+    else:
+        kind = str(z["cost"])
+        rowb, colb = np.full(q, -0.0), g
+        rv, ri, _, _, _ = oracle.scan(kind, x, y, rowb, colb, rk=min(rk + 1, n), ck=0, exact=False)
+        score = lambda r, c: oracle.pair_scores(kind, x, y, rowb, colb, None, None, r, c)[0]  # noqa: E731
+        bound = lambda r, c: norm_error_bound(kind, x, y, r, c, rowb, colb)  # noqa: E731
+    # top-1 value and index of every row
+    r_all = np.arange(q)
+    e1 = bound(r_all, z["top1_indices"])
+    assert np.all(np.abs(rv[:, 0] - z["top1_values"]) <= 2 * e1 + 1e-300)
+    same = ri[:, 0] == z["top1_indices"]
+    gap = rv[:, 0] - (rv[:, 1] if rv.shape[1] > 1 else -np.inf)
+    assert np.all(same | (gap <= 2 * e1)), f"{path}: top-1 index differs outside the error band"
+    # the candidate pairs: each row's top-k set
+    ref = set(zip(z["rows"].tolist(), z["cols"].tolist()))
+    ours = {(r, int(c)) for r in range(q) for c in ri[r, :rk] if c >= 0}
+    diff = np.array(sorted(ours ^ ref), dtype=np.int64).reshape(-1, 2)
+    if diff.size:
+        s = score(diff[:, 0], diff[:, 1])
+        e = bound(diff[:, 0], diff[:, 1])
+        kth = rv[diff[:, 0], rk - 1]
+        assert np.all(np.abs(s - kth) <= 2 * e + 1e-300), f"{path}: candidate differences outside the error band"
