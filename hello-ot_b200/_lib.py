@@ -36,7 +36,8 @@ class HBError(RuntimeError):
 class PdlpControls(ctypes.Structure):
     _fields_ = [("evaluation_frequency", c_int32), ("scalar_rescaling", c_int32), ("iteration_limit", c_int64),
                 ("time_limit_seconds", c_double), ("tol_objective", c_double), ("tol_primal", c_double),
-                ("tol_dual", c_double), ("initial_primal_weight", c_double)]
+                ("tol_dual", c_double), ("initial_primal_weight", c_double), ("atomic_sums", c_int32),
+                ("pad", c_int32)]
 
 
 class PdlpInfo(ctypes.Structure):

@@ -294,6 +294,7 @@ int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const doubl
     ctl.tol_dual = controls->tol_dual;
     ctl.rescale = controls->scalar_rescaling;
     ctl.weight0 = controls->initial_primal_weight;
+    ctl.atomic = controls->atomic_sums != 0;
     hb::PdlpResult r{};
     static_assert(sizeof(hb::TraceRow) == sizeof(hb_pdlp_trace_row), "trace row layout");
     int tlen = 0;
@@ -302,6 +303,7 @@ int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const doubl
                             reinterpret_cast<hb::TraceRow*>(trace), trace ? trace_capacity : 0, &tlen, workspace,
                             workspace_bytes, static_cast<cudaStream_t>(stream), err);
     if (rc) return fail(rc == 2 ? HB_BAD_INPUT : rc == 3 ? HB_WORKSPACE : HB_CUDA, err);
+    collect_timing();  // the solve synchronised its stream before returning
     info->iterations = r.iterations;
     info->restarts = r.restarts;
     info->termination = r.reason;

@@ -53,6 +53,7 @@ struct PdlpControls {
     double tol_objective, tol_primal, tol_dual;
     int rescale;
     double weight0;  // > 0: initial primal weight instead of the norm ratio
+    int atomic;      // node sums by atomics in the edge pass (order varies run to run)
 };
 struct PdlpResult {
     int64_t iterations, restarts;

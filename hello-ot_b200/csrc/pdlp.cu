@@ -49,6 +49,7 @@ struct Dev {
     double *cost, *cs, *ax, *x, *px, *rx, *dx;  // per sorted edge
     double *mass, *scale, *bs, *ns, *ay, *y, *py, *dy, *td;
     double* sd;     // [n] source dual / node scale, the value every edge of the row uses
+    double *ssum, *tsum;  // [n], [m] node sums of the reflected primal (atomic mode; zero between passes)
     double* red;    // [RED_BLOCKS][8]
     double* scal;   // [16] reduced scalars
     int* status;
@@ -167,48 +168,103 @@ struct Step {
 // One PDHG iteration runs as three kernels (solver.cpp:255-281):
 //  edge_pass   : thread per edge, primal update, reflection, Halpern averaging
 //                (coalesced over the source-sorted edges, perfectly balanced);
-//  source_pass : thread per source row, ordered sum of its reflected primal and
-//                the source dual update;
+//  source_pass : warp per 32 source rows (coalesced staging), ordered sum of
+//                each row's reflected primal and the source dual update;
 //  target_pass : thread per target, ordered gather-sum and the target dual update.
 // Each node sums its edges sequentially in the reference's edge order.
+template <bool ATOMIC>
 __global__ void __launch_bounds__(256) edge_pass(Dev D, Step s) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
-        const double at = D.sd[D.e_row[p]] + D.td[D.e_col[p]];
-        const double xv = D.x[p];
-        const double pxv = max0(xv - s.primal_step * (D.cs[p] - at));
-        const double r = 2.0 * pxv - xv;
-        if (s.checkpoint) D.dx[p] = r - xv;
-        D.x[p] = s.halpern * r + (1.0 - s.halpern) * D.ax[p];
-        D.rx[p] = r;
-        if (s.major) D.px[p] = pxv;
+    const int lane = threadIdx.x & 31;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < D.e; base += stride) {  // block-uniform
+        const int64_t p = base + threadIdx.x;
+        const bool live = p < D.e;
+        double r = 0.0;
+        int row = -1;
+        if (live) {
+            row = D.e_row[p];
+            const int col = D.e_col[p];
+            const double at = D.sd[row] + D.td[col];
+            const double xv = D.x[p];
+            const double pxv = max0(xv - s.primal_step * (D.cs[p] - at));
+            r = 2.0 * pxv - xv;
+            if (s.checkpoint) D.dx[p] = r - xv;
+            D.x[p] = s.halpern * r + (1.0 - s.halpern) * D.ax[p];
+            if (s.major) D.px[p] = pxv;
+            if (ATOMIC) atomicAdd(D.tsum + col, r);
+            else D.rx[p] = r;
+        }
+        if (ATOMIC) {
+            // the warp's edges are sorted by source: suffix sums within each run of one
+            // source (a lane adds lane+off only inside its run), then one atomic per run
+            double v = r;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const double vo = __shfl_down_sync(0xffffffffu, v, off);
+                const int ro = __shfl_down_sync(0xffffffffu, row, off);
+                if (lane + off < 32 && ro == row) v += vo;
+            }
+            const int prev = __shfl_up_sync(0xffffffffu, row, 1);
+            if (live && (lane == 0 || prev != row)) atomicAdd(D.ssum + row, v);
+        }
     }
 }
 
+// Sums of the segments [off[v], off[v+1]) of `vals` for the 32 consecutive nodes
+// v = v0 + lane of a warp, each in index order.  The warp's whole range is staged
+// through shared memory in coalesced chunks; every lane then adds its own
+// node's values of the chunk.  All lanes take the same loop (warp-uniform).
+constexpr int SEG_CHUNK = 256;
+__device__ __forceinline__ double warp_segment_sum(const double* __restrict__ vals, const int* __restrict__ off,
+                                                   int v0, int nodes, double* stage) {
+    const int lane = threadIdx.x & 31, v = v0 + lane;
+    const int w0 = off[v0], w1 = off[min(v0 + 32, nodes)];
+    const int b0 = v < nodes ? off[v] : w1, b1 = v < nodes ? off[v + 1] : w1;
+    double sum = 0.0;
+    for (int c0 = w0; c0 < w1; c0 += SEG_CHUNK) {
+        const int c1 = min(w1, c0 + SEG_CHUNK);
+        for (int i = c0 + lane; i < c1; i += 32) stage[i - c0] = __ldg(vals + i);
+        __syncwarp();
+        const int lo = max(b0, c0), hi = min(b1, c1);
+        for (int q = lo; q < hi; ++q) sum += stage[q - c0];
+        __syncwarp();
+    }
+    return sum;
+}
+
+template <bool ATOMIC>
 __global__ void __launch_bounds__(256) source_pass(Dev D, Step s) {
-    const int stride = gridDim.x * blockDim.x;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D.n; i += stride) {
-        const int b0 = D.s_off[i], b1 = D.s_off[i + 1];
-        double sum = 0.0;
-        const double* rx = D.rx;
-#pragma unroll 4
-        for (int p = b0; p < b1; ++p) sum += __ldg(rx + p);
-        const double yv = D.y[i];
-        const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
-        const double refl = 2.0 * pyv - yv;
-        if (s.checkpoint) D.dy[i] = refl - yv;
-        const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
-        D.y[i] = ynew;
-        D.sd[i] = ynew / D.ns[i];
-        if (s.major) D.py[i] = pyv;
+    __shared__ double stage[ATOMIC ? 1 : 8][ATOMIC ? 1 : SEG_CHUNK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int v0 = (blockIdx.x * 8 + warp) * 32;
+    if (v0 >= D.n) return;  // warp-uniform
+    double sum;
+    if (ATOMIC) {
+        const int i = v0 + lane;
+        sum = i < D.n ? D.ssum[i] : 0.0;
+        if (i < D.n) D.ssum[i] = 0.0;
+    } else {
+        sum = warp_segment_sum(D.rx, D.s_off, v0, D.n, stage[warp]);
     }
+    const int i = v0 + lane;
+    if (i >= D.n) return;
+    const double yv = D.y[i];
+    const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+    const double refl = 2.0 * pyv - yv;
+    if (s.checkpoint) D.dy[i] = refl - yv;
+    const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+    D.y[i] = ynew;
+    D.sd[i] = ynew / D.ns[i];
+    if (s.major) D.py[i] = pyv;
 }
 
+template <bool ATOMIC>
 __global__ void __launch_bounds__(256) target_pass(Dev D, Step s) {
     const int stride = gridDim.x * blockDim.x;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < D.m; j += stride) {
-        const int b0 = D.t_off[j], b1 = D.t_off[j + 1];
+        const int b0 = ATOMIC ? 0 : D.t_off[j], b1 = ATOMIC ? 0 : D.t_off[j + 1];
         double sum = 0.0;
+        if (ATOMIC) { sum = D.tsum[j]; D.tsum[j] = 0.0; }
         int sl = b0;
         for (; sl + 4 <= b1; sl += 4) {  // four independent gathers in flight, summed in order
             const double r0 = D.rx[D.t_pos[sl]], r1 = D.rx[D.t_pos[sl + 1]];
@@ -358,7 +414,7 @@ PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e)
     take_d(D.cost, e); take_d(D.cs, e); take_d(D.ax, e); take_d(D.x, e); take_d(D.px, e); take_d(D.rx, e);
     take_d(D.dx, e);
     take_d(D.mass, nodes); take_d(D.scale, nodes); take_d(D.bs, nodes); take_d(D.ns, nodes); take_d(D.ay, nodes);
-    take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m); take_d(D.sd, n);
+    take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m); take_d(D.sd, n); take_d(D.ssum, n); take_d(D.tsum, m);
     take_d(D.red, (size_t)pdlp::RED_BLOCKS * 8); take_d(D.scal, 16);
     take_i(D.status, 1);
     take_i(L.r32, e); take_i(L.c32, e); take_i(L.iota, e); take_i(L.keys_out, e); take_i(L.t_orig, e);
@@ -403,6 +459,8 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         return 6;
     };
     cudaMemsetAsync(D.status, 0, sizeof(int), st);
+    cudaMemsetAsync(D.ssum, 0, sizeof(double) * n, st);
+    cudaMemsetAsync(D.tsum, 0, sizeof(double) * m, st);
     // --- incidence structure (solver.cpp:74-90): sort by source, then by target
     pdlp::check_convert<<<gb, 256, 0, st>>>(rows, cols, e, (int)n, (int)m, L.r32, L.c32, D.status);
     HB_LAUNCHED(1);
@@ -544,11 +602,16 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             s.major = ((count + 1) % F) == 0;
             const bool is_restart = t == 0 && restart;
             s.checkpoint = s.major || is_restart;
-            pdlp::edge_pass<<<gb, 256, 0, st>>>(D, s);
-            HB_LAUNCHED(1);
-            pdlp::source_pass<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(D, s);
-            HB_LAUNCHED(1);
-            pdlp::target_pass<<<(unsigned)((m + 255) / 256), 256, 0, st>>>(D, s);
+            if (ctl.atomic) {
+                pdlp::edge_pass<true><<<gb, 256, 0, st>>>(D, s);
+                pdlp::source_pass<true><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(D, s);
+                pdlp::target_pass<true><<<(unsigned)((m + 255) / 256), 256, 0, st>>>(D, s);
+            } else {
+                pdlp::edge_pass<false><<<gb, 256, 0, st>>>(D, s);
+                pdlp::source_pass<false><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(D, s);
+                pdlp::target_pass<false><<<(unsigned)((m + 255) / 256), 256, 0, st>>>(D, s);
+            }
+            HB_LAUNCHED(2);
             HB_LAUNCHED(1);
             if (s.checkpoint) {
                 pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);

@@ -52,7 +52,10 @@ class NativeRestrictedOTPDLP:
 
     def __init__(self, *, device="cuda", evaluation_frequency: int = 200, time_limit_seconds: float = 3600.0,
                  iteration_limit: int = np.iinfo(np.int32).max, record_state_trace: bool = False,
-                 initial_primal_weight: float = 0.0):
+                 initial_primal_weight: float = 0.0, deterministic: bool = True):
+        """deterministic=False accumulates the node sums with atomics in the edge pass:
+        about 1.5x faster per iteration on large random supports, but the summation
+        order (so the last bits of the iterates) varies from run to run."""
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("NativeRestrictedOTPDLP runs on CUDA devices only")
@@ -63,6 +66,7 @@ class NativeRestrictedOTPDLP:
         self.iteration_limit = int(iteration_limit)
         self.record_state_trace = bool(record_state_trace)
         self.initial_primal_weight = float(initial_primal_weight)
+        self.deterministic = bool(deterministic)
         if self.evaluation_frequency < 1:
             raise ValueError("evaluation_frequency must be >= 1")
         if self.time_limit_seconds <= 0.0 or self.iteration_limit < 1:
@@ -118,7 +122,7 @@ class NativeRestrictedOTPDLP:
         y_out = torch.empty(n + m, dtype=torch.float64, device=dev)
         ctl = PdlpControls(self.evaluation_frequency, int(bool(scalar_rescaling)), self.iteration_limit,
                            self.time_limit_seconds, objective_tolerance, primal_tolerance, dual_tolerance,
-                           self.initial_primal_weight)
+                           self.initial_primal_weight, int(not self.deterministic), 0)
         info = PdlpInfo()
         cap = 4096 if self.record_state_trace else 0
         trace = (PdlpTraceRow * max(cap, 1))()

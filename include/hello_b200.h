@@ -211,6 +211,10 @@ typedef struct hb_pdlp_controls {
     double time_limit_seconds;
     double tol_objective, tol_primal, tol_dual;
     double initial_primal_weight;  /* > 0 overrides the initial norm-ratio weight */
+    int32_t atomic_sums;           /* 1: node sums accumulated with atomics in the edge pass (faster; the
+                                      summation order, so the last bits, vary from run to run);
+                                      0: ordered sums, the reference's order, bit-reproducible */
+    int32_t pad;
 } hb_pdlp_controls;
 
 enum { HB_PDLP_OPTIMAL = 1, HB_PDLP_ITERATION_LIMIT = 2, HB_PDLP_NUMERICAL_DIVERGENCE = 3, HB_PDLP_TIME_LIMIT = 4 };

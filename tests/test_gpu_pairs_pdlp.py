@@ -94,6 +94,27 @@ def test_pdlp_converges_like_oracle(hb, cuda, oracle, shape):
     assert abs(got.iterations - ref["iterations"]) <= 2 * 200
 
 
+@pytest.mark.parametrize("shape", [(30, 40, 180), (1000, 700, 20000), (3000, 2500, 60000)])
+def test_pdlp_atomic_sums_converge_like_oracle(hb, cuda, oracle, shape):
+    """Atomic node sums change the summation order (so the last bits) but not the solve:
+    same termination, objective within the tolerance, and one block of iterations
+    within round-off of the ordered sums."""
+    rows, cols, c, a, b = _random_support(*shape, seed=shape[0] + 7)
+    ref = oracle.pdlp(rows, cols, c, a, b, frequency=200, tolerance=1e-7)
+    got = hb.NativeRestrictedOTPDLP(device=cuda, deterministic=False).solve_restricted(
+        rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=1e-7)
+    assert ref["termination_reason"] == got.termination_reason == "OPTIMAL"
+    assert got.obj_val == pytest.approx(ref["obj_val"], rel=1e-6)
+    assert got.primal_feas < 1e-7 and got.dual_feas < 1e-7 and got.gap < 1e-7
+    F = 60
+    blk = oracle.pdlp(rows, cols, c, a, b, frequency=F, iteration_limit=F, tolerance=0.0)
+    fast = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=F, iteration_limit=F, deterministic=False,
+                                     initial_primal_weight=blk["primal_weight"])
+    out = fast.solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=0.0)
+    np.testing.assert_allclose(out.x.cpu().numpy(), blk["x"], rtol=1e-9, atol=1e-12 * np.abs(blk["x"]).max())
+    np.testing.assert_allclose(out.y.cpu().numpy(), blk["y"], rtol=1e-9, atol=1e-12 * np.abs(blk["y"]).max())
+
+
 @pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pdlp_*.npz")))
 def test_pdlp_golden(hb, cuda, path):
     with np.load(GOLDEN / path) as z:
