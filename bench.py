@@ -577,7 +577,7 @@ def run_norm(args, hb, dev, peaks):
     achieved = 2 * d * n * n / (kms[0] / 1e3) / 1e12 if kms else float("nan")
     extra = {"dtype": "f32 distance, f64 score", "roofline": {
         "bound": "fp32 pipe", "achieved": achieved, "peak": peak, "unit": "Tinst/s", "frac": achieved / peak,
-        "traffic": None, "kernel": "hb::norm::scan_kernel<0,8,1,0> (pass 1)",
+        "traffic": None, "kernel": "hb::norm::scan_kernel<0,8,1,0,1> (one pass: row and column lists)",
         "peak_source": "nominal: SMs x 128 fp32 lanes x max SM clock"}}
     if not args.no_cpu:
         import oracle

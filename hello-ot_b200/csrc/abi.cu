@@ -155,7 +155,8 @@ int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (!x || !y || !f || !g || !workspace) return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
     if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
         return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
-    if (cost_type < 0 || cost_type > 2) return fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2)");
+    if ((cost_type & ~HB_NORM_TWO_PASS) < 0 || (cost_type & ~HB_NORM_TWO_PASS) > 2)
+        return fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2), optionally | HB_NORM_TWO_PASS");
     if (!valid_k(k)) return fail(HB_BAD_ARGUMENT, "k must be in 0..32");
     if (k > 0 && (!row_vals || !row_idx || !col_vals || !col_idx)) return fail(HB_BAD_ARGUMENT, "null output pointer");
     if (compute_stats && !stats5) return fail(HB_BAD_ARGUMENT, "null stats pointer");

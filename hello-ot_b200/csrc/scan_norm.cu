@@ -14,6 +14,7 @@
 // register block from k-major shared-memory slabs; the distance tile is then
 // handed through shared memory to a row-per-thread epilogue (two threads per
 // row, one per half of the columns) that keeps the row top-k in registers.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -27,11 +28,18 @@ namespace norm {
 
 constexpr int BM = 128, BN = 128, BKS = 8, THREADS = 256;
 
+// Slab position of tile row r: the 8 rows ty, ty+16, ..., ty+112 of the thread
+// with distance-block row ty sit side by side, so a thread reads its 8 values
+// with two 16-byte loads (and likewise for columns).
+__device__ __forceinline__ int slab_pos(int r) { return (r & 15) * 8 + (r >> 4); }
+
 struct Smem {
-    float xs[2][BKS][BM];
+    float xs[2][BKS][BM];  // k-major slabs, rows at slab_pos
     float ys[2][BKS][BN];
     float dist[BM][BN + 1];
-    double dbias[BN];
+    double dbias[BN];      // the tile's column biases
+    double rbx[BM];        // the tile's row biases (one-pass column epilogue)
+    float cthr[BN];        // the tile's column thresholds (one pass)
     double red[8 * 5];
 };
 
@@ -45,6 +53,12 @@ struct Params {
     double* part_v;  // [groups*2][q][K]
     int* part_i;
     double* cta_stats;
+    // one pass: CTA b owns row group b / groups (rbg row blocks) x column group b % groups
+    int rb, rbg;
+    int* ckey;      // [ct * BN] column screening thresholds (ordered-int image of fp32)
+    double* cval;   // [row groups * 2][n][K] column lists (per row group and row half)
+    int* cidx;
+    int* progress;  // [grid] tiles started by each CTA
 };
 
 template <int KIND>
@@ -60,15 +74,43 @@ __device__ __forceinline__ void load_slab(const float* __restrict__ src, int row
     // 128 rows x 8 features, stored k-major; thread t covers row t/2, features (t%2)*4..+3
     const int t = threadIdx.x;
     const int r = t >> 1, kb = (t & 1) * 4;
-    const int gr = r0 + r;
+    const int gr = r0 + r, pos = slab_pos(r);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int k = k0 + kb + j;
-        dst[kb + j][r] = (gr < rows_total && k < d) ? src[(int64_t)gr * d + k] : 0.0f;
+        dst[kb + j][pos] = (gr < rows_total && k < d) ? src[(int64_t)gr * d + k] : 0.0f;
     }
 }
 
-template <int KIND, int K, bool STATS, bool SWAP>
+// Order-preserving integer image of an fp32 value (atomicMax on thresholds).
+__device__ __forceinline__ int order_key(float f) {
+    const int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float order_value(int key) { return __int_as_float(key >= 0 ? key : key ^ 0x7FFFFFFF); }
+
+// One pass: a column group's CTAs (one per row group) stream the same column
+// tiles; each stays within PACE tiles of the slowest so the tiles one of them
+// reads are still in L2 for the others.  The wait is bounded (PACE_SPINS
+// sleeps, then it proceeds): no CTA depends on another making progress.
+constexpr int PACE = 2, PACE_SPINS = 64;
+__device__ __forceinline__ void pace(const Params& p, int t) {
+    volatile int* prog = p.progress;
+    prog[blockIdx.x] = t;
+    const int g = blockIdx.x % p.groups, gr = gridDim.x / p.groups;
+    for (int spin = 0; spin < PACE_SPINS; ++spin) {
+        int slow = INT32_MAX;
+        for (int r = 0; r < gr; ++r) slow = min(slow, prog[r * p.groups + g]);
+        if (t - slow <= PACE) return;
+        __nanosleep(500);
+    }
+}
+
+// ONE (one pass, K <= 8): after the row epilogue, thread (column c, row half h)
+// screens the 64 rows of its half against the column's threshold and inserts
+// the candidates into the column's list for (row group, h) in HBM; a full list
+// raises the shared threshold.  Scores are the row epilogue's: (g - c) + f.
+template <int KIND, int K, bool STATS, bool SWAP, bool ONE>
 __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
@@ -78,7 +120,15 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
     const int er = t & (BM - 1), half = t >> 7;   // epilogue: row er, columns half*64..+63
     double acc[5] = {0, 0, 0, 0, 0};
     TopK<KK> top;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    int u0 = blockIdx.x, ustep = gridDim.x, uend = p.units;
+    if (ONE) {
+        const int rg = blockIdx.x / p.groups, g = blockIdx.x % p.groups;
+        const int rb0 = rg * p.rbg, rb1 = min(p.rb, rb0 + p.rbg);
+        u0 = rb0 * p.groups + g; ustep = p.groups; uend = rb1 > rb0 ? rb1 * p.groups : 0;
+    }
+    const int64_t list_base = ONE ? (int64_t)((blockIdx.x / p.groups) * 2 + half) * p.n : 0;
+    int tile = 0;
+    for (int u = u0; u < uend; u += ustep) {
         const int rb = u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         const int row = rb * BM + er;
@@ -86,8 +136,9 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
         // no query bias: add -0.0, the exact identity (keeps g - c bit for bit, signed zeros included)
         const double rbias = rvalid && p.q_bias ? p.q_bias[row] : -0.0;
         top.reset();
-        for (int ct = g * p.tpg; ct < ct1; ++ct) {
+        for (int ct = g * p.tpg; ct < ct1; ++ct, ++tile) {
             const int c0 = ct * BN;
+            if (ONE && t == 0) pace(p, tile);
             float dist[8][8];
 #pragma unroll
             for (int i = 0; i < 8; ++i)
@@ -103,13 +154,17 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                     load_slab(p.x, p.q, p.d, rb * BM, (sl + 1) * BKS, s.xs[cur ^ 1]);
                     load_slab(p.y, p.n, p.d, c0, (sl + 1) * BKS, s.ys[cur ^ 1]);
                 }
-                const int kn = min(BKS, p.d - sl * BKS);
-                for (int k = 0; k < kn; ++k) {
-                    float xv[8], yv[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) xv[i] = s.xs[cur][k][ty + 16 * i];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) yv[j] = s.ys[cur][k][tx + 16 * j];
+                // features past d are zero in both slabs: they add |0 - 0| = 0 (or (0-0)^2),
+                // which leaves every fp32 partial sum unchanged, so the loop runs a full slab
+                // (not unrolled: unrolling hoists the slab loads and spills the 8x8 block)
+#pragma unroll 1
+                for (int k = 0; k < BKS; ++k) {
+                    const float4 xa = *reinterpret_cast<const float4*>(&s.xs[cur][k][ty * 8]);
+                    const float4 xb = *reinterpret_cast<const float4*>(&s.xs[cur][k][ty * 8 + 4]);
+                    const float4 ya = *reinterpret_cast<const float4*>(&s.ys[cur][k][tx * 8]);
+                    const float4 yb = *reinterpret_cast<const float4*>(&s.ys[cur][k][tx * 8 + 4]);
+                    const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                    const float yv[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -124,7 +179,13 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                 for (int j = 0; j < 8; ++j)
                     s.dist[ty + 16 * i][tx + 16 * j] = KIND == 2 ? sqrtf(dist[i][j]) : dist[i][j];
             const int ncols = min(BN, p.n - c0);
-            if (t < BN) s.dbias[t] = t < ncols ? p.d_bias[c0 + t] : 0.0;
+            if (t < BN) {
+                s.dbias[t] = t < ncols ? p.d_bias[c0 + t] : 0.0;
+                if (ONE) {
+                    s.rbx[t] = rbias;  // thread t < BM owns row t (half 0)
+                    s.cthr[t] = t < ncols ? order_value(p.ckey[c0 + t]) : INFINITY;
+                }
+            }
             __syncthreads();
             if (rvalid) {
                 const int cb0 = half * 64;
@@ -169,6 +230,35 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                     top.offer(sc, c0 + cb0 + j);
                 }
             }
+            if (ONE && K > 0) {  // column side: thread (column er, row half `half`)
+                const int c = er, r0 = half * 64;
+                const int rlive = min(64, p.q - rb * BM - r0);  // valid rows of this half
+                if (c < ncols && rlive > 0) {
+                    const double cb = s.dbias[c];
+                    const double thr = (double)s.cthr[c];
+                    uint64_t cmask = 0;
+#pragma unroll 16
+                    for (int r = 0; r < 64; ++r) {
+                        const double sc = (cb - (double)s.dist[r0 + r][c]) + s.rbx[r0 + r];
+                        cmask |= (r < rlive && sc >= thr) ? (1ull << r) : 0ull;
+                    }
+                    if (cmask) {
+                        const int64_t base = (list_base + c0 + c) * KK;
+                        TopK<KK> cl;
+#pragma unroll
+                        for (int q2 = 0; q2 < KK; ++q2) { cl.v[q2] = p.cval[base + q2]; cl.i[q2] = p.cidx[base + q2]; }
+                        while (cmask) {
+                            const int r = __ffsll(cmask) - 1;
+                            cmask &= cmask - 1;
+                            cl.offer((cb - (double)s.dist[r0 + r][c]) + s.rbx[r0 + r], rb * BM + r0 + r);
+                        }
+#pragma unroll
+                        for (int q2 = 0; q2 < KK; ++q2) { p.cval[base + q2] = cl.v[q2]; p.cidx[base + q2] = cl.i[q2]; }
+                        if (cl.i[KK - 1] != INT32_MAX)
+                            atomicMax(p.ckey + c0 + c, order_key(__double2float_rd(cl.v[KK - 1])));
+                    }
+                }
+            }
             __syncthreads();
         }
         if (K > 0 && rvalid) {
@@ -179,6 +269,7 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
             for (int j = 0; j < KK; ++j) { pv[j] = top.v[j]; pi[j] = top.i[j]; }
         }
     }
+    if (ONE && t == 0) *(volatile int*)(p.progress + blockIdx.x) = INT32_MAX;  // done: never wait for this CTA
     if (STATS) {
         const int lane = t & 31, w = t >> 5;
 #pragma unroll
@@ -209,9 +300,9 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
 
 namespace {
 
-template <int KIND, int K, bool STATS, bool SWAP>
+template <int KIND, int K, bool STATS, bool SWAP, bool ONE = false>
 cudaError_t norm_launch(const norm::Params& p, int grid, cudaStream_t st) {
-    auto fn = norm::scan_kernel<KIND, K, STATS, SWAP>;
+    auto fn = norm::scan_kernel<KIND, K, STATS, SWAP, ONE>;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(norm::Smem));
@@ -239,6 +330,35 @@ cudaError_t norm_k(int K, const norm::Params& p, int grid, cudaStream_t st) {
     }
 }
 
+template <int KIND, bool STATS>
+cudaError_t norm_one_k(int K, const norm::Params& p, int grid, cudaStream_t st) {
+    switch (K) {
+        case 1: return norm_launch<KIND, 1, STATS, false, true>(p, grid, st);
+        case 2: return norm_launch<KIND, 2, STATS, false, true>(p, grid, st);
+        case 4: return norm_launch<KIND, 4, STATS, false, true>(p, grid, st);
+        case 8: return norm_launch<KIND, 8, STATS, false, true>(p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <bool STATS>
+cudaError_t norm_one(int kind, int K, const norm::Params& p, int grid, cudaStream_t st) {
+    switch (kind) {
+        case 0: return norm_one_k<0, STATS>(K, p, grid, st);
+        case 1: return norm_one_k<1, STATS>(K, p, grid, st);
+        case 2: return norm_one_k<2, STATS>(K, p, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+__global__ void init_norm_columns(double* cval, int* cidx, int* ckey, int64_t lists, int64_t nkeys, int K) {
+    const int64_t total = lists * K > nkeys ? lists * K : nkeys;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        if (e < lists * K) { cval[e] = -INFINITY; cidx[e] = INT32_MAX; }
+        if (e < nkeys) ckey[e] = norm::order_key(-INFINITY);
+    }
+}
+
 template <bool STATS, bool SWAP>
 cudaError_t norm_kind(int kind, int K, const norm::Params& p, int grid, cudaStream_t st) {
     switch (kind) {
@@ -262,45 +382,96 @@ struct NormLayout {
     double *pv1 = nullptr, *pv2 = nullptr, *cta = nullptr;
     int *pi1 = nullptr, *pi2 = nullptr;
     ScanPlan p1{}, p2{};
+    // one pass (1 <= K <= 8): rectangles of gr row groups x gc column groups
+    bool one = false;
+    int gr = 0, rbg = 0, gc = 0, tpg = 0, rb = 0, ct = 0, grid = 0;
+    double* cval = nullptr;
+    int *cidx = nullptr, *ckey = nullptr, *progress = nullptr;
     size_t bytes = 0;
     bool ok = true;
 };
 
-NormLayout norm_layout(void* base, size_t size, int64_t q, int64_t n, int k) {
+constexpr int NORM_ONE_PASS_ROW_GROUPS = 8;
+
+NormLayout norm_layout(void* base, size_t size, int64_t q, int64_t n, int k, bool one) {
     NormLayout L;
     const int sms = sm_count();
     const int K = k > 0 ? bucket_of(k) : 0;
     Arena ar{static_cast<char*>(base), size, 0};
-    L.p1 = scan_plan(q, n, norm::BM, norm::BN, 2, sms, 1);
-    L.p2 = scan_plan(n, q, norm::BM, norm::BN, 2, sms, 1);
-    if (K > 0) {
-        L.pv1 = ar.take<double>((size_t)L.p1.groups * 2 * q * K);
-        L.pi1 = ar.take<int>((size_t)L.p1.groups * 2 * q * K);
-        L.pv2 = ar.take<double>((size_t)L.p2.groups * 2 * n * K);
-        L.pi2 = ar.take<int>((size_t)L.p2.groups * 2 * n * K);
-        if (base && (!L.pv1 || !L.pi1 || !L.pv2 || !L.pi2)) L.ok = false;
+    auto fail_if = [&](const void* ptr) { if (base && !ptr) L.ok = false; };
+    L.one = one && K >= 1 && K <= 8;
+    if (L.one) {
+        L.rb = (int)((q + norm::BM - 1) / norm::BM);
+        L.ct = (int)((n + norm::BN - 1) / norm::BN);
+        L.gr = std::min(NORM_ONE_PASS_ROW_GROUPS, L.rb);
+        L.rbg = (L.rb + L.gr - 1) / L.gr;
+        L.gr = (L.rb + L.rbg - 1) / L.rbg;
+        const int gc = std::min(L.ct, std::max(1, 2 * sms / L.gr));  // two CTAs per SM
+        L.tpg = (L.ct + gc - 1) / gc;
+        L.gc = (L.ct + L.tpg - 1) / L.tpg;
+        L.grid = L.gr * L.gc;
+        const size_t lists = (size_t)L.gr * 2 * n;
+        L.pv1 = ar.take<double>((size_t)L.gc * 2 * q * K); fail_if(L.pv1);
+        L.pi1 = ar.take<int>((size_t)L.gc * 2 * q * K); fail_if(L.pi1);
+        L.cval = ar.take<double>(lists * K); fail_if(L.cval);
+        L.cidx = ar.take<int>(lists * K); fail_if(L.cidx);
+        L.ckey = ar.take<int>((size_t)L.ct * norm::BN); fail_if(L.ckey);
+        L.progress = ar.take<int>((size_t)L.grid); fail_if(L.progress);
+        L.cta = ar.take<double>((size_t)L.grid * 5); fail_if(L.cta);
+    } else {
+        L.p1 = scan_plan(q, n, norm::BM, norm::BN, 2, sms, 1);
+        L.p2 = scan_plan(n, q, norm::BM, norm::BN, 2, sms, 1);
+        if (K > 0) {
+            L.pv1 = ar.take<double>((size_t)L.p1.groups * 2 * q * K); fail_if(L.pv1);
+            L.pi1 = ar.take<int>((size_t)L.p1.groups * 2 * q * K); fail_if(L.pi1);
+            L.pv2 = ar.take<double>((size_t)L.p2.groups * 2 * n * K); fail_if(L.pv2);
+            L.pi2 = ar.take<int>((size_t)L.p2.groups * 2 * n * K); fail_if(L.pi2);
+        }
+        L.cta = ar.take<double>((size_t)(L.p1.grid > L.p2.grid ? L.p1.grid : L.p2.grid) * 5); fail_if(L.cta);
     }
-    L.cta = ar.take<double>((size_t)(L.p1.grid > L.p2.grid ? L.p1.grid : L.p2.grid) * 5);
-    if (base && !L.cta) L.ok = false;
     L.bytes = ar.used + 256;
     return L;
 }
 
-size_t norm_bytes(int64_t q, int64_t n, int k) { return norm_layout(nullptr, 0, q, n, k).bytes; }
+// One workspace size serves both modes.
+size_t norm_bytes(int64_t q, int64_t n, int k) {
+    return std::max(norm_layout(nullptr, 0, q, n, k, false).bytes, norm_layout(nullptr, 0, q, n, k, true).bytes);
+}
 
 int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
               int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
               size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only) {
-    NormLayout L = norm_layout(ws, ws_bytes, q, n, k);
-    if (!L.ok) { err = "workspace too small for the norm scan"; return 3; }
+    const bool two_pass = (kind & HB_NORM_TWO_PASS) != 0;
+    kind &= 0xF;
     const int K = k > 0 ? bucket_of(k) : 0;
+    NormLayout L = norm_layout(ws, ws_bytes, q, n, k, !rows_only && !two_pass);
+    if (!L.ok) { err = "workspace too small for the norm scan"; return 3; }
     norm::Params p{};
     p.x = x; p.y = y; p.q = (int)q; p.n = (int)n; p.d = (int)d;
-    p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
     p.q_bias = f; p.d_bias = g;
     p.part_v = L.pv1; p.part_i = L.pi1; p.cta_stats = L.cta;
-    cudaError_t e = want_stats ? norm_kind<true, false>(kind, K, p, L.p1.grid, st)
-                               : norm_kind<false, false>(kind, K, p, L.p1.grid, st);
+    cudaError_t e;
+    if (L.one) {
+        const int blocks = sm_count() * 8;
+        init_norm_columns<<<blocks, 256, 0, st>>>(L.cval, L.cidx, L.ckey, (int64_t)L.gr * 2 * n,
+                                                  (int64_t)L.ct * norm::BN, K);
+        count_launches(1);
+        e = cudaMemsetAsync(L.progress, 0, sizeof(int) * L.grid, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        p.groups = L.gc; p.tpg = L.tpg; p.ct = L.ct; p.units = L.rb * L.gc;
+        p.rb = L.rb; p.rbg = L.rbg;
+        p.ckey = L.ckey; p.cval = L.cval; p.cidx = L.cidx; p.progress = L.progress;
+        e = want_stats ? norm_one<true>(kind, K, p, L.grid, st) : norm_one<false>(kind, K, p, L.grid, st);
+        if (e != cudaSuccess) { err = std::string("norm scan: ") + cudaGetErrorString(e); return 6; }
+        if (want_stats) { finalize_stats<<<1, 32, 0, st>>>(L.cta, L.grid, stats5); count_launches(1); }
+        e = merge_any(K, L.pv1, L.pi1, L.gc * 2, q, k, rv, ri, st);
+        if (e == cudaSuccess) e = merge_any(K, L.cval, L.cidx, L.gr * 2, n, k, cv, ci, st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        return 0;
+    }
+    p.groups = L.p1.groups; p.tpg = L.p1.tpg; p.ct = L.p1.ct; p.units = L.p1.units;
+    e = want_stats ? norm_kind<true, false>(kind, K, p, L.p1.grid, st)
+                   : norm_kind<false, false>(kind, K, p, L.p1.grid, st);
     if (e != cudaSuccess) { err = std::string("norm pass 1: ") + cudaGetErrorString(e); return 6; }
     if (want_stats) { finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid, stats5); count_launches(1); }
     if (K > 0) {
@@ -362,7 +533,8 @@ extern "C" int hb_norm_scan_noalloc(const float* x, const float* y, int64_t q, i
     if (!x || !y || !f || !g) return abi_fail(HB_BAD_ARGUMENT, "null input pointer");
     if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
         return abi_fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
-    if (cost_type < 0 || cost_type > 2) return abi_fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2)");
+    if ((cost_type & ~HB_NORM_TWO_PASS) < 0 || (cost_type & ~HB_NORM_TWO_PASS) > 2)
+        return abi_fail(HB_BAD_ARGUMENT, "cost_type must be 0 (l1), 1 (linf) or 2 (l2), optionally | HB_NORM_TWO_PASS");
     if (k < 0 || k > 32) return abi_fail(HB_BAD_ARGUMENT, "k must be in 0..32");
     if (k > 0 && (!row_vals || !row_idx || !col_vals || !col_idx)) return abi_fail(HB_BAD_ARGUMENT, "null output pointer");
     if (compute_stats && !stats5) return abi_fail(HB_BAD_ARGUMENT, "null stats pointer");

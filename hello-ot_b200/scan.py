@@ -106,12 +106,16 @@ def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute
 NORM_KIND = {"l1": 0, "linf": 1, "l2": 2, 0: 0, 1: 1, 2: 2}
 
 
-def norm_scan(x, y, f, g, k, cost_type, *, compute_stats=True):
-    """Bidirectional ℓ1/ℓ∞/ℓ2 scan on the CUDA cores (outputs as l2sq_scan)."""
+NORM_TWO_PASS = 0x10
+
+
+def norm_scan(x, y, f, g, k, cost_type, *, compute_stats=True, passes=None):
+    """Bidirectional ℓ1/ℓ∞/ℓ2 scan on the CUDA cores (outputs as l2sq_scan).
+    k <= 8 makes one pass over the pairs unless passes=2 (same lists bit for bit)."""
     x, y, f, g = map(_c, (x, y, f, g))
     q, d = x.shape
     n = y.shape[0]
-    kind = NORM_KIND[cost_type]
+    kind = NORM_KIND[cost_type] | (NORM_TWO_PASS if passes == 2 else 0)
     L = lib()
     dev = x.device
     kk = int(k)

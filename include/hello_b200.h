@@ -134,7 +134,12 @@ int hb_norm_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d
  *
  * score = (g_j - c_ij) + f_i with c_ij the fp32 distance (features summed in
  * index order, ℓ2 via fma then sqrtf).  Outputs and k as for hb_l2sq_scan.
+ * For 1 <= k <= 8 the scan makes one pass over the pairs (column lists kept
+ * per row group in the workspace); cost_type | HB_NORM_TWO_PASS forces a
+ * second pass with the clouds' roles exchanged instead.  Both give the same
+ * lists bit for bit.  The workspace size covers both.
  * ------------------------------------------------------------------------- */
+#define HB_NORM_TWO_PASS 0x10
 size_t hb_norm_scan_workspace(int64_t q, int64_t n, int k);
 int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
                  int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,

@@ -204,6 +204,37 @@ def test_norm_scan_bit_exact(hb, cuda, oracle, kind, q, n, d, k):
     np.testing.assert_allclose(stats[:2], es[:2], rtol=1e-12)
 
 
+# (q, n, d, k): several row blocks per row group, ragged tiles, k > n, one feature
+NORM_ONE_PASS_CASES = [(3000, 777, 20, 8), (130, 2600, 3, 4), (5, 3, 2, 8), (1100, 900, 1, 1), (2049, 2050, 64, 2)]
+
+
+@pytest.mark.parametrize("kind", ["l1", "linf", "l2"])
+@pytest.mark.parametrize("q,n,d,k", NORM_ONE_PASS_CASES)
+def test_norm_one_pass_equals_two_pass(hb, cuda, kind, q, n, d, k):
+    """One pass (column lists per row group) and two passes (roles exchanged) see the same
+    fp32 distances and fp64 scores: identical lists; certificate sums to summation order."""
+    rng = np.random.default_rng(q + 2 * n + d)
+    x = rng.normal(size=(q, d)).astype(np.float32)
+    y = (x[rng.integers(0, q, n)] + 0.4 * rng.normal(size=(n, d))).astype(np.float32)
+    f = rng.normal(size=q) * d * 0.5
+    g = rng.normal(size=n) * d * 0.5 + d
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    args = (T(x, torch.float32), T(y, torch.float32), T(f, torch.float64), T(g, torch.float64), k, kind)
+    hb.set_kernel_timing(True)
+    try:
+        one = [t.clone() for t in hb.norm_scan(*args)]
+        assert len(hb.last_kernel_times()) == 1  # one scan kernel launch
+        two = [t.clone() for t in hb.norm_scan(*args, passes=2)]
+        assert len(hb.last_kernel_times()) == 2
+    finally:
+        hb.set_kernel_timing(False)
+    for u, v in zip(one[:4], two[:4]):
+        assert torch.equal(u, v)
+    s1, s2 = one[4].cpu().numpy(), two[4].cpu().numpy()
+    assert s1[2] == s2[2] and s1[3] == s2[3] and s1[4] == s2[4]
+    np.testing.assert_allclose(s1[:2], s2[:2], rtol=1e-12)
+
+
 @pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("scan_l*.npz") if "l2sq" not in p.name))
 def test_norm_scan_golden_certificate(hb, cuda, oracle, path):
     with np.load(GOLDEN / path) as z:
