@@ -524,7 +524,9 @@ def run_pdlp(args, hb, dev, peaks):
 
 def run_pairs(args, hb, dev, peaks):
     """Active-support pair costs: a step evaluates E = 8 (n + m) candidate edges
-    (k = 8 per row and column) of an n x n, d-dim problem; metric Gedges/s."""
+    (k = 8 per row and column) of an n x n, d-dim problem; metric Gedges/s.  The
+    edges come grouped by source row, the order the reference's CSR-blocked
+    evaluation uses (pairs.py:380-412); targets are random."""
     n, d = args.n, args.d
     e = 8 * 2 * n
     g = torch.Generator(device=dev)
@@ -532,18 +534,30 @@ def run_pairs(args, hb, dev, peaks):
     x = torch.randn(n, d, device=dev, generator=g)
     y = torch.randn(n, d, device=dev, generator=g)
     a, b = (x.double() ** 2).sum(1), (y.double() ** 2).sum(1)
-    rows = torch.randint(0, n, (e,), device=dev, generator=g)
+    rows = torch.sort(torch.randint(0, n, (e,), device=dev, generator=g)).values
     cols = torch.randint(0, n, (e,), device=dev, generator=g)
     hb.set_kernel_timing(True)
     sec = _timed(lambda: hb.pair_costs(3, x, y, rows, cols, a, b, 2.0), args, dev)
     kms = hb.last_kernel_times()
+    # the same edges in random order (every source row gathered per edge)
+    perm = torch.randperm(e, device=dev, generator=g)
+    rows_r, cols_r = rows[perm].contiguous(), cols[perm].contiguous()
+    sec_r = _timed(lambda: hb.pair_costs(3, x, y, rows_r, cols_r, a, b, 2.0), args, dev)
+    kms_r = hb.last_kernel_times()
     hb.set_kernel_timing(False)
-    bytes_call = e * (8 + 8 + 8 + 2 * 4 * d + 16)
+    # algorithmic bytes: indices + output per edge, each source row once, each target row per edge
+    # (random targets have no reuse), row norms once per row
+    u_r = int(torch.unique(rows).numel())
+    bytes_call = e * (8 + 8 + 8 + 4 * d) + u_r * (4 * d + 8) + 8 * int(torch.unique(cols).numel())
     achieved = bytes_call / (kms[0] / 1e3) / 1e9 if kms else bytes_call / sec / 1e9
     extra = {"dtype": "f32 in, f64 accumulate", "roofline": {
         "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-        "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "hb::pairs::pair_kernel<3,...>",
-        "bytes_per_edge": bytes_call / e}}
+        "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "hb::pairs::pair_kernel<3,32,1>",
+        "bytes_per_edge": bytes_call / e,
+        "note": "each source row once, each target row per edge (no target reuse on a random support)"},
+        "random_order": {"value": e / sec_r / 1e9, "unit": "Gedges/s",
+                         "kernel_ms": kms_r[0] if kms_r else None,
+                         "gathered_gbs": e * (24 + 8 * d) / (kms_r[0] / 1e3) / 1e9 if kms_r else None}}
     if not args.no_cpu:  # the reference's CPU branch: a[r] + b[c] - s * einsum (pairs.py:296-307)
         xs, ys = x.cpu().numpy(), y.cpu().numpy()
         asub, bsub = a.cpu().numpy().astype(np.float32), b.cpu().numpy().astype(np.float32)
@@ -554,8 +568,8 @@ def run_pairs(args, hb, dev, peaks):
         extra["cpu_baseline"] = {"value": rs.size / dt / 1e9, "unit": "Gedges/s", "cores": 1, "kind": "port",
                                  "sample": f"{rs.size} edges with the reference's numpy CPU branch"}
     _line(args, "pair costs Gedges/s", e / sec / 1e9, "Gedges/s", sec,
-          {"workload": f"l2sq pair costs, E={e} random edges of a {n} x {n} problem, d={d}", "edges": e, "d": d},
-          extra)
+          {"workload": f"l2sq pair costs, E={e} edges of a {n} x {n} problem grouped by source row, "
+                       f"random targets, d={d}", "edges": e, "d": d}, extra)
 
 
 def run_norm(args, hb, dev, peaks):

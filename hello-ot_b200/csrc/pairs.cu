@@ -10,7 +10,9 @@
 // exact in fp64).  A group of G lanes serves one edge and reads the two
 // feature rows with 128-bit loads when the rows are 16-byte aligned; the
 // group reduces with a fixed xor-shuffle tree, so results are deterministic.
-// HBM-bound: every edge gathers its database row once.
+// Each warp takes one contiguous block of edges, so the source row of edges
+// grouped by source (the reference's CSR-blocked order) is read from HBM once
+// and then from L1.  HBM-bound: every edge gathers its database row once.
 #include <string>
 
 #include "common.cuh"
@@ -39,14 +41,17 @@ __global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, 
                                                    const double* __restrict__ b, double scale,
                                                    const int64_t* __restrict__ rows, const int64_t* __restrict__ cols,
                                                    int64_t count, double* __restrict__ out, int* status) {
-    // warp-uniform loop: each warp takes 32/G consecutive edges per step
+    // warp-uniform loop: each warp walks its own contiguous block of edges,
+    // 32/G consecutive edges per step
     const int lane = threadIdx.x & 31, sub = lane & (G - 1);
     const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     constexpr int EPW = 32 / G;
-    for (int64_t eb = warp_id * EPW; eb < count; eb += warps * EPW) {
+    const int64_t per_warp = ((count + warps - 1) / warps + EPW - 1) / EPW * EPW;
+    const int64_t e_end = min(count, (warp_id + 1) * per_warp);
+    for (int64_t eb = warp_id * per_warp; eb < e_end; eb += EPW) {
         const int64_t e = eb + lane / G;
-        const bool live = e < count;
+        const bool live = e < e_end;
         const int64_t r = live ? rows[e] : 0, c = live ? cols[e] : 0;
         const bool ok = live && r >= 0 && r < nx && c >= 0 && c < ny;
         double acc = 0.0;
