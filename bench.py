@@ -55,7 +55,7 @@ DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 2.379, (256, "fp32", "two-pass
 # per-path default sizes: config 5 (m = n = 2^20, d = 256) for the l2sq scans, pair costs and
 # the PDHG; config 3 (n = m = 262144, d = 128) for the l1 scan
 PATH_SIZES = {"scan": (1_048_576, 256), "initial": (1_048_576, 256), "pairs": (1_048_576, 256),
-              "pdlp": (1_048_576, 256), "norm": (262_144, 128)}
+              "pdlp": (1_048_576, 256), "norm": (262_144, 128), "support": (1_048_576, 256)}
 
 
 def parse_args():
@@ -64,10 +64,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial"],
+    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial", "support"],
                    help="scan (default, the headline): l2sq pricing scan; norm: l1 scan (config 3 shape); "
                         "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations; "
-                        "initial: l2sq directional top-16 scan (config 5 shape)")
+                        "initial: l2sq directional top-16 scan (config 5 shape); "
+                        "support: active-support candidate filter")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
     p.add_argument("--n", type=int, default=None, help="points per side (default: the path's config)")
     p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
@@ -640,6 +641,49 @@ def run_initial(args, hb, dev, peaks):
            "median_pair_cost": med}, extra)
 
 
+def run_support(args, hb, dev, peaks):
+    """Active-support filter (ActiveSupport.filter_new_candidate_pairs): a support of
+    10 (n + m) unsorted keys and the 8 (n + m) row-side plus 8 (n + m) column-side
+    candidates of one scan, a third of them already in the support; metric candidates/s."""
+    n = m = args.n
+    g = torch.Generator(device=dev)
+    g.manual_seed(42)
+    size, cand = 10 * (n + m), 16 * (n + m)
+    keys = torch.unique(torch.randint(0, n * m, (int(size * 1.05),), device=dev, generator=g))[:size]
+    keys = keys[torch.randperm(keys.numel(), device=dev, generator=g)]
+    old = keys[torch.randint(0, keys.numel(), (cand // 3,), device=dev, generator=g)]
+    ck = torch.cat([old, torch.randint(0, n * m, (cand - old.numel(),), device=dev, generator=g)])
+    rows, cols = (ck // m).to(torch.int32), (ck % m).to(torch.int32)
+    hb.set_kernel_timing(True)
+    sec = _timed(lambda: hb.filter_new_candidate_pairs(keys, n, m, rows, cols), args, dev)
+    hb.set_kernel_timing(False)
+    new = hb.filter_new_candidate_pairs(keys, n, m, rows, cols)[3]
+    bytes_call = 8 * cand + 8 * keys.numel() + 8 * new  # read candidates and support keys, write new pairs
+    achieved = bytes_call / sec / 1e9
+    extra = {"dtype": "int64 keys", "roofline": {
+        "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+        "kernel": "hb::support (CUB radix sorts of both key sets, flag pass, compaction)",
+        "note": "algorithmic bytes: candidates and support keys read once, new pairs written once; "
+                "the radix sorts move each key several times"}}
+    if not args.no_cpu:  # the reference's own torch calls (active_support.py:483-506) on the host, 1/16 sample
+        kc, rc_, cc_ = keys[: keys.numel() // 16].cpu(), rows[: cand // 16].cpu(), cols[: cand // 16].cpu()
+        t0 = time.perf_counter()
+        ck2 = torch.unique(rc_.to(torch.int64) * m + cc_.to(torch.int64), sorted=True)
+        act = torch.sort(kc).values
+        pos = torch.searchsorted(act, ck2)
+        mem = (pos < act.numel()) & (act[pos.clamp_max(act.numel() - 1)] == ck2)
+        _ = ck2[~mem]
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": rc_.numel() / dt / 1e9, "unit": "Gcandidates/s",
+                                 "cores": torch.get_num_threads(), "kind": "port",
+                                 "sample": f"{rc_.numel()} candidates against {kc.numel()} support keys, "
+                                           "the reference's torch calls on the host"}
+    _line(args, "support filter Gcandidates/s", cand / sec / 1e9, "Gcandidates/s", sec,
+          {"workload": f"support filter, n=m={n}, support {keys.numel()} keys, {cand} candidates",
+           "n": n, "m": m, "support": int(keys.numel()), "candidates": cand, "new": int(new)}, extra)
+
+
 def run_other(args):
     import __graft_entry__ as entry
 
@@ -647,7 +691,8 @@ def run_other(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks, _ = load_peaks()
-    {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm, "initial": run_initial}[args.path](args, hb, dev, peaks)
+    {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm, "initial": run_initial,
+     "support": run_support}[args.path](args, hb, dev, peaks)
 
 
 def main():

@@ -21,7 +21,7 @@ CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "libhello_b200.so"
 INCLUDE = HERE.parent / "include"
-SOURCES = ["abi.cu", "scan_l2sq.cu", "scan_norm.cu", "pairs.cu", "pdlp.cu"]
+SOURCES = ["abi.cu", "scan_l2sq.cu", "scan_norm.cu", "pairs.cu", "pdlp.cu", "support.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + str(INCLUDE), "-Xptxas", "-warn-spills"]

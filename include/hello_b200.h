@@ -244,6 +244,24 @@ int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const doubl
                            hb_pdlp_trace_row* trace, int32_t trace_capacity, int32_t* trace_length,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Active-support maintenance: new candidate pairs.
+ *
+ * Replaces ActiveSupport.filter_new_candidate_pairs
+ * (src/hello_ot/restricted_ot/active_support.py:483-506).
+ *
+ * Candidate keys rows[i] * n_target + cols[i] are sorted and made unique; a key
+ * present among the n_active support keys (active_sorted != 0: already sorted
+ * ascending) is dropped.  new_rows / new_cols (capacity n_candidates) receive
+ * the remaining pairs in ascending key order, *new_count (host) their number.
+ * A candidate index outside [0, n_source) x [0, n_target) is HB_BAD_INPUT.
+ * ------------------------------------------------------------------------- */
+size_t hb_filter_new_pairs_workspace(int64_t n_active, int64_t n_candidates);
+int hb_filter_new_pairs(const int64_t* active_keys, int64_t n_active, int32_t active_sorted, const int32_t* rows,
+                        const int32_t* cols, int64_t n_candidates, int64_t n_source, int64_t n_target,
+                        int32_t* new_rows, int32_t* new_cols, int64_t* new_count, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -158,6 +158,21 @@ def pdlp(rows, cols, costs, source_mass, target_mass, x0=None, y0=None, *, frequ
                 abs_primal=info.ap, abs_dual=info.ad, primal_weight=info.weight)
 
 
+def filter_new_pairs(active_keys, rows, cols, n_target):
+    """New candidate pairs (ActiveSupport.filter_new_candidate_pairs,
+    src/hello_ot/restricted_ot/active_support.py:483-506): the unique candidate
+    keys row * n_target + col, ascending, minus the support keys.  Returns
+    (new_rows int32, new_cols int32, found, new_count)."""
+    rows = np.asarray(rows, np.int64).reshape(-1)
+    cols = np.asarray(cols, np.int64).reshape(-1)
+    found = int(rows.size)
+    keys = np.unique(rows * int(n_target) + cols)
+    active = np.asarray(active_keys, np.int64).reshape(-1)
+    if active.size:
+        keys = keys[~np.isin(keys, active)]
+    return (keys // int(n_target)).astype(np.int32), (keys % int(n_target)).astype(np.int32), found, int(keys.size)
+
+
 def load_ref(kind: str):
     """The reference's compiled CPU module ``hello_ot_cpp._scan`` / ``._lp``."""
     if not (REF_DIR / "hello_ot_cpp" / "__init__.py").exists():

@@ -48,6 +48,7 @@ from hello_ot._internal.lp.cpp_restricted_ot import CppRestrictedOTPDLP  # noqa:
 from hello_ot._internal.lp.torch_restricted_ot import TorchRestrictedOTPDLP  # noqa: E402
 from hello_ot.costs.pairs import _cost_pairs_lowrank_batched  # noqa: E402
 from hello_ot.costs.metric import pair_costs_metric  # noqa: E402
+from hello_ot.restricted_ot.active_support import ActiveSupport  # noqa: E402
 
 SCAN_L2SQ = [  # (name, q, n, d, k, seed, dual scale)
     ("l2sq_a", 37, 53, 8, 3, 1, 1.0),
@@ -150,6 +151,25 @@ def directional_case(name, family, cost, q, n, d, k, seed):
                         top1_values=cand.values.numpy(), top1_indices=cand.indices.numpy())
 
 
+def support_cases():
+    """ActiveSupport.filter_new_candidate_pairs (active_support.py:483-506) on CPU."""
+    rng = np.random.default_rng(51)
+    for name, ns, nt, size, cand in (("a", 40, 30, 200, 500), ("b", 1000, 700, 20000, 30000), ("empty", 50, 60, 0, 300)):
+        keys = rng.choice(ns * nt, size=size, replace=False)
+        rows, cols = keys // nt, keys % nt
+        sup = ActiveSupport(n_source=ns, n_target=nt, device="cpu")
+        sup.initialize_from_arrays(rows=rows, cols=cols, costs=np.zeros(size), x_prev=np.zeros(size))
+        # candidates: some already in the support, some repeated
+        cr = np.concatenate([rows[: size // 3], rng.integers(0, ns, cand)])
+        cc = np.concatenate([cols[: size // 3], rng.integers(0, nt, cand)])
+        dup = rng.integers(0, cr.size, cand // 5)
+        cr, cc = np.concatenate([cr, cr[dup]]), np.concatenate([cc, cc[dup]])
+        nr, nc, found, new = sup.filter_new_candidate_pairs(cr, cc)
+        np.savez_compressed(HERE / f"support_{name}.npz", n_source=ns, n_target=nt, active_keys=keys.astype(np.int64),
+                            rows=cr.astype(np.int32), cols=cc.astype(np.int32), new_rows=nr.numpy(),
+                            new_cols=nc.numpy(), found=found, new_count=new)
+
+
 def pdlp_cases():
     cases = []
     rng = np.random.default_rng(12)
@@ -217,6 +237,7 @@ if __name__ == "__main__":
         norm_case(*case)
     for case in DIRECTIONAL:
         directional_case(*case)
+    support_cases()
     pdlp_cases()
     pairs_cases()
     print("fixtures written to", HERE)

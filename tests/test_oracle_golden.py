@@ -153,3 +153,11 @@ def test_directional_oracle_matches_reference(oracle, path):
         e = bound(diff[:, 0], diff[:, 1])
         kth = rv[diff[:, 0], rk - 1]
         assert np.all(np.abs(s - kth) <= 2 * e + 1e-300), f"{path}: candidate differences outside the error band"
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("support_*.npz")))
+def test_support_filter_oracle_matches_reference(oracle, path):
+    z = _load(path)
+    nr, nc, found, new = oracle.filter_new_pairs(z["active_keys"], z["rows"], z["cols"], int(z["n_target"]))
+    assert found == int(z["found"]) and new == int(z["new_count"])
+    assert np.array_equal(nr, z["new_rows"]) and np.array_equal(nc, z["new_cols"])
