@@ -55,7 +55,8 @@ DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 2.379, (256, "fp32", "two-pass
 # per-path default sizes: config 5 (m = n = 2^20, d = 256) for the l2sq scans, pair costs and
 # the PDHG; config 3 (n = m = 262144, d = 128) for the l1 scan
 PATH_SIZES = {"scan": (1_048_576, 256), "initial": (1_048_576, 256), "pairs": (1_048_576, 256),
-              "pdlp": (1_048_576, 256), "norm": (262_144, 128), "support": (1_048_576, 256)}
+              "pdlp": (1_048_576, 256), "norm": (262_144, 128), "support": (1_048_576, 256),
+              "prune": (1_048_576, 256)}
 
 
 def parse_args():
@@ -64,11 +65,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial", "support"],
+    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial", "support", "prune"],
                    help="scan (default, the headline): l2sq pricing scan; norm: l1 scan (config 3 shape); "
                         "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations; "
                         "initial: l2sq directional top-16 scan (config 5 shape); "
-                        "support: active-support candidate filter")
+                        "support: active-support candidate filter; prune: budgeted pruning selection")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
     p.add_argument("--n", type=int, default=None, help="points per side (default: the path's config)")
     p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
@@ -684,6 +685,51 @@ def run_support(args, hb, dev, peaks):
            "n": n, "m": m, "support": int(keys.numel()), "candidates": cand, "new": int(new)}, extra)
 
 
+def run_prune(args, hb, dev, peaks):
+    """Budgeted pruning selection (DualGapCleaning, protect-new): a support of 10 (n + m)
+    edges, 30% with flow, creation iterations spread over the last few; remove the 20%
+    with the largest reduced costs among the old zero-flow edges; metric edges/s."""
+    n = m = args.n
+    e = 10 * (n + m)
+    g = torch.Generator(device=dev)
+    g.manual_seed(42)
+    rows = torch.randint(0, n, (e,), device=dev, generator=g, dtype=torch.int32)
+    cols = torch.randint(0, m, (e,), device=dev, generator=g, dtype=torch.int32)
+    costs = torch.rand(e, device=dev, generator=g, dtype=torch.float64) * 3
+    x = torch.where(torch.rand(e, device=dev, generator=g) < 0.3,
+                    torch.rand(e, device=dev, generator=g, dtype=torch.float64), torch.zeros((), device=dev,
+                                                                                           dtype=torch.float64))
+    creation = torch.randint(-2, 6, (e,), device=dev, generator=g, dtype=torch.int32)
+    duals = torch.randn(n + m, device=dev, generator=g, dtype=torch.float64)
+    num = e // 5
+    sec = _timed(lambda: hb.select_prune_positions(rows, cols, costs, x, creation, duals, n, m, num, 5), args, dev)
+    bytes_call = e * (4 + 4 + 8 + 8 + 4) + 4 * num  # edge arrays read once, positions written
+    achieved = bytes_call / sec / 1e9
+    extra = {"dtype": "f64 reduced costs, int32 positions", "roofline": {
+        "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+        "kernel": "hb::support prune (values pass, compaction, stable radix sort of the removable edges)",
+        "note": "algorithmic bytes: the five edge arrays read once, positions written once; the sort moves "
+                "the removable edges' keys several times"}}
+    if not args.no_cpu:  # the reference's torch calls (pruning_values + _select_zero_flow_removals), 1/16 sample
+        k = e // 16
+        r_, c_, w_, x_, cr_ = (t[:k].cpu() for t in (rows, cols, costs, x, creation))
+        d_ = duals.cpu()
+        t0 = time.perf_counter()
+        rc = w_ - (d_[:n].index_select(0, r_.long()) + d_[n:].index_select(0, c_.long()))
+        rc = torch.where(torch.isfinite(rc), rc, torch.full_like(rc, -torch.inf))
+        pool = (cr_ != 5) & (cr_ != -1) & ~(x_.abs() > 1e-15)
+        idx = torch.nonzero(pool, as_tuple=False).view(-1)
+        order = torch.argsort(rc.index_select(0, idx), descending=True, stable=True)
+        _ = idx.index_select(0, order)[: num // 16]
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": k / dt / 1e9, "unit": "Gedges/s", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": f"{k} edges, the reference's torch calls on the host"}
+    _line(args, "pruning selection Gedges/s", e / sec / 1e9, "Gedges/s", sec,
+          {"workload": f"budgeted pruning selection, n=m={n}, support {e} edges, remove {num}",
+           "n": n, "m": m, "edges": e, "remove": num}, extra)
+
+
 def run_other(args):
     import __graft_entry__ as entry
 
@@ -692,7 +738,7 @@ def run_other(args):
     torch.cuda.set_device(dev)
     peaks, _ = load_peaks()
     {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm, "initial": run_initial,
-     "support": run_support}[args.path](args, hb, dev, peaks)
+     "support": run_support, "prune": run_prune}[args.path](args, hb, dev, peaks)
 
 
 def main():

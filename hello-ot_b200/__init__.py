@@ -14,6 +14,6 @@ from .scan import (ScanExtension, LowrankBidirScanResult, flatten_candidates, l2
                    norm_scan, norm_topk, raw_lowrank_bidir_feasibility_pricing_scan, scan_routes, topk_bucket)
 from .pairs import cost_pairs_lowrank, pair_costs, pair_costs_metric  # noqa: F401
 from .pdlp import NativeRestrictedOTPDLP, SolverResult  # noqa: F401
-from .support import filter_new_candidate_pairs, support_filter  # noqa: F401
+from .support import filter_new_candidate_pairs, select_prune_positions, support_filter  # noqa: F401
 
 __version__ = "0.1.0"

@@ -22,7 +22,8 @@ EXPORTS = ("hb_abi_version", "hb_last_error", "hb_kernel_launch_count", "hb_set_
            "hb_last_kernel_times", "hb_l2sq_scan_workspace", "hb_l2sq_scan", "hb_l2sq_topk_workspace",
            "hb_l2sq_topk", "hb_norm_topk_workspace", "hb_norm_topk", "hb_norm_scan_workspace",
            "hb_norm_scan", "hb_norm_scan_noalloc", "hb_merge_topk", "hb_pair_costs_workspace", "hb_pair_costs", "hb_restricted_ot_workspace",
-           "hb_restricted_ot_solve", "hb_filter_new_pairs_workspace", "hb_filter_new_pairs")
+           "hb_restricted_ot_solve", "hb_filter_new_pairs_workspace", "hb_filter_new_pairs",
+           "hb_prune_select_workspace", "hb_prune_select")
 
 
 class HBError(RuntimeError):
@@ -93,6 +94,11 @@ def load_library(path: Path | str = LIB_PATH):
     lib.hb_filter_new_pairs.restype = c_int
     lib.hb_filter_new_pairs.argtypes = [P, c_int64, c_int32, P, P, c_int64, c_int64, c_int64, P, P,
                                         ctypes.POINTER(c_int64), P, c_size_t, P]
+    lib.hb_prune_select_workspace.restype = c_size_t
+    lib.hb_prune_select_workspace.argtypes = [c_int64]
+    lib.hb_prune_select.restype = c_int
+    lib.hb_prune_select.argtypes = [P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int32, c_int64, P,
+                                    ctypes.POINTER(c_int64), P, c_size_t, P]
     lib.hb_norm_scan_workspace.restype = c_size_t
     lib.hb_norm_scan_workspace.argtypes = [c_int64, c_int64, c_int]
     lib.hb_norm_scan.restype = c_int

@@ -262,6 +262,26 @@ int hb_filter_new_pairs(const int64_t* active_keys, int64_t n_active, int32_t ac
                         int32_t* new_rows, int32_t* new_cols, int64_t* new_count, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Budgeted pruning: positions to remove from the active support.
+ *
+ * Replaces DualGapCleaning.select_indices_to_remove in protect-new mode with
+ * ActiveSupport.pruning_values (src/hello_ot/refinement/budgeted_pruning.py:27-57,
+ * 119-201; src/hello_ot/restricted_ot/active_support.py:401-421).
+ *
+ * An edge is removable when creation_iteration != current_inner_iter, != -1
+ * (structural) and |x_prev| <= 1e-15.  Reduced cost = costs - (duals[row] +
+ * duals[n_source + col]) in fp64, non-finite -> -inf.  *removable_count (host)
+ * receives the number of removable edges; when it is >= num_to_remove,
+ * positions receives the num_to_remove removable positions with the largest
+ * reduced costs, descending, equal values by ascending position.
+ * ------------------------------------------------------------------------- */
+size_t hb_prune_select_workspace(int64_t n_edges);
+int hb_prune_select(const int32_t* rows, const int32_t* cols, const double* costs, const double* x_prev,
+                    const int32_t* creation_iteration, int64_t n_edges, const double* duals, int64_t n_source,
+                    int64_t n_target, int32_t current_inner_iter, int64_t num_to_remove, int32_t* positions,
+                    int64_t* removable_count, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

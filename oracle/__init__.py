@@ -173,6 +173,26 @@ def filter_new_pairs(active_keys, rows, cols, n_target):
     return (keys // int(n_target)).astype(np.int32), (keys % int(n_target)).astype(np.int32), found, int(keys.size)
 
 
+def prune_select(rows, cols, costs, x_prev, creation, duals, n_source, num_to_remove, current_iter):
+    """Removal positions of DualGapCleaning in protect-new mode
+    (src/hello_ot/refinement/budgeted_pruning.py:27-57, 119-175; reduced costs as
+    ActiveSupport.pruning_values, src/hello_ot/restricted_ot/active_support.py:401-421).
+    Returns (positions int32 or None when too few are removable, removable count)."""
+    rows = np.asarray(rows, np.int64)
+    cols = np.asarray(cols, np.int64)
+    duals = np.asarray(duals, np.float64)
+    u, v = duals[:n_source], duals[n_source:]
+    rc = np.asarray(costs, np.float64) - (u[rows] + v[cols])
+    rc = np.where(np.isfinite(rc), rc, -np.inf)
+    creation = np.asarray(creation, np.int64)
+    removable = (creation != current_iter) & (creation != -1) & ~(np.abs(np.asarray(x_prev, np.float64)) > 1e-15)
+    idx = np.flatnonzero(removable)
+    if idx.size < num_to_remove:
+        return None, int(idx.size)
+    order = np.argsort(-rc[idx], kind="stable")
+    return idx[order[:num_to_remove]].astype(np.int32), int(idx.size)
+
+
 def load_ref(kind: str):
     """The reference's compiled CPU module ``hello_ot_cpp._scan`` / ``._lp``."""
     if not (REF_DIR / "hello_ot_cpp" / "__init__.py").exists():

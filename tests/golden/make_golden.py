@@ -49,6 +49,7 @@ from hello_ot._internal.lp.torch_restricted_ot import TorchRestrictedOTPDLP  # n
 from hello_ot.costs.pairs import _cost_pairs_lowrank_batched  # noqa: E402
 from hello_ot.costs.metric import pair_costs_metric  # noqa: E402
 from hello_ot.restricted_ot.active_support import ActiveSupport  # noqa: E402
+from hello_ot.refinement.budgeted_pruning import DualGapCleaning  # noqa: E402
 
 SCAN_L2SQ = [  # (name, q, n, d, k, seed, dual scale)
     ("l2sq_a", 37, 53, 8, 3, 1, 1.0),
@@ -170,6 +171,27 @@ def support_cases():
                             new_cols=nc.numpy(), found=found, new_count=new)
 
 
+def prune_cases():
+    """DualGapCleaning.select_indices_to_remove, protect-new mode (budgeted_pruning.py:177-201)."""
+    rng = np.random.default_rng(61)
+    for name, ns, nt, size, frac in (("a", 30, 40, 400, 0.2), ("b", 800, 600, 20000, 0.35)):
+        keys = rng.choice(ns * nt, size=size, replace=False)
+        rows, cols = keys // nt, keys % nt
+        costs = rng.random(size) * 3
+        x = np.where(rng.random(size) < 0.3, rng.random(size), 0.0)
+        creation = rng.integers(-2, 6, size).astype(np.int32)  # -1 structural, -2 initial, 5 = current
+        duals = rng.normal(size=ns + nt)
+        costs[:7] = np.round(costs[:7])   # a few exactly tied reduced costs
+        duals_t = duals.copy()
+        sup = ActiveSupport(n_source=ns, n_target=nt, device="cpu")
+        sup.initialize_from_arrays(rows=rows, cols=cols, costs=costs, x_prev=x, creation_iteration=creation)
+        num = int(frac * size)
+        out = DualGapCleaning().select_indices_to_remove(sup, num, duals=duals_t, n_source=ns, current_inner_iter=5)
+        np.savez_compressed(HERE / f"prune_{name}.npz", n_source=ns, n_target=nt, rows=rows.astype(np.int32),
+                            cols=cols.astype(np.int32), costs=costs, x=x, creation=creation, duals=duals,
+                            num=num, current=5, positions=np.asarray(out, np.int32))
+
+
 def pdlp_cases():
     cases = []
     rng = np.random.default_rng(12)
@@ -238,6 +260,7 @@ if __name__ == "__main__":
     for case in DIRECTIONAL:
         directional_case(*case)
     support_cases()
+    prune_cases()
     pdlp_cases()
     pairs_cases()
     print("fixtures written to", HERE)

@@ -161,3 +161,11 @@ def test_support_filter_oracle_matches_reference(oracle, path):
     nr, nc, found, new = oracle.filter_new_pairs(z["active_keys"], z["rows"], z["cols"], int(z["n_target"]))
     assert found == int(z["found"]) and new == int(z["new_count"])
     assert np.array_equal(nr, z["new_rows"]) and np.array_equal(nc, z["new_cols"])
+
+
+@pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("prune_*.npz")))
+def test_prune_oracle_matches_reference(oracle, path):
+    z = _load(path)
+    pos, _ = oracle.prune_select(z["rows"], z["cols"], z["costs"], z["x"], z["creation"], z["duals"],
+                                 int(z["n_source"]), int(z["num"]), int(z["current"]))
+    assert np.array_equal(pos, z["positions"])
