@@ -23,7 +23,8 @@ EXPORTS = ("hb_abi_version", "hb_last_error", "hb_kernel_launch_count", "hb_set_
            "hb_l2sq_topk", "hb_norm_topk_workspace", "hb_norm_topk", "hb_norm_scan_workspace",
            "hb_norm_scan", "hb_norm_scan_noalloc", "hb_merge_topk", "hb_pair_costs_workspace", "hb_pair_costs", "hb_restricted_ot_workspace",
            "hb_restricted_ot_solve", "hb_filter_new_pairs_workspace", "hb_filter_new_pairs",
-           "hb_prune_select_workspace", "hb_prune_select")
+           "hb_prune_select_workspace", "hb_prune_select", "hb_norm_scan_ex", "hb_norm_topk_ex",
+           "hb_pair_costs_ex")
 
 
 class HBError(RuntimeError):
@@ -39,6 +40,12 @@ class PdlpControls(ctypes.Structure):
                 ("time_limit_seconds", c_double), ("tol_objective", c_double), ("tol_primal", c_double),
                 ("tol_dual", c_double), ("initial_primal_weight", c_double), ("atomic_sums", c_int32),
                 ("pad", c_int32)]
+
+
+class Perturbation(ctypes.Structure):
+    """hb_perturbation: norm-cost noise (sigma == 0: none)."""
+    _fields_ = [("sigma", c_double), ("seed", c_int64), ("mode", c_int32), ("row_is_source", c_int32),
+                ("query_index", c_void_p), ("database_index", c_void_p), ("coefficients", c_int64 * 6)]
 
 
 class PdlpInfo(ctypes.Structure):
@@ -104,6 +111,10 @@ def load_library(path: Path | str = LIB_PATH):
     lib.hb_norm_scan.restype = c_int
     lib.hb_norm_scan.argtypes = [P, P, c_int64, c_int64, c_int64, P, P, c_int, c_int, c_int, P, P, P, P, P, P,
                                  c_size_t, P]
+    lib.hb_norm_scan_ex.restype = c_int
+    lib.hb_norm_scan_ex.argtypes = lib.hb_norm_scan.argtypes + [POINTER(Perturbation)]
+    lib.hb_norm_topk_ex.restype = c_int
+    lib.hb_norm_topk_ex.argtypes = lib.hb_norm_topk.argtypes + [POINTER(Perturbation)]
     lib.hb_norm_scan_noalloc.restype = c_int
     lib.hb_norm_scan_noalloc.argtypes = [P, P, c_int64, c_int64, c_int64, P, P, c_int, c_int, c_int, P, P, P, P, P, P]
     lib.hb_merge_topk.restype = c_int
@@ -112,6 +123,8 @@ def load_library(path: Path | str = LIB_PATH):
     lib.hb_pair_costs.restype = c_int
     lib.hb_pair_costs.argtypes = [c_int, P, P, c_int64, c_int64, c_int64, P, P, c_double, P, P, c_int64, P, P,
                                   c_size_t, P]
+    lib.hb_pair_costs_ex.restype = c_int
+    lib.hb_pair_costs_ex.argtypes = lib.hb_pair_costs.argtypes + [POINTER(Perturbation)]
     lib.hb_restricted_ot_workspace.restype = c_size_t
     lib.hb_restricted_ot_workspace.argtypes = [c_int64, c_int64, c_int64]
     lib.hb_restricted_ot_solve.restype = c_int

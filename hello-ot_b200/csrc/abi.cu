@@ -1,11 +1,13 @@
 // extern "C" entry points of libhello_b200.so (declared in include/hello_b200.h).
 // Argument validation, workspace sizing, stream synchronisation and the
 // translation of device status words into HB_* codes live here.
+#include <cmath>
 #include <cstdio>
 #include <string>
 
 #include "../../include/hello_b200.h"
 #include "common.cuh"
+#include "perturb.cuh"
 #include "scan_common.cuh"
 
 #include "internal.h"
@@ -99,6 +101,38 @@ int hb_last_kernel_times(double* ms, int capacity) {
     return n;
 }
 
+}  // extern "C"
+
+// hb_perturbation -> the kernels' parameters; false (with the message set) when invalid.
+static bool make_perturb(const hb_perturbation* in, hb::Perturb* out, bool pairs) {
+    *out = hb::Perturb{};
+    if (!in || in->sigma == 0.0) return true;
+    if (!std::isfinite(in->sigma) || in->sigma < 0.0 || (in->mode != 0 && in->mode != 1)) {
+        fail(HB_BAD_ARGUMENT, "perturbation: sigma must be finite and >= 0, mode 0 (rank2) or 1 (index_hash)");
+        return false;
+    }
+    if (!in->query_index || !in->database_index) {
+        fail(HB_BAD_ARGUMENT, "perturbation: global indices are required when sigma > 0");
+        return false;
+    }
+    if (pairs && !in->row_is_source) {
+        fail(HB_BAD_ARGUMENT, "perturbation: pair costs take source rows (row_is_source = 1)");
+        return false;
+    }
+    out->sigma = in->sigma;
+    out->seed_term = (float)((double)in->seed * 0.001);
+    out->mode = in->mode;
+    out->row_is_source = in->row_is_source != 0;
+    const int64_t* c = in->coefficients;
+    out->a0 = (float)c[0]; out->b0 = (float)c[1]; out->o0 = (float)c[2];
+    out->a1 = (float)c[3]; out->b1 = (float)c[4]; out->o1 = (float)c[5];
+    out->row_index = in->query_index;
+    out->col_index = in->database_index;
+    return true;
+}
+
+extern "C" {
+
 size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups) {
     if (q < 1 || n < 1 || d < 1 || !valid_k(k)) return 0;
     return hb::l2sq_bytes(q, n, d, k, precision, min_groups);
@@ -152,6 +186,16 @@ size_t hb_norm_scan_workspace(int64_t q, int64_t n, int k) {
 int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
                  int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
                  int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream) {
+    return hb_norm_scan_ex(x, y, q, n, d, f, g, cost_type, k, compute_stats, row_vals, row_idx, col_vals, col_idx,
+                           stats5, workspace, workspace_bytes, stream, nullptr);
+}
+
+int hb_norm_scan_ex(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
+                    int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
+                    int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream,
+                    const hb_perturbation* perturbation) {
+    hb::Perturb pert;
+    if (!make_perturb(perturbation, &pert, false)) return HB_BAD_ARGUMENT;
     if (!x || !y || !f || !g || !workspace) return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
     if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
         return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
@@ -164,7 +208,7 @@ int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     std::string err;
     int rc = hb::norm_scan(x, y, q, n, d, f, g, cost_type, k, compute_stats, row_vals, row_idx, col_vals, col_idx,
-                           stats5, workspace, workspace_bytes, st, err);
+                           stats5, workspace, workspace_bytes, st, err, false, &pert);
     if (rc) return fail(rc == 3 ? HB_WORKSPACE : HB_LAUNCH, err);
     return finish(st, nullptr, "norm scan");
 }
@@ -211,6 +255,15 @@ size_t hb_norm_topk_workspace(int64_t q, int64_t n, int k) {
 int hb_norm_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* g, int cost_type,
                  int k, int compute_stats, double* row_vals, int32_t* row_idx, double* stats2, void* workspace,
                  size_t workspace_bytes, void* stream) {
+    return hb_norm_topk_ex(x, y, q, n, d, g, cost_type, k, compute_stats, row_vals, row_idx, stats2, workspace,
+                           workspace_bytes, stream, nullptr);
+}
+
+int hb_norm_topk_ex(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* g, int cost_type,
+                    int k, int compute_stats, double* row_vals, int32_t* row_idx, double* stats2, void* workspace,
+                    size_t workspace_bytes, void* stream, const hb_perturbation* perturbation) {
+    hb::Perturb pert;
+    if (!make_perturb(perturbation, &pert, false)) return HB_BAD_ARGUMENT;
     if (!x || !y || !g || !workspace) return fail(HB_BAD_ARGUMENT, "null input or workspace pointer");
     if (!row_vals || !row_idx) return fail(HB_BAD_ARGUMENT, "null output pointer");
     if (q < 1 || n < 1 || d < 1 || q >= INT32_MAX || n >= INT32_MAX || d >= INT32_MAX)
@@ -227,7 +280,7 @@ int hb_norm_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d
                                                               ((hb::norm_bytes(q, n, k) + 7) & ~size_t(7)))
                                    : nullptr;
     int rc = hb::norm_scan(x, y, q, n, d, nullptr, g, cost_type, k, compute_stats, row_vals, row_idx, nullptr, nullptr,
-                           stats5, workspace, workspace_bytes, st, err, true);
+                           stats5, workspace, workspace_bytes, st, err, true, &pert);
     if (rc) return fail(rc == 3 ? HB_WORKSPACE : HB_LAUNCH, err);
     if (compute_stats) {
         cudaError_t e = cudaMemcpyAsync(stats2, stats5 + 1, sizeof(double), cudaMemcpyDeviceToDevice, st);
@@ -255,6 +308,16 @@ size_t hb_pair_costs_workspace(void) { return 256; }
 int hb_pair_costs(int cost_type, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d,
                   const double* a, const double* b, double dot_scale, const int64_t* rows, const int64_t* cols,
                   int64_t count, double* out, void* workspace, size_t workspace_bytes, void* stream) {
+    return hb_pair_costs_ex(cost_type, x, y, nx, ny, d, a, b, dot_scale, rows, cols, count, out, workspace,
+                            workspace_bytes, stream, nullptr);
+}
+
+int hb_pair_costs_ex(int cost_type, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d,
+                     const double* a, const double* b, double dot_scale, const int64_t* rows, const int64_t* cols,
+                     int64_t count, double* out, void* workspace, size_t workspace_bytes, void* stream,
+                     const hb_perturbation* perturbation) {
+    hb::Perturb pert;
+    if (!make_perturb(perturbation, &pert, true)) return HB_BAD_ARGUMENT;
     if (cost_type < 0 || cost_type > 3) return fail(HB_BAD_ARGUMENT, "cost_type must be 0..3");
     if (count < 0 || d < 1 || d >= INT32_MAX || nx < 1 || ny < 1) return fail(HB_BAD_ARGUMENT, "invalid sizes");
     if (count == 0) { g_error.clear(); return HB_OK; }
@@ -267,7 +330,8 @@ int hb_pair_costs(int cost_type, const float* x, const float* y, int64_t nx, int
     int* status = static_cast<int*>(workspace);
     cudaMemsetAsync(status, 0, sizeof(int), st);
     std::string err;
-    int rc = hb::pair_costs(cost_type, x, y, nx, ny, d, a, b, dot_scale, rows, cols, count, out, status, st, err);
+    int rc = hb::pair_costs(cost_type, x, y, nx, ny, d, a, b, dot_scale, rows, cols, count, out, status, st, err,
+                            &pert);
     if (rc) return fail(rc == 2 ? HB_BAD_ARGUMENT : HB_LAUNCH, err);
     return finish(st, status, "pair costs");
 }

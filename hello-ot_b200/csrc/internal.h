@@ -7,6 +7,8 @@
 
 namespace hb {
 
+struct Perturb;  // cost perturbation parameters (perturb.cuh)
+
 // Instrumentation: a process-wide count of kernel launches issued by this
 // library, and optional CUDA-event timing of the main kernels of a call.
 void count_launches(int n);
@@ -32,7 +34,8 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
 size_t norm_bytes(int64_t q, int64_t n, int k);
 int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
               int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
-              size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only = false);
+              size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only = false,
+              const struct Perturb* pert = nullptr);
 
 // partial top-k merge (scan_l2sq.cu): lists of `width` entries, bucket K >= width
 cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out,
@@ -43,7 +46,7 @@ cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t
 // pair costs (pairs.cu)
 int pair_costs(int kind, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d, const double* a,
                const double* b, double scale, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
-               int* status, cudaStream_t st, std::string& err);
+               int* status, cudaStream_t st, std::string& err, const Perturb* pert = nullptr);
 
 // restricted-OT PDHG (pdlp.cu)
 struct PdlpControls {

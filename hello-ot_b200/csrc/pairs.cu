@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "perturb.cuh"
 
 namespace hb {
 namespace pairs {
@@ -40,7 +41,8 @@ __global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, 
                                                    int64_t ny, int d, const double* __restrict__ a,
                                                    const double* __restrict__ b, double scale,
                                                    const int64_t* __restrict__ rows, const int64_t* __restrict__ cols,
-                                                   int64_t count, double* __restrict__ out, int* status) {
+                                                   int64_t count, double* __restrict__ out, int* status,
+                                                   const Perturb pert) {
     // warp-uniform loop: each warp walks its own contiguous block of edges,
     // 32/G consecutive edges per step
     const int lane = threadIdx.x & 31, sub = lane & (G - 1);
@@ -81,7 +83,11 @@ __global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, 
             } else if (KIND == 3) {
                 out[e] = (a[r] + b[c]) - scale * acc;
             } else {
-                out[e] = KIND == 2 ? sqrt(acc) : acc;
+                const double dist = KIND == 2 ? sqrt(acc) : acc;
+                // perturbed norm costs: the noise of (source row, target column) added in fp64
+                out[e] = pert.sigma != 0.0 ? dist + noise_of(pert, noise_input(pert, pert.row_index[r]),
+                                                                noise_input(pert, pert.col_index[c]))
+                                           : dist;
             }
         }
     }
@@ -90,10 +96,12 @@ __global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, 
 template <int KIND, int G>
 void launch_g(bool vec, const float* x, const float* y, int64_t nx, int64_t ny, int d, const double* a,
               const double* b, double s, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
-              int* status, int blocks, cudaStream_t st) {
+              int* status, int blocks, cudaStream_t st, const Perturb& pert) {
     timing_mark(st);
-    if (vec) pair_kernel<KIND, G, true><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status);
-    else pair_kernel<KIND, G, false><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status);
+    if (vec)
+        pair_kernel<KIND, G, true><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
+    else
+        pair_kernel<KIND, G, false><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
     timing_mark(st);
     count_launches(1);
 }
@@ -101,7 +109,7 @@ void launch_g(bool vec, const float* x, const float* y, int64_t nx, int64_t ny, 
 template <int KIND>
 void launch_kind(const float* x, const float* y, int64_t nx, int64_t ny, int d, const double* a, const double* b,
                  double s, const int64_t* rows, const int64_t* cols, int64_t count, double* out, int* status,
-                 cudaStream_t st, int sms) {
+                 cudaStream_t st, int sms, const Perturb& pert) {
     const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0);
     const int chunks = vec ? d / 4 : d;  // loads per edge
     const int g = chunks <= 1 ? 1 : chunks <= 2 ? 2 : chunks <= 4 ? 4 : chunks <= 8 ? 8 : chunks <= 16 ? 16 : 32;
@@ -109,12 +117,12 @@ void launch_kind(const float* x, const float* y, int64_t nx, int64_t ny, int d, 
     const int64_t cap = (int64_t)sms * 16;
     const int blocks = (int)(want < 1 ? 1 : (want > cap ? cap : want));
     switch (g) {
-        case 1: launch_g<KIND, 1>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
-        case 2: launch_g<KIND, 2>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
-        case 4: launch_g<KIND, 4>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
-        case 8: launch_g<KIND, 8>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
-        case 16: launch_g<KIND, 16>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
-        default: launch_g<KIND, 32>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st); break;
+        case 1: launch_g<KIND, 1>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
+        case 2: launch_g<KIND, 2>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
+        case 4: launch_g<KIND, 4>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
+        case 8: launch_g<KIND, 8>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
+        case 16: launch_g<KIND, 16>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
+        default: launch_g<KIND, 32>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
     }
 }
 
@@ -122,16 +130,18 @@ void launch_kind(const float* x, const float* y, int64_t nx, int64_t ny, int d, 
 
 int pair_costs(int kind, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d, const double* a,
                const double* b, double scale, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
-               int* status, cudaStream_t st, std::string& err) {
+               int* status, cudaStream_t st, std::string& err, const Perturb* pert_in) {
     if (count == 0) return 0;
+    Perturb pert;
+    if (pert_in && pert_in->sigma != 0.0 && kind != 3) pert = *pert_in;  // the l2^2 kind is never perturbed here
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     switch (kind) {
-        case 0: pairs::launch_kind<0>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
-        case 1: pairs::launch_kind<1>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
-        case 2: pairs::launch_kind<2>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
-        case 3: pairs::launch_kind<3>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms); break;
+        case 0: pairs::launch_kind<0>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms, pert); break;
+        case 1: pairs::launch_kind<1>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms, pert); break;
+        case 2: pairs::launch_kind<2>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms, pert); break;
+        case 3: pairs::launch_kind<3>(x, y, nx, ny, (int)d, a, b, scale, rows, cols, count, out, status, st, sms, pert); break;
         default: err = "unknown pair cost kind"; return 2;
     }
     cudaError_t e = cudaGetLastError();

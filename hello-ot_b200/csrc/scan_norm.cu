@@ -21,6 +21,7 @@
 #include "../../include/hello_b200.h"
 #include "common.cuh"
 #include "internal.h"
+#include "perturb.cuh"
 #include "scan_common.cuh"
 
 namespace hb {
@@ -40,6 +41,7 @@ struct Smem {
     double dbias[BN];      // the tile's column biases
     double rbx[BM];        // the tile's row biases (one-pass column epilogue)
     float cthr[BN];        // the tile's column thresholds (one pass)
+    float2 rnz[BM], cnz[BN];  // perturbation: noise inputs of the tile's rows and columns
     double red[8 * 5];
 };
 
@@ -59,6 +61,7 @@ struct Params {
     double* cval;   // [row groups * 2][n][K] column lists (per row group and row half)
     int* cidx;
     int* progress;  // [grid] tiles started by each CTA
+    Perturb pert;   // cost perturbation (sigma == 0: none)
 };
 
 template <int KIND>
@@ -127,6 +130,12 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
         u0 = rb0 * p.groups + g; ustep = p.groups; uend = rb1 > rb0 ? rb1 * p.groups : 0;
     }
     const int64_t list_base = ONE ? (int64_t)((blockIdx.x / p.groups) * 2 + half) * p.n : 0;
+    const bool perturbed = p.pert.sigma != 0.0;
+    // the cost of tile entry (rl, cl) in fp64, with the perturbation noise when it is on
+    auto pcost = [&](int rl, int cl) -> double {
+        const double c = (double)s.dist[rl][cl];
+        return perturbed ? c + noise_of(p.pert, s.rnz[rl], s.cnz[cl]) : c;
+    };
     int tile = 0;
     for (int u = u0; u < uend; u += ustep) {
         const int rb = u / p.groups, g = u % p.groups;
@@ -185,6 +194,10 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                     s.rbx[t] = rbias;  // thread t < BM owns row t (half 0)
                     s.cthr[t] = t < ncols ? order_value(p.ckey[c0 + t]) : INFINITY;
                 }
+                if (perturbed) {
+                    s.cnz[t] = t < ncols ? noise_input(p.pert, p.pert.col_index[c0 + t]) : make_float2(0.f, 0.f);
+                    s.rnz[t] = rvalid ? noise_input(p.pert, p.pert.row_index[row]) : make_float2(0.f, 0.f);
+                }
             }
             __syncthreads();
             if (rvalid) {
@@ -200,7 +213,7 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
 #pragma unroll 16
                 for (int j = 0; j < 64; ++j) {
                     const bool ok = j < live;
-                    const double cost = (double)s.dist[er][cb0 + j];
+                    const double cost = pcost(er, cb0 + j);
                     const double cbias = s.dbias[cb0 + j];
                     const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
                     if (STATS) {
@@ -224,7 +237,7 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                 while (K > 0 && mask) {
                     const int j = __ffsll(mask) - 1;
                     mask &= mask - 1;
-                    const double cost = (double)s.dist[er][cb0 + j];
+                    const double cost = pcost(er, cb0 + j);
                     const double cbias = s.dbias[cb0 + j];
                     const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
                     top.offer(sc, c0 + cb0 + j);
@@ -239,7 +252,7 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                     uint64_t cmask = 0;
 #pragma unroll 16
                     for (int r = 0; r < 64; ++r) {
-                        const double sc = (cb - (double)s.dist[r0 + r][c]) + s.rbx[r0 + r];
+                        const double sc = (cb - pcost(r0 + r, c)) + s.rbx[r0 + r];
                         cmask |= (r < rlive && sc >= thr) ? (1ull << r) : 0ull;
                     }
                     if (cmask) {
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                         while (cmask) {
                             const int r = __ffsll(cmask) - 1;
                             cmask &= cmask - 1;
-                            cl.offer((cb - (double)s.dist[r0 + r][c]) + s.rbx[r0 + r], rb * BM + r0 + r);
+                            cl.offer((cb - pcost(r0 + r, c)) + s.rbx[r0 + r], rb * BM + r0 + r);
                         }
 #pragma unroll
                         for (int q2 = 0; q2 < KK; ++q2) { p.cval[base + q2] = cl.v[q2]; p.cidx[base + q2] = cl.i[q2]; }
@@ -440,7 +453,7 @@ size_t norm_bytes(int64_t q, int64_t n, int k) {
 
 int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
               int kind, int k, int want_stats, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws,
-              size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only) {
+              size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only, const Perturb* pert) {
     const bool two_pass = (kind & HB_NORM_TWO_PASS) != 0;
     kind &= 0xF;
     const int K = k > 0 ? bucket_of(k) : 0;
@@ -450,6 +463,7 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     p.x = x; p.y = y; p.q = (int)q; p.n = (int)n; p.d = (int)d;
     p.q_bias = f; p.d_bias = g;
     p.part_v = L.pv1; p.part_i = L.pi1; p.cta_stats = L.cta;
+    if (pert && pert->sigma != 0.0) p.pert = *pert;
     cudaError_t e;
     if (L.one) {
         const int blocks = sm_count() * 8;
@@ -484,6 +498,8 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
         p2.q_bias = g; p2.d_bias = f;
         p2.part_v = L.pv2; p2.part_i = L.pi2;
+        std::swap(p2.pert.row_index, p2.pert.col_index);  // rows are the targets now
+        p2.pert.row_is_source = !p.pert.row_is_source;
         e = norm_kind<false, true>(kind, K, p2, L.p2.grid, st);
         if (e != cudaSuccess) { err = std::string("norm pass 2: ") + cudaGetErrorString(e); return 6; }
         e = merge_any(K, L.pv2, L.pi2, L.p2.groups * 2, n, k, cv, ci, st);

@@ -10,6 +10,8 @@ edge order; results come back as numpy unless the indices were torch tensors.
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -24,8 +26,9 @@ def _dev(a, device, dtype):
     return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype).to(device).contiguous()
 
 
-def pair_costs(kind: int, x, y, rows, cols, a=None, b=None, dot_scale: float = 1.0):
-    """Device entry: x, y CUDA fp32; rows, cols CUDA int64; returns CUDA fp64."""
+def pair_costs(kind: int, x, y, rows, cols, a=None, b=None, dot_scale: float = 1.0, perturbation=None):
+    """Device entry: x, y CUDA fp32; rows, cols CUDA int64; returns CUDA fp64.
+    perturbation (norm kinds): the (Perturbation, tensors) pair of perturb.make_perturbation."""
     L = lib()
     device = x.device
     x, y = x.contiguous(), y.contiguous()
@@ -41,9 +44,9 @@ def pair_costs(kind: int, x, y, rows, cols, a=None, b=None, dot_scale: float = 1
         b = b.to(device=device, dtype=torch.float64).contiguous()
     ws = Workspace.get(device, L.hb_pair_costs_workspace())
     with torch.cuda.device(device):
-        rc = L.hb_pair_costs(int(kind), ptr(x), ptr(y), x.shape[0], y.shape[0], x.shape[1], ptr(a), ptr(b),
-                             float(dot_scale), ptr(rows), ptr(cols), rows.numel(), ptr(out), ptr(ws), ws.numel(),
-                             stream_handle(device))
+        rc = L.hb_pair_costs_ex(int(kind), ptr(x), ptr(y), x.shape[0], y.shape[0], x.shape[1], ptr(a), ptr(b),
+                                float(dot_scale), ptr(rows), ptr(cols), rows.numel(), ptr(out), ptr(ws), ws.numel(),
+                                stream_handle(device), ctypes.byref(perturbation[0]) if perturbation else None)
     check(rc)
     return out
 
@@ -65,9 +68,9 @@ def cost_pairs_lowrank(level_cache, rows, cols, *, device=None, **_legacy):
 
 def pair_costs_metric(*, source_points, target_points, rows, cols, cost_type, perturbation=None,
                       compute_precision="fp64", cached_points=None, device=None, **_legacy):
-    """fp64 ℓ1/ℓ∞/ℓ2 cost of every edge."""
-    if perturbation is not None:
-        raise NotImplementedError("hello_ot_b200 does not implement cost perturbation")
+    """fp64 ℓ1/ℓ∞/ℓ2 cost of every edge (h/costs/metric.py:85), with the reference's
+    full-cost perturbation dict (mode "full_cost_perturb": sigma, seed, noise "rank2" /
+    "index_hash", source_global_index, target_global_index) added in fp64."""
     as_torch = torch.is_tensor(rows)
     if device is None:
         device = rows.device if as_torch and rows.is_cuda else torch.device("cuda", torch.cuda.current_device())
@@ -75,5 +78,16 @@ def pair_costs_metric(*, source_points, target_points, rows, cols, cost_type, pe
         src, tgt = cached_points
     else:
         src, tgt = _dev(source_points, device, torch.float32), _dev(target_points, device, torch.float32)
-    out = pair_costs(KIND[str(cost_type)], src, tgt, _dev(rows, device, torch.int64), _dev(cols, device, torch.int64))
+    pert = None
+    if (isinstance(perturbation, dict) and str(perturbation.get("mode", "")).strip().lower() == "full_cost_perturb"
+            and float(perturbation.get("sigma", 0.0)) != 0.0):
+        from .perturb import make_perturbation
+        si, ti = perturbation.get("source_global_index"), perturbation.get("target_global_index")
+        if si is None or ti is None:
+            raise ValueError("full metric perturbation requires source_global_index and target_global_index.")
+        pert = make_perturbation(src, tgt, _dev(si, device, torch.int64), _dev(ti, device, torch.int64),
+                                 float(perturbation["sigma"]), int(perturbation.get("seed", 0)),
+                                 str(perturbation.get("noise", "rank2")).strip().lower(), True, None)
+    out = pair_costs(KIND[str(cost_type)], src, tgt, _dev(rows, device, torch.int64), _dev(cols, device, torch.int64),
+                     perturbation=pert)
     return out if as_torch else out.cpu().numpy()

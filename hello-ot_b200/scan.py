@@ -16,6 +16,7 @@ Differences from the reference, all deliberate:
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import time
 from collections import Counter
@@ -26,6 +27,7 @@ import numpy as np
 import torch
 
 from ._lib import Workspace, check, lib, ptr, stream_handle
+from .perturb import make_perturbation
 
 BUCKETS = (1, 2, 4, 8, 16, 32)
 PRECISION = {"fp32": 3, "3xtf32": 3, "tf32": 1}
@@ -109,9 +111,10 @@ NORM_KIND = {"l1": 0, "linf": 1, "l2": 2, 0: 0, 1: 1, 2: 2}
 NORM_TWO_PASS = 0x10
 
 
-def norm_scan(x, y, f, g, k, cost_type, *, compute_stats=True, passes=None):
+def norm_scan(x, y, f, g, k, cost_type, *, compute_stats=True, passes=None, perturbation=None):
     """Bidirectional ℓ1/ℓ∞/ℓ2 scan on the CUDA cores (outputs as l2sq_scan).
-    k <= 8 makes one pass over the pairs unless passes=2 (same lists bit for bit)."""
+    k <= 8 makes one pass over the pairs unless passes=2 (same lists bit for bit).
+    perturbation: the (Perturbation, tensors) pair of perturb.make_perturbation, or None."""
     x, y, f, g = map(_c, (x, y, f, g))
     q, d = x.shape
     n = y.shape[0]
@@ -126,8 +129,9 @@ def norm_scan(x, y, f, g, k, cost_type, *, compute_stats=True, passes=None):
     stats = torch.zeros(5, dtype=torch.float64, device=dev)
     ws = Workspace.get(dev, L.hb_norm_scan_workspace(q, n, kk))
     with torch.cuda.device(dev):
-        rc = L.hb_norm_scan(ptr(x), ptr(y), q, n, d, ptr(f), ptr(g), kind, kk, int(bool(compute_stats)), ptr(rv),
-                            ptr(ri), ptr(cv), ptr(ci), ptr(stats), ptr(ws), ws.numel(), stream_handle(dev))
+        rc = L.hb_norm_scan_ex(ptr(x), ptr(y), q, n, d, ptr(f), ptr(g), kind, kk, int(bool(compute_stats)), ptr(rv),
+                               ptr(ri), ptr(cv), ptr(ci), ptr(stats), ptr(ws), ws.numel(), stream_handle(dev),
+                               ctypes.byref(perturbation[0]) if perturbation else None)
     check(rc)
     return rv[:, :kk], ri[:, :kk], cv[:, :kk], ci[:, :kk], stats
 
@@ -152,7 +156,7 @@ def l2sq_topk(x, y, x_bias, y_bias, k, *, dot_scale=2.0, precision="fp32"):
     return vals, idx
 
 
-def norm_topk(x, y, g, k, cost_type, *, compute_stats=False):
+def norm_topk(x, y, g, k, cost_type, *, compute_stats=False, perturbation=None):
     """One-sided ℓ1/ℓ∞/ℓ2 top-k on the CUDA cores: for every x row the best k of
     g_j - c_ij (fp64 score of the fp32 distance), descending, lower index on ties.
     Returns (scores q x k fp64, indices q x k int32, stats [sum c^2, max |c|] or None)."""
@@ -166,8 +170,9 @@ def norm_topk(x, y, g, k, cost_type, *, compute_stats=False):
     stats = torch.zeros(2, dtype=torch.float64, device=dev) if compute_stats else None
     ws = Workspace.get(dev, L.hb_norm_topk_workspace(q, n, int(k)))
     with torch.cuda.device(dev):
-        rc = L.hb_norm_topk(ptr(x), ptr(y), q, n, d, ptr(g), NORM_KIND[cost_type], int(k), int(bool(compute_stats)),
-                            ptr(vals), ptr(idx), ptr(stats), ptr(ws), ws.numel(), stream_handle(dev))
+        rc = L.hb_norm_topk_ex(ptr(x), ptr(y), q, n, d, ptr(g), NORM_KIND[cost_type], int(k),
+                               int(bool(compute_stats)), ptr(vals), ptr(idx), ptr(stats), ptr(ws), ws.numel(),
+                               stream_handle(dev), ctypes.byref(perturbation[0]) if perturbation else None)
     check(rc)
     return vals, idx, stats
 
@@ -182,7 +187,7 @@ class ScanExtension:
     """Scan entry points with the reference ABI (generic_scan.py:468-597)."""
 
     supports_assignment_statistics = False
-    supports_cost_perturbation = False
+    supports_cost_perturbation = True
     supports_fp64_accumulation = True
     index_hash_arithmetic = None
 
@@ -241,12 +246,14 @@ class ScanExtension:
                          compute_precision=0, collect_statistics=False):
         """[values q x k ascending c - g, indices int64 (, stats [sum c^2, max |c|])]
         (generic_scan.py:520-531 -> directional(minimum=True), initial.cu:34-107)."""
-        _no_perturbation(sigma)
         if compute_precision not in (0,):
             raise NotImplementedError("hello_ot_b200 norm scans compute fp32 distances (compute_precision=0)")
         _check(query, db, k, (dual_db, len(db)))
+        pert = make_perturbation(query, db, query_global_index, database_global_index, sigma, seed, perturb_mode,
+                                 row_is_source, index_hash_coeffs)
         self._record("norm_initial")
-        scores, ids, stats = norm_topk(query, db, dual_db, k, cost_type, compute_stats=bool(collect_statistics))
+        scores, ids, stats = norm_topk(query, db, dual_db, k, cost_type, compute_stats=bool(collect_statistics),
+                                       perturbation=pert)
         out = [scores.neg_(), ids.long()]
         if collect_statistics:
             out.append(stats)
@@ -267,12 +274,13 @@ class ScanExtension:
                                       row_is_source=True, index_hash_coeffs=None, compute_precision=0,
                                       rows_per_block_hint=8):
         """[rv, ri int64, cv, ci int64, num, den, max s+, max |c|, count int64] (generic_scan.py:533-543)."""
-        _no_perturbation(sigma)
         if compute_precision not in (0,):
             raise NotImplementedError("hello_ot_b200 norm scans compute fp32 distances (compute_precision=0)")
         _check(query, db, k, (query_dual, len(query)), (db_dual, len(db)))
+        pert = make_perturbation(query, db, query_global_index, database_global_index, sigma, seed, perturb_mode,
+                                 row_is_source, index_hash_coeffs)
         self._record("norm_pricing")
-        rv, ri, cv, ci, s = norm_scan(query, db, query_dual, db_dual, k, cost_type)
+        rv, ri, cv, ci, s = norm_scan(query, db, query_dual, db_dual, k, cost_type, perturbation=pert)
         return [rv, ri.long(), cv, ci.long(), s[0], s[1], s[2], s[3], s[4].long()]
 
     def fused_gcost_certificate(self, query, db, query_dual, db_dual, cost_type, query_global_index=None,
@@ -281,19 +289,23 @@ class ScanExtension:
         """[num, den, max s+, max |c|, count int64] (generic_scan.py:545-558)."""
         if isinstance(query_global_index, (int, bool)) and database_global_index is None:
             compute_denominator, query_global_index = query_global_index, None
-        _no_perturbation(sigma)
         _check(query, db, 1, (query_dual, len(query)), (db_dual, len(db)))
+        pert = make_perturbation(query, db, query_global_index, database_global_index, sigma, seed, perturb_mode,
+                                 row_is_source, index_hash_coeffs)
         self._record("norm_certificate")
-        s = norm_scan(query, db, query_dual, db_dual, 0, cost_type)[4]
+        s = norm_scan(query, db, query_dual, db_dual, 0, cost_type, perturbation=pert)[4]
         den = s[1] if compute_denominator else s[1].new_zeros(())
         return [s[0], den, s[2], s[3], s[4].long()]
 
     def fused_gcost_pairs(self, query, db, rows, cols, cost_type, source_index=None, target_index=None, sigma=0.,
                           seed=0, mode=1, coefficients=None):
-        """fp64 cost of each (row, col) edge (norm_cost_scan_kernel.cu:249-275)."""
-        _no_perturbation(sigma)
+        """fp64 cost of each (row, col) edge (norm_cost_scan_kernel.cu:249-275), plus the
+        perturbation noise of (source_index[row], target_index[col]) when sigma > 0."""
         from .pairs import pair_costs
-        return pair_costs(NORM_KIND[cost_type], query, db, rows, cols)
+        pert = None
+        if sigma is not None and float(sigma) != 0.0:
+            pert = make_perturbation(query, db, source_index, target_index, sigma, seed, mode, True, coefficients)
+        return pair_costs(NORM_KIND[cost_type], query, db, rows, cols, perturbation=pert)
 
 
 @dataclass

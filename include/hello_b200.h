@@ -88,6 +88,30 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
                  void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Cost perturbation of the norm costs (the _ex entry points below).
+ *
+ * Replaces the sigma > 0 arguments of the reference's fused norm kernels:
+ * NoiseParams / sigma_noise (src/hello_ot/_native/generic_scan/cost.cu:350-423,
+ * norm_cost_scan_kernel.cu:48-...), with the coefficients of
+ * src/hello_ot/costs/metric_perturbation.py:19-33 (_index_hash_parameters).
+ * The perturbed cost is c_ij + noise(source, target) in fp64; mode 1
+ * (index_hash) noise is sigma * fp32 hash of the two global indices, mode 0
+ * (rank2) fp32(sigma) * (__sinf(...) / 2 + 1/2).  query_index / database_index
+ * (device, int64) hold the global index of each x row / y row (for pair costs:
+ * of each source row / target row); row_is_source tells whether the x rows
+ * are the sources.  sigma == 0 (or a null pointer) means no perturbation.
+ * ------------------------------------------------------------------------- */
+typedef struct hb_perturbation {
+    double sigma;
+    int64_t seed;
+    int32_t mode;          /* 0 rank2, 1 index_hash */
+    int32_t row_is_source; /* 1: x rows are sources */
+    const int64_t* query_index;
+    const int64_t* database_index;
+    int64_t coefficients[6]; /* index_hash: (source, target, offset) for prime 2003, then for 2011 */
+} hb_perturbation;
+
+/* ---------------------------------------------------------------------------
  * ℓ2² directional top-k (one side only: the initial dual-assignment scan).
  *
  * Replaces ScanExtension.initialization_directional_topk_raw and its alias
@@ -122,6 +146,9 @@ size_t hb_norm_topk_workspace(int64_t q, int64_t n, int k);
 int hb_norm_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* g, int cost_type,
                  int k, int compute_stats, double* row_vals, int32_t* row_idx, double* stats2, void* workspace,
                  size_t workspace_bytes, void* stream);
+int hb_norm_topk_ex(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* g, int cost_type,
+                    int k, int compute_stats, double* row_vals, int32_t* row_idx, double* stats2, void* workspace,
+                    size_t workspace_bytes, void* stream, const hb_perturbation* perturbation);
 
 /* ---------------------------------------------------------------------------
  * ℓ1 / ℓ∞ / ℓ2 full-space pricing scan (CUDA cores), bidirectional top-k +
@@ -144,6 +171,10 @@ size_t hb_norm_scan_workspace(int64_t q, int64_t n, int k);
 int hb_norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
                  int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
                  int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream);
+int hb_norm_scan_ex(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* f, const double* g,
+                    int cost_type, int k, int compute_stats, double* row_vals, int32_t* row_idx, double* col_vals,
+                    int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes, void* stream,
+                    const hb_perturbation* perturbation);
 
 /* ---------------------------------------------------------------------------
  * Allocation-free variant of hb_norm_scan (no counterpart in the reference).
@@ -193,6 +224,10 @@ size_t hb_pair_costs_workspace(void);
 int hb_pair_costs(int cost_type, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d,
                   const double* a, const double* b, double dot_scale, const int64_t* rows, const int64_t* cols,
                   int64_t count, double* out, void* workspace, size_t workspace_bytes, void* stream);
+int hb_pair_costs_ex(int cost_type, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d,
+                     const double* a, const double* b, double dot_scale, const int64_t* rows, const int64_t* cols,
+                     int64_t count, double* out, void* workspace, size_t workspace_bytes, void* stream,
+                     const hb_perturbation* perturbation);
 
 /* ---------------------------------------------------------------------------
  * Restricted-OT Halpern-PDHG (balanced transport LP on the active support).

@@ -193,6 +193,27 @@ def prune_select(rows, cols, costs, x_prev, creation, duals, n_source, num_to_re
     return idx[order[:num_to_remove]].astype(np.int32), int(idx.size)
 
 
+def noise(src, tgt, sigma, seed, mode, coeffs):
+    """Norm-cost perturbation noise in fp64 (cost.cu:380-423 sigma_noise; the NumPy form
+    of metric_perturbation.py:35-59).  mode 1 (index_hash): every fp32 step rounded
+    on its own, bit for bit as the reference.  mode 0 (rank2): np.sin in fp32, an
+    approximation of the fused kernels' __sinf."""
+    src = np.asarray(src, np.int64)
+    tgt = np.asarray(tgt, np.int64)
+    f32 = np.float32
+    if int(mode) == 0:
+        z = (src.astype(f32) * f32(12.9898) + tgt.astype(f32) * f32(78.233)) + f32(int(seed) * 0.001)
+        v = np.sin(z).astype(f32) * f32(0.5) + f32(0.5)
+        return (f32(sigma) * v).astype(np.float64)
+    h = []
+    for prime, (a, b, o) in zip((2003, 2011), (coeffs[0:3], coeffs[3:6])):
+        s_, t_ = np.remainder(src, prime).astype(f32), np.remainder(tgt, prime).astype(f32)
+        x = ((f32(a) * s_ + f32(b) * t_) + s_ * t_) + f32(o)
+        h.append(x - f32(prime) * np.floor(x * f32(1.0 / prime)))
+    v = ((h[0] + f32(2003) * h[1]) + f32(0.5)) * f32(1.0 / 4028033.0)
+    return float(sigma) * v.astype(np.float64)
+
+
 def load_ref(kind: str):
     """The reference's compiled CPU module ``hello_ot_cpp._scan`` / ``._lp``."""
     if not (REF_DIR / "hello_ot_cpp" / "__init__.py").exists():

@@ -50,6 +50,8 @@ from hello_ot.costs.pairs import _cost_pairs_lowrank_batched  # noqa: E402
 from hello_ot.costs.metric import pair_costs_metric  # noqa: E402
 from hello_ot.restricted_ot.active_support import ActiveSupport  # noqa: E402
 from hello_ot.refinement.budgeted_pruning import DualGapCleaning  # noqa: E402
+from hello_ot.costs.metric_perturbation import (_apply_metric_pair_perturbation, _index_hash_parameters,  # noqa: E402
+                                                _metric_index_hash_noise_numpy)
 
 SCAN_L2SQ = [  # (name, q, n, d, k, seed, dual scale)
     ("l2sq_a", 37, 53, 8, 3, 1, 1.0),
@@ -192,6 +194,40 @@ def prune_cases():
                             num=num, current=5, positions=np.asarray(out, np.int32))
 
 
+def perturb_cases():
+    """Norm-cost perturbation (metric_perturbation.py): index-hash noise, its coefficients,
+    perturbed metric pair costs, and a perturbed torch norm scan (torch_scan.py:488-503)."""
+    rng = np.random.default_rng(71)
+    seed = 1234
+    src = np.concatenate([rng.integers(0, 5000, 400), rng.integers(0, 3_000_000, 400), [0, 2002, 2003, 4021]])
+    tgt = np.concatenate([rng.integers(0, 5000, 400), rng.integers(0, 3_000_000, 400), [2010, 2011, 0, 4022]])
+    coeffs = np.asarray(sum(_index_hash_parameters(seed), ()), np.int64)
+    x = rng.normal(size=(70, 9)).astype(np.float32)
+    y = rng.normal(size=(50, 9)).astype(np.float32)
+    rows, cols = rng.integers(0, 70, 600), rng.integers(0, 50, 600)
+    si, ti = rng.permutation(1_000_000)[:70], rng.permutation(1_000_000)[:50]
+    out = {}
+    for cost in ("l1", "l2", "linf"):
+        base = np.asarray(pair_costs_metric(source_points=x, target_points=y, rows=rows, cols=cols, cost_type=cost,
+                                            compute_precision="fp64"))
+        out[f"pairs_{cost}"] = np.asarray(_apply_metric_pair_perturbation(
+            base, rows, cols, {"mode": "full_cost_perturb", "sigma": 0.05, "seed": seed, "noise": "index_hash",
+                               "source_global_index": si, "target_global_index": ti}))
+    # a perturbed ℓ1 scan (the torch tile path adds the noise in the tile's dtype)
+    med = 6.0
+    f = rng.normal(size=70) * med * 0.4 + 0.5 * med
+    g = rng.normal(size=50) * med * 0.4 + 0.5 * med
+    pert = {"mode": "full_cost_perturb", "sigma": 0.3, "seed": seed, "noise": "index_hash",
+            "source_global_index": si, "target_global_index": ti}
+    res = bidirectional_violation_scan(source_points=x, target_points=y, source_offset=None, target_offset=None,
+                                       source_dual=f, target_dual=g, score_family="norm_cost", cost_type="l1",
+                                       dot_scale=1.0, topk=4, theta=0.0, device="cpu", perturbation=pert)
+    np.savez_compressed(HERE / "perturb.npz", src=src, tgt=tgt, seed=seed, coeffs=coeffs,
+                        noise=_metric_index_hash_noise_numpy(src, tgt, seed=seed), x=x, y=y, rows=rows, cols=cols,
+                        si=si, ti=ti, f=f, g=g, scan_rows=np.asarray(res.rows), scan_cols=np.asarray(res.cols),
+                        dual_feasibility=res.dual_feasibility, **out)
+
+
 def pdlp_cases():
     cases = []
     rng = np.random.default_rng(12)
@@ -261,6 +297,7 @@ if __name__ == "__main__":
         directional_case(*case)
     support_cases()
     prune_cases()
+    perturb_cases()
     pdlp_cases()
     pairs_cases()
     print("fixtures written to", HERE)

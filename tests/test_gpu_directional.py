@@ -130,7 +130,7 @@ def test_directional_input_errors(hb, cuda):
         ext.initialization_directional_topk_raw(x, x, v, v, 64, 64, 3, 2.0)
     with pytest.raises(ValueError, match="tile or scale"):
         ext.initialization_directional_topk_raw(x, x, v, v, 64, 64, 4, 3.0)
-    with pytest.raises(NotImplementedError, match="perturbation"):
+    with pytest.raises(ValueError, match="global indices"):  # sigma > 0 needs the global indices
         ext.fused_gcost_topk(x, x, v, 4, "l1", sigma=0.5)
     L = hb.lib()
     assert L.hb_l2sq_topk(x.data_ptr(), x.data_ptr(), 8, 8, 4, v.data_ptr(), v.data_ptr(), 64, 2.0, 3,

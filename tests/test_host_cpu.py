@@ -79,7 +79,7 @@ def test_scan_extension_validates_before_launch(hb):
         ext.fused_bidir_topk_stats_raw(x, x, v, v, v, v, 8, 8, 64, 2, True, True, False, 2, 2.0)
     with pytest.raises(ValueError, match="power-of-two bucket"):
         ext.fused_bidir_topk_stats_raw(x, x, v, v, v, v, 8, 8, 64, 3, True, True, False, 0, 2.0)
-    with pytest.raises(NotImplementedError, match="perturbation"):
+    with pytest.raises(ValueError):  # CPU tensors (and, with sigma > 0, no global indices)
         ext.fused_gcost_bidir_certificate(x, x, v, v, 2, 0, sigma=0.1)
 
 

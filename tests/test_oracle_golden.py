@@ -169,3 +169,19 @@ def test_prune_oracle_matches_reference(oracle, path):
     pos, _ = oracle.prune_select(z["rows"], z["cols"], z["costs"], z["x"], z["creation"], z["duals"],
                                  int(z["n_source"]), int(z["num"]), int(z["current"]))
     assert np.array_equal(pos, z["positions"])
+
+
+def test_perturbation_noise_matches_reference(oracle, hb):
+    """Index-hash noise bit for bit against the reference's NumPy form, and the
+    coefficients the host layer derives from the seed."""
+    z = _load("perturb.npz")
+    seed = int(z["seed"])
+    from hello_ot_b200.perturb import index_hash_coefficients  # host logic, no GPU
+    assert tuple(z["coeffs"].tolist()) == index_hash_coefficients(seed)
+    got = oracle.noise(z["src"], z["tgt"], 1.0, seed, 1, z["coeffs"])
+    assert np.array_equal(got, z["noise"].astype(np.float64))
+    # perturbed metric pair costs: fp64 distance + sigma * noise
+    for kind in ("l1", "l2", "linf"):
+        base = oracle.pair_costs(kind, z["x"], z["y"], z["rows"], z["cols"])
+        pert = base + oracle.noise(z["si"][z["rows"]], z["ti"][z["cols"]], 0.05, seed, 1, z["coeffs"])
+        np.testing.assert_allclose(pert, z[f"pairs_{kind}"], rtol=1e-13, atol=0)
