@@ -36,6 +36,14 @@ namespace pdlp {
 
 constexpr int RED_BLOCKS = 1184;  // reduction partial slots (8 per SM on a B200)
 constexpr int RED_THREADS = 256;
+// Iteration blocks of up to STEP_CAP iterations run as one CUDA graph whose
+// kernels read their per-iteration parameters from D.steps.
+constexpr int STEP_CAP = 8192;
+
+struct Step {
+    double primal_step, dual_step, halpern;
+    int checkpoint, major;
+};
 
 struct Dev {
     int n, m, nodes;
@@ -51,6 +59,7 @@ struct Dev {
     double* sd;     // [n] source dual / node scale, the value every edge of the row uses
     double *ssum, *tsum;  // [n], [m] node sums of the reflected primal (atomic mode; zero between passes)
     double* red;    // [RED_BLOCKS][8]
+    Step* steps;    // [frequency] the current block's per-iteration parameters
     double* scal;   // [16] reduced scalars
     int* status;
 };
@@ -160,10 +169,7 @@ __global__ void init_state(Dev D, const double* masses, const double* y0, const 
 }
 
 // ------------------------------------------------------------------ iteration
-struct Step {
-    double primal_step, dual_step, halpern;
-    int checkpoint, major;
-};
+
 
 // One PDHG iteration runs as three kernels (solver.cpp:255-281):
 //  edge_pass   : thread per edge, primal update, reflection, Halpern averaging
@@ -173,7 +179,8 @@ struct Step {
 //  target_pass : thread per target, ordered gather-sum and the target dual update.
 // Each node sums its edges sequentially in the reference's edge order.
 template <bool ATOMIC>
-__global__ void __launch_bounds__(256) edge_pass(Dev D, Step s) {
+__global__ void __launch_bounds__(256) edge_pass(Dev D, int it) {
+    const Step s = D.steps[it];
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int lane = threadIdx.x & 31;
     for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < D.e; base += stride) {  // block-uniform
@@ -233,7 +240,8 @@ __device__ __forceinline__ double warp_segment_sum(const double* __restrict__ va
 }
 
 template <bool ATOMIC>
-__global__ void __launch_bounds__(256) source_pass(Dev D, Step s) {
+__global__ void __launch_bounds__(256) source_pass(Dev D, int it) {
+    const Step s = D.steps[it];
     __shared__ double stage[ATOMIC ? 1 : 8][ATOMIC ? 1 : SEG_CHUNK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int v0 = (blockIdx.x * 8 + warp) * 32;
@@ -259,7 +267,8 @@ __global__ void __launch_bounds__(256) source_pass(Dev D, Step s) {
 }
 
 template <bool ATOMIC>
-__global__ void __launch_bounds__(256) target_pass(Dev D, Step s) {
+__global__ void __launch_bounds__(256) target_pass(Dev D, int it) {
+    const Step s = D.steps[it];
     const int stride = gridDim.x * blockDim.x;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < D.m; j += stride) {
         const int b0 = ATOMIC ? 0 : D.t_off[j], b1 = ATOMIC ? 0 : D.t_off[j + 1];
@@ -416,6 +425,8 @@ PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e)
     take_d(D.mass, nodes); take_d(D.scale, nodes); take_d(D.bs, nodes); take_d(D.ns, nodes); take_d(D.ay, nodes);
     take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m); take_d(D.sd, n); take_d(D.ssum, n); take_d(D.tsum, m);
     take_d(D.red, (size_t)pdlp::RED_BLOCKS * 8); take_d(D.scal, 16);
+    D.steps = ar.take<pdlp::Step>((size_t)pdlp::STEP_CAP);
+    if (base && !D.steps) L.ok = false;
     take_i(D.status, 1);
     take_i(L.r32, e); take_i(L.c32, e); take_i(L.iota, e); take_i(L.keys_out, e); take_i(L.t_orig, e);
     take_i(L.t_keys, e); take_i(L.inv, e);
@@ -526,6 +537,46 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     bool restart = false;
     int tlen = 0;
     const int F = ctl.frequency;
+    // One iteration: the three kernels reading D.steps[it].
+    auto launch_iteration = [&](cudaStream_t s_, int it, bool counted) {
+        if (ctl.atomic) {
+            pdlp::edge_pass<true><<<gb, 256, 0, s_>>>(D, it);
+            pdlp::source_pass<true><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);
+            pdlp::target_pass<true><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
+        } else {
+            pdlp::edge_pass<false><<<gb, 256, 0, s_>>>(D, it);
+            pdlp::source_pass<false><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);
+            pdlp::target_pass<false><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
+        }
+        if (counted) HB_LAUNCHED(3);
+    };
+    // A block of F iterations as one graph (captured on a private stream, launched on st):
+    // the fixed-point reductions run after iteration 0 (used when the block starts with a
+    // restart; their result is ignored otherwise) and after the last (major) iteration.
+    struct Graph {
+        cudaStream_t cs = nullptr;
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        ~Graph() {
+            if (exec) cudaGraphExecDestroy(exec);
+            if (g) cudaGraphDestroy(g);
+            if (cs) cudaStreamDestroy(cs);
+        }
+    } graph;
+    std::vector<pdlp::Step> hsteps((size_t)std::min(F, pdlp::STEP_CAP));
+    if (F <= pdlp::STEP_CAP && cudaStreamCreateWithFlags(&graph.cs, cudaStreamNonBlocking) == cudaSuccess &&
+        cudaStreamBeginCapture(graph.cs, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        for (int t = 0; t < F; ++t) {
+            launch_iteration(graph.cs, t, false);  // captured, not launched
+            if (t == 0 || t == F - 1) {
+                pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, graph.cs>>>(D);
+                pdlp::finish_red<<<1, 32, 0, graph.cs>>>(D.red, pdlp::RED_BLOCKS, 3, D.scal, t == F - 1 ? 9 : 5);
+            }
+        }
+        const bool captured = cudaStreamEndCapture(graph.cs, &graph.g) == cudaSuccess && graph.g;
+        if (!captured || cudaGraphInstantiate(&graph.exec, graph.g, 0) != cudaSuccess) graph.exec = nullptr;
+        cudaGetLastError();  // a failed capture leaves the direct launches below
+    }
     for (;;) {
         pdlp::evaluate_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D, vb, objective);
         HB_LAUNCHED(1);
@@ -593,36 +644,37 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         }
         const double primal_step = 0.998 / weight, dual_step = 0.998 * weight;
         const bool first_block = count == 0;
-        if (first_block) timing_mark(st);
-        for (int t = 0; t < F; ++t) {
+        auto step_of = [&](int t) {
             pdlp::Step s;
             s.primal_step = primal_step;
             s.dual_step = dual_step;
-            s.halpern = double(inner + 1) / double(inner + 2);
-            s.major = ((count + 1) % F) == 0;
-            const bool is_restart = t == 0 && restart;
-            s.checkpoint = s.major || is_restart;
-            if (ctl.atomic) {
-                pdlp::edge_pass<true><<<gb, 256, 0, st>>>(D, s);
-                pdlp::source_pass<true><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(D, s);
-                pdlp::target_pass<true><<<(unsigned)((m + 255) / 256), 256, 0, st>>>(D, s);
-            } else {
-                pdlp::edge_pass<false><<<gb, 256, 0, st>>>(D, s);
-                pdlp::source_pass<false><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(D, s);
-                pdlp::target_pass<false><<<(unsigned)((m + 255) / 256), 256, 0, st>>>(D, s);
+            s.halpern = double(inner + t + 1) / double(inner + t + 2);
+            s.major = ((count + t + 1) % F) == 0;
+            s.checkpoint = s.major || (t == 0 && restart);
+            return s;
+        };
+        if (first_block) timing_mark(st);
+        if (graph.exec) {
+            for (int t = 0; t < F; ++t) hsteps[t] = step_of(t);
+            if (cudaMemcpyAsync(D.steps, hsteps.data(), sizeof(pdlp::Step) * F, cudaMemcpyHostToDevice, st) !=
+                    cudaSuccess || cudaGraphLaunch(graph.exec, st) != cudaSuccess)
+                return fail("iteration block");
+            HB_LAUNCHED(3 * F + (F == 1 ? 2 : 4));
+        } else {
+            for (int t = 0; t < F; ++t) {
+                hsteps[0] = step_of(t);
+                cudaMemcpyAsync(D.steps, hsteps.data(), sizeof(pdlp::Step), cudaMemcpyHostToDevice, st);
+                launch_iteration(st, 0, true);
+                if (hsteps[0].checkpoint) {
+                    pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);
+                    // scal[5..7]: terms at the restart iteration, scal[9..11]: at the major iteration
+                    pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 3, D.scal, hsteps[0].major ? 9 : 5);
+                    HB_LAUNCHED(2);
+                }
             }
-            HB_LAUNCHED(2);
-            HB_LAUNCHED(1);
-            if (s.checkpoint) {
-                pdlp::fixed_point_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D);
-                HB_LAUNCHED(1);
-                // scal[5..7]: terms at the restart iteration, scal[9..11]: at the major iteration
-                pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 3, D.scal, s.major ? 9 : 5);
-                HB_LAUNCHED(1);
-            }
-            ++count;
-            ++inner;
         }
+        count += F;
+        inner += F;
         if (first_block) timing_mark(st);
         if (cudaGetLastError() != cudaSuccess) return fail("iteration");
     }
