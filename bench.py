@@ -56,7 +56,7 @@ DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 2.379, (256, "fp32", "two-pass
 # the PDHG; config 3 (n = m = 262144, d = 128) for the l1 scan
 PATH_SIZES = {"scan": (1_048_576, 256), "initial": (1_048_576, 256), "pairs": (1_048_576, 256),
               "pdlp": (1_048_576, 256), "norm": (262_144, 128), "support": (1_048_576, 256),
-              "prune": (1_048_576, 256)}
+              "prune": (1_048_576, 256), "coarsest": (1024, 32)}
 
 
 def parse_args():
@@ -65,11 +65,13 @@ def parse_args():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial", "support", "prune"],
+    p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial", "support", "prune",
+                                                   "coarsest"],
                    help="scan (default, the headline): l2sq pricing scan; norm: l1 scan (config 3 shape); "
                         "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations; "
                         "initial: l2sq directional top-16 scan (config 5 shape); "
-                        "support: active-support candidate filter; prune: budgeted pruning selection")
+                        "support: active-support candidate filter; prune: budgeted pruning selection; "
+                        "coarsest: dense exact transport of a coarsest level (n = m = 1024, d = 32)")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
     p.add_argument("--n", type=int, default=None, help="points per side (default: the path's config)")
     p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
@@ -730,6 +732,68 @@ def run_prune(args, hb, dev, peaks):
            "n": n, "m": m, "edges": e, "remove": num}, extra)
 
 
+def coarsest_problem(n, d, seed):
+    """A coarsest level of config 1's shape: x ~ N(0, I), y = z + 2 tanh(z), uniform
+    masses, dense l2sq cost (fp64)."""
+    rng = np.random.default_rng(seed)
+    x = rng.normal(size=(n, d))
+    z = rng.normal(size=(n, d))
+    y = z + 2.0 * np.tanh(z)
+    cost = (x * x).sum(1)[:, None] + (y * y).sum(1)[None, :] - 2.0 * x @ y.T
+    return np.maximum(cost, 0.0), np.full(n, 1.0 / n), np.full(n, 1.0 / n)
+
+
+def run_coarsest(args, hb, dev, peaks):
+    """Coarsest-level exact transport (the POT ot.emd leaf solve of the reference): a step
+    is one dense n x n solve to relative KKT 1e-9 with the plan, duals and distance
+    returned; metric solves/s.  value: cost resident on the device; e2e: host cost in,
+    host plan and duals out."""
+    n, d = args.n, args.d
+    cost, a, b = coarsest_problem(n, d, 42)
+    C, A, B = (torch.as_tensor(v, device=dev) for v in (cost, a, b))
+    out = {}
+
+    def dev_step():
+        out["r"] = hb.solve_leaf_from_cost(cost=C, source_mass=A, target_mass=B, tolerance=1e-9, device=dev)
+
+    sec = _timed(dev_step, args, dev)
+    r = out["r"]
+    iters = r["iterations"]
+    e2e_sec = None
+    if not args.no_e2e:
+        e2e_sec = _timed(lambda: hb.solve_leaf_from_cost(cost=cost, source_mass=a, target_mass=b, tolerance=1e-9,
+                                                         device=dev), args, dev)
+    e = n * n
+    bytes_iter = 44 * e + 32 * (2 * n)
+    achieved = bytes_iter * iters / sec / 1e9
+    extra = {"dtype": "f64", "roofline": {
+        "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+        "kernel": "hb::pdlp iterations on the complete support (whole solve incl. evaluations and restarts)",
+        "bytes_per_iteration": bytes_iter, "iterations": iters},
+        "objective": r["distance"], "termination": r["termination_reason"]}
+    if e2e_sec is not None:
+        extra["e2e"] = {"value": 1.0 / e2e_sec, "unit": "solves/s", "h2d_bytes_per_step": 8 * (e + 2 * n),
+                        "d2h_bytes_per_step": 16 * len(r["warm_start_state"].x_prev) + 8 * 2 * n}
+    if not args.no_cpu:  # the reference's C++ PDHG (solver.cpp) on the same LP; POT is absent here
+        import oracle
+        lp = oracle.load_ref("lp")
+        threads = os.cpu_count() or 1
+        rows = np.repeat(np.arange(n), n)
+        cols = np.tile(np.arange(n), n)
+        t0 = time.perf_counter()
+        ref = lp.solve_once(rows, cols, cost.ravel(), np.concatenate((a, b)), np.zeros(e), np.zeros(2 * n), n,
+                            threads, 200, 3600.0, 10 ** 7, 1e-9, 1e-9, 1e-9, False, False)
+        dt = time.perf_counter() - t0
+        extra["cpu_baseline"] = {"value": 1.0 / dt, "unit": "solves/s", "cores": threads, "kind": "reference",
+                                 "sample": f"one solve of the same LP by the reference C++ PDHG (solve_once, "
+                                           f"{ref['iterations']} iterations, objective {ref['obj_val']:.12g}); "
+                                           "the reference's POT network simplex is not installed"}
+    _line(args, "coarsest exact solves/s", 1.0 / sec, "solves/s", sec,
+          {"workload": f"coarsest level, dense {n} x {n} l2sq OT, d={d}, relative KKT 1e-9",
+           "n": n, "d": d, "edges": e}, extra)
+
+
 def run_other(args):
     import __graft_entry__ as entry
 
@@ -738,7 +802,7 @@ def run_other(args):
     torch.cuda.set_device(dev)
     peaks, _ = load_peaks()
     {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm, "initial": run_initial,
-     "support": run_support, "prune": run_prune}[args.path](args, hb, dev, peaks)
+     "support": run_support, "prune": run_prune, "coarsest": run_coarsest}[args.path](args, hb, dev, peaks)
 
 
 def main():

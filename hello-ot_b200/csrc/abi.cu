@@ -359,7 +359,10 @@ int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const doubl
     ctl.tol_dual = controls->tol_dual;
     ctl.rescale = controls->scalar_rescaling;
     ctl.weight0 = controls->initial_primal_weight;
-    ctl.atomic = controls->atomic_sums != 0;
+    if (controls->atomic_sums < HB_PDLP_SUMS_ORDERED || controls->atomic_sums > HB_PDLP_SUMS_TREE)
+        return fail(HB_BAD_ARGUMENT, "atomic_sums must be one of HB_PDLP_SUMS_ORDERED, _ATOMIC, _TREE");
+    ctl.atomic = controls->atomic_sums == HB_PDLP_SUMS_ATOMIC;
+    ctl.tree = controls->atomic_sums == HB_PDLP_SUMS_TREE;
     hb::PdlpResult r{};
     static_assert(sizeof(hb::TraceRow) == sizeof(hb_pdlp_trace_row), "trace row layout");
     int tlen = 0;

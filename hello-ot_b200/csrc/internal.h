@@ -57,6 +57,7 @@ struct PdlpControls {
     int rescale;
     double weight0;  // > 0: initial primal weight instead of the norm ratio
     int atomic;      // node sums by atomics in the edge pass (order varies run to run)
+    int tree;        // high-degree sides summed by a fixed lane tree (not the reference's order)
 };
 struct PdlpResult {
     int64_t iterations, restarts;

@@ -293,6 +293,76 @@ __global__ void __launch_bounds__(256) target_pass(Dev D, int it) {
     }
 }
 
+// Wide variants for high-degree nodes (mean degree >= WIDE_DEGREE, e.g. the complete
+// support of a coarsest level): one warp per node.  The warp stages the node's
+// reflected primal values (contiguous for sources, gathered through t_pos for
+// targets) into shared memory in chunks of SEG_CHUNK, and lane 0 adds them in edge
+// order, so the sums are the same as the thread-per-node passes'.
+constexpr int WIDE_DEGREE = 64;
+
+__device__ __forceinline__ void dual_update(const Dev& D, const Step& s, int i, double sum) {
+    const double yv = D.y[i];
+    const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+    const double refl = 2.0 * pyv - yv;
+    if (s.checkpoint) D.dy[i] = refl - yv;
+    const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+    D.y[i] = ynew;
+    if (s.major) D.py[i] = pyv;
+    if (i < D.n) D.sd[i] = ynew / D.ns[i];
+    else D.td[i - D.n] = ynew / D.ns[i];
+}
+
+// Blocks [0, src_blocks) take sources, the next tgt_blocks blocks take targets: the two
+// sides only read the edge pass's output, so one launch runs both side by side.
+// TREE: every lane adds its own strided values in order, then a fixed butterfly over
+// the lanes (a deterministic order, not the reference's; no serial chain).
+constexpr int WIDE_CHUNK = 512;
+template <bool TREE>
+__global__ void __launch_bounds__(256) node_pass_wide(Dev D, int it, int src_blocks) {
+    __shared__ double stage[TREE ? 1 : 8][TREE ? 1 : WIDE_CHUNK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool target = (int)blockIdx.x >= src_blocks;  // block-uniform
+    const int v = ((int)blockIdx.x - (target ? src_blocks : 0)) * 8 + warp;
+    if (v >= (target ? D.m : D.n)) return;  // warp-uniform
+    const int* off = target ? D.t_off : D.s_off;
+    const int b0 = off[v], b1 = off[v + 1];
+    double* st = stage[TREE ? 0 : warp];
+    double sum = 0.0;
+    for (int c0 = b0; c0 < b1; c0 += WIDE_CHUNK) {
+        const int c1 = min(b1, c0 + WIDE_CHUNK);
+        // all of a lane's loads of the chunk in flight at once (positions, then values)
+        constexpr int PER_LANE = WIDE_CHUNK / 32;
+        int pos[PER_LANE];
+#pragma unroll
+        for (int u = 0; u < PER_LANE; ++u) {
+            const int q = c0 + u * 32 + lane;
+            pos[u] = q < c1 ? (target ? __ldg(D.t_pos + q) : q) : -1;
+        }
+        double val[PER_LANE];
+#pragma unroll
+        for (int u = 0; u < PER_LANE; ++u) val[u] = pos[u] >= 0 ? __ldg(D.rx + pos[u]) : 0.0;
+        if (TREE) {
+#pragma unroll
+            for (int u = 0; u < PER_LANE; ++u) sum += val[u];
+            continue;
+        }
+#pragma unroll
+        for (int u = 0; u < PER_LANE; ++u) st[u * 32 + lane] = val[u];
+        __syncwarp();
+        if (lane == 0) {
+            const int len = c1 - c0;
+#pragma unroll 8
+            for (int q = 0; q < len; ++q) sum += st[q];
+        }
+        __syncwarp();
+    }
+    if (TREE) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    if (lane == 0) dual_update(D, D.steps[it], target ? D.n + v : v, sum);
+}
+
 // ------------------------------------------------------------------ reductions
 template <int CNT>
 __device__ __forceinline__ void block_store(double (&v)[CNT], double* red) {
@@ -537,6 +607,8 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     bool restart = false;
     int tlen = 0;
     const int F = ctl.frequency;
+    const bool wide_sources = e >= (int64_t)pdlp::WIDE_DEGREE * n, wide_targets = e >= (int64_t)pdlp::WIDE_DEGREE * m;
+    const int per_iter = (!ctl.atomic && wide_sources && wide_targets) ? 2 : 3;  // kernels per iteration
     // One iteration: the three kernels reading D.steps[it].
     auto launch_iteration = [&](cudaStream_t s_, int it, bool counted) {
         if (ctl.atomic) {
@@ -545,10 +617,15 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             pdlp::target_pass<true><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
         } else {
             pdlp::edge_pass<false><<<gb, 256, 0, s_>>>(D, it);
-            pdlp::source_pass<false><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);
-            pdlp::target_pass<false><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
+            const int sb = wide_sources ? (n + 7) / 8 : 0, tb = wide_targets ? (m + 7) / 8 : 0;
+            if (sb + tb > 0) {
+                if (ctl.tree) pdlp::node_pass_wide<true><<<(unsigned)(sb + tb), 256, 0, s_>>>(D, it, sb);
+                else pdlp::node_pass_wide<false><<<(unsigned)(sb + tb), 256, 0, s_>>>(D, it, sb);
+            }
+            if (!wide_sources) pdlp::source_pass<false><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);
+            if (!wide_targets) pdlp::target_pass<false><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
         }
-        if (counted) HB_LAUNCHED(3);
+        if (counted) HB_LAUNCHED(per_iter);
     };
     // A block of F iterations as one graph (captured on a private stream, launched on st):
     // the fixed-point reductions run after iteration 0 (used when the block starts with a
@@ -659,7 +736,7 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             if (cudaMemcpyAsync(D.steps, hsteps.data(), sizeof(pdlp::Step) * F, cudaMemcpyHostToDevice, st) !=
                     cudaSuccess || cudaGraphLaunch(graph.exec, st) != cudaSuccess)
                 return fail("iteration block");
-            HB_LAUNCHED(3 * F + (F == 1 ? 2 : 4));
+            HB_LAUNCHED(per_iter * F + (F == 1 ? 2 : 4));
         } else {
             for (int t = 0; t < F; ++t) {
                 hsteps[0] = step_of(t);

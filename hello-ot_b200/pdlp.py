@@ -20,6 +20,7 @@ import torch
 from ._lib import PdlpControls, PdlpInfo, PdlpTraceRow, Workspace, check, lib, ptr, stream_handle
 
 REASONS = {1: "OPTIMAL", 2: "ITERATION_LIMIT", 3: "NUMERICAL_DIVERGENCE", 4: "TIME_LIMIT"}
+SUMMATION = {"ordered": 0, "atomic": 1, "tree": 2}  # hb_pdlp_controls.atomic_sums (HB_PDLP_SUMS_*)
 
 
 @dataclass
@@ -52,10 +53,14 @@ class NativeRestrictedOTPDLP:
 
     def __init__(self, *, device="cuda", evaluation_frequency: int = 200, time_limit_seconds: float = 3600.0,
                  iteration_limit: int = np.iinfo(np.int32).max, record_state_trace: bool = False,
-                 initial_primal_weight: float = 0.0, deterministic: bool = True):
-        """deterministic=False accumulates the node sums with atomics in the edge pass:
-        about 1.5x faster per iteration on large random supports, but the summation
-        order (so the last bits of the iterates) varies from run to run."""
+                 initial_primal_weight: float = 0.0, deterministic: bool = True, summation: str = None):
+        """summation (node sums of the primal): "ordered" (the default) adds each node's
+        edges in the reference's order, bit-identical to it; "atomic" (also chosen by
+        deterministic=False) accumulates with atomics in the edge pass, about 1.5x faster
+        per iteration on large random supports, but the order (so the last bits of the
+        iterates) varies from run to run; "tree" is "ordered" except on a side whose mean
+        degree is >= 64 (a dense support), where a fixed lane tree adds each node's edges:
+        reproducible run to run, not the reference's order, several times faster there."""
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("NativeRestrictedOTPDLP runs on CUDA devices only")
@@ -66,7 +71,12 @@ class NativeRestrictedOTPDLP:
         self.iteration_limit = int(iteration_limit)
         self.record_state_trace = bool(record_state_trace)
         self.initial_primal_weight = float(initial_primal_weight)
-        self.deterministic = bool(deterministic)
+        if summation is None:
+            summation = "ordered" if deterministic else "atomic"
+        if summation not in SUMMATION:
+            raise ValueError(f"summation must be one of {sorted(SUMMATION)}")
+        self.summation = summation
+        self.deterministic = summation != "atomic"
         if self.evaluation_frequency < 1:
             raise ValueError("evaluation_frequency must be >= 1")
         if self.time_limit_seconds <= 0.0 or self.iteration_limit < 1:
@@ -122,7 +132,7 @@ class NativeRestrictedOTPDLP:
         y_out = torch.empty(n + m, dtype=torch.float64, device=dev)
         ctl = PdlpControls(self.evaluation_frequency, int(bool(scalar_rescaling)), self.iteration_limit,
                            self.time_limit_seconds, objective_tolerance, primal_tolerance, dual_tolerance,
-                           self.initial_primal_weight, int(not self.deterministic), 0)
+                           self.initial_primal_weight, SUMMATION[self.summation], 0)
         info = PdlpInfo()
         cap = 4096 if self.record_state_trace else 0
         trace = (PdlpTraceRow * max(cap, 1))()

@@ -251,11 +251,19 @@ typedef struct hb_pdlp_controls {
     double time_limit_seconds;
     double tol_objective, tol_primal, tol_dual;
     double initial_primal_weight;  /* > 0 overrides the initial norm-ratio weight */
-    int32_t atomic_sums;           /* 1: node sums accumulated with atomics in the edge pass (faster; the
-                                      summation order, so the last bits, vary from run to run);
-                                      0: ordered sums, the reference's order, bit-reproducible */
+    int32_t atomic_sums;           /* node-sum order, one of HB_PDLP_SUMS_*:
+                                      ORDERED (0): each node sums its edges in the reference's order,
+                                        bit-reproducible and bit-identical to the reference;
+                                      ATOMIC (1): atomics in the edge pass (fastest on large random
+                                        supports; the order, so the last bits, vary run to run);
+                                      TREE (2): as ORDERED, except that a side whose mean degree is
+                                        >= 64 (a dense support, e.g. a coarsest level) sums each node
+                                        in a fixed lane-strided tree: bit-reproducible run to run,
+                                        not the reference's order, several times faster there */
     int32_t pad;
 } hb_pdlp_controls;
+
+enum { HB_PDLP_SUMS_ORDERED = 0, HB_PDLP_SUMS_ATOMIC = 1, HB_PDLP_SUMS_TREE = 2 };
 
 enum { HB_PDLP_OPTIMAL = 1, HB_PDLP_ITERATION_LIMIT = 2, HB_PDLP_NUMERICAL_DIVERGENCE = 3, HB_PDLP_TIME_LIMIT = 4 };
 

@@ -67,11 +67,23 @@ def _random_support(ns, nt, extra, seed):
     return rows[perm], cols[perm], rng.random(rows.size) * 3, wa / wa.sum(), wb / wb.sum()
 
 
-@pytest.mark.parametrize("shape", [(30, 40, 180), (300, 400, 4000), (1000, 700, 20000)])
+def _complete_support(ns, nt, seed):
+    rng = np.random.default_rng(seed)
+    rows, cols = np.repeat(np.arange(ns), nt), np.tile(np.arange(nt), ns)
+    perm = rng.permutation(rows.size)
+    wa, wb = rng.uniform(0.5, 1.5, ns), rng.uniform(0.5, 1.5, nt)
+    return rows[perm], cols[perm], rng.random(rows.size) * 3, wa / wa.sum(), wb / wb.sum()
+
+
+# (sources, targets, extra edges) of a random support; extra == -1: the complete support
+# (mean degree >= 64 on both sides, or on the source side only: the warp-per-node passes)
+@pytest.mark.parametrize("shape", [(30, 40, 180), (300, 400, 4000), (1000, 700, 20000), (96, 130, -1),
+                                   (40, 700, -1)])
 def test_pdlp_block_is_bit_exact(hb, cuda, oracle, shape):
     """One block of iterations with the same step sizes reproduces the reference
     arithmetic exactly (no restart inside the block)."""
-    rows, cols, c, a, b = _random_support(*shape, seed=shape[0])
+    rows, cols, c, a, b = (_complete_support(shape[0], shape[1], 3) if shape[2] < 0
+                           else _random_support(*shape, seed=shape[0]))
     F = 60
     ref = oracle.pdlp(rows, cols, c, a, b, frequency=F, iteration_limit=F, tolerance=0.0)
     solver = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=F, iteration_limit=F,
@@ -115,6 +127,28 @@ def test_pdlp_atomic_sums_converge_like_oracle(hb, cuda, oracle, shape):
     np.testing.assert_allclose(out.y.cpu().numpy(), blk["y"], rtol=1e-9, atol=1e-12 * np.abs(blk["y"]).max())
 
 
+@pytest.mark.parametrize("shape", [(96, 130), (40, 700), (300, 20)])
+def test_pdlp_tree_sums(hb, cuda, oracle, shape):
+    """summation="tree" on complete supports: one block within round-off of the
+    reference's ordered sums, bit-reproducible from run to run, and the same solve."""
+    rows, cols, c, a, b = _complete_support(*shape, seed=11)
+    F = 60
+    blk = oracle.pdlp(rows, cols, c, a, b, frequency=F, iteration_limit=F, tolerance=0.0)
+    outs = []
+    for _ in range(2):
+        s = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=F, iteration_limit=F, summation="tree",
+                                      initial_primal_weight=blk["primal_weight"])
+        outs.append(s.solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=0.0))
+    assert torch.equal(outs[0].x, outs[1].x) and torch.equal(outs[0].y, outs[1].y)
+    np.testing.assert_allclose(outs[0].x.cpu().numpy(), blk["x"], rtol=1e-9, atol=1e-12 * np.abs(blk["x"]).max())
+    np.testing.assert_allclose(outs[0].y.cpu().numpy(), blk["y"], rtol=1e-9, atol=1e-12 * np.abs(blk["y"]).max())
+    ref = oracle.pdlp(rows, cols, c, a, b, frequency=200, tolerance=1e-8)
+    got = hb.NativeRestrictedOTPDLP(device=cuda, summation="tree").solve_restricted(
+        rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=1e-8)
+    assert ref["termination_reason"] == got.termination_reason == "OPTIMAL"
+    assert got.obj_val == pytest.approx(ref["obj_val"], rel=1e-7)
+
+
 @pytest.mark.parametrize("path", sorted(p.name for p in GOLDEN.glob("pdlp_*.npz")))
 def test_pdlp_golden(hb, cuda, path):
     with np.load(GOLDEN / path) as z:
@@ -143,3 +177,13 @@ def test_pdlp_input_errors(hb, cuda):
     r = s.solve_restricted(rows=rows, cols=cols, costs=costs, source_mass=[0.4, 0.6], target_mass=[0.5, 0.5],
                            tolerance=1e-7)
     assert r.success and r.obj_val == pytest.approx(0.1, abs=2e-6)
+    with pytest.raises(ValueError, match="summation"):
+        hb.NativeRestrictedOTPDLP(device=cuda, summation="pairwise")
+    bad = hb.NativeRestrictedOTPDLP(device=cuda)
+    bad.summation = "invalid"
+    hb.pdlp.SUMMATION["invalid"] = 3  # an out-of-range order reaches the C ABI check
+    try:
+        with pytest.raises(ValueError, match="HB_PDLP_SUMS"):
+            bad.solve_restricted(rows=rows, cols=cols, costs=costs, source_mass=[0.4, 0.6], target_mass=[0.5, 0.5])
+    finally:
+        del hb.pdlp.SUMMATION["invalid"]

@@ -107,3 +107,8 @@ def test_l2sq_pass_flags_are_validated_before_launch(hb):
     assert call(16, 3 | one) == hb._lib.HB_BAD_ARGUMENT
     assert "one-pass scan needs" in lib.hb_last_error().decode()
     assert call(0, 1 | one) == hb._lib.HB_BAD_ARGUMENT
+
+
+def test_coarsest_rejects_cpu_device(hb):
+    with pytest.raises(ValueError, match="CUDA"):
+        hb.solve_leaf_from_cost(cost=np.ones((2, 2)), source_mass=[0.5, 0.5], target_mass=[0.5, 0.5], device="cpu")
