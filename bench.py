@@ -73,6 +73,7 @@ def parse_args():
                         "support: active-support candidate filter; prune: budgeted pruning selection; "
                         "coarsest: dense exact transport of a coarsest level (n = m = 1024, d = 32)")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
+    p.add_argument("--norm-kind", default="l1", choices=["l1", "linf", "l2"], help="cost of --path norm")
     p.add_argument("--n", type=int, default=None, help="points per side (default: the path's config)")
     p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
     p.add_argument("--k", type=int, default=8)
@@ -577,16 +578,20 @@ def run_pairs(args, hb, dev, peaks):
 
 
 def run_norm(args, hb, dev, peaks):
-    """ℓ1 pricing scan, config 3 shape (n = m = 262144, d = 128, k = 8)."""
-    n, d, k = args.n, args.d, args.k
+    """Norm pricing scan (ℓ1 by default), config 3 shape (n = m = 262144, d = 128, k = 8)."""
+    n, d, k, kind = args.n, args.d, args.k, args.norm_kind
     g = torch.Generator(device=dev)
     g.manual_seed(42)
     x = torch.randn(n, d, device=dev, generator=g)
     y = torch.randn(n, d, device=dev, generator=g)
-    f = torch.randn(n, device=dev, dtype=torch.float64, generator=g) * d
-    gg = torch.randn(n, device=dev, dtype=torch.float64, generator=g) * d
+    # duals ~ N(0, 1) x the median pairwise cost (65536 sampled pairs), as config 5 specifies
+    sr = torch.randint(0, n, (65536,), device=dev, generator=g)
+    sc = torch.randint(0, n, (65536,), device=dev, generator=g)
+    med = float(hb.pair_costs({"l1": 0, "linf": 1, "l2": 2}[kind], x, y, sr, sc).median())
+    f = torch.randn(n, device=dev, dtype=torch.float64, generator=g) * med
+    gg = torch.randn(n, device=dev, dtype=torch.float64, generator=g) * med
     hb.set_kernel_timing(True)
-    sec = _timed(lambda: hb.norm_scan(x, y, f, gg, k, "l1"), args, dev)
+    sec = _timed(lambda: hb.norm_scan(x, y, f, gg, k, kind), args, dev)
     kms = hb.last_kernel_times()
     hb.set_kernel_timing(False)
     # FP32-pipe roofline: 2 d instructions per pair; peak = 148 SMs x 128 lanes x max clock
@@ -595,20 +600,21 @@ def run_norm(args, hb, dev, peaks):
     achieved = 2 * d * n * n / (kms[0] / 1e3) / 1e12 if kms else float("nan")
     extra = {"dtype": "f32 distance, f64 score", "roofline": {
         "bound": "fp32 pipe", "achieved": achieved, "peak": peak, "unit": "Tinst/s", "frac": achieved / peak,
-        "traffic": None, "kernel": "hb::norm::scan_kernel<0,8,1,0,1> (one pass: row and column lists)",
+        "traffic": None, "kernel": f"hb::norm::scan_kernel ({kind}; one pass: row and column lists)",
         "peak_source": "nominal: SMs x 128 fp32 lanes x max SM clock"}}
     if not args.no_cpu:
         import oracle
         rows = 64
         xs, ys = x[:rows].cpu().numpy(), y.cpu().numpy()
         t0 = time.perf_counter()
-        oracle.scan("l1", xs, ys, f[:rows].cpu().numpy(), gg.cpu().numpy(), rk=k, ck=0, exact=False,
+        oracle.scan(kind, xs, ys, f[:rows].cpu().numpy(), gg.cpu().numpy(), rk=k, ck=0, exact=False,
                     threads=os.cpu_count() or 1)
         dt = time.perf_counter() - t0
         extra["cpu_baseline"] = {"value": rows * n / dt / 1e9, "unit": "Gpairs/s", "cores": os.cpu_count() or 1,
                                  "kind": "port", "sample": f"{rows} source rows x {n} targets, oracle fp32 model"}
-    _line(args, "l1 pricing-scan Gpairs/s (m·n)", n * n / sec / 1e9, "Gpairs/s", sec,
-          {"workload": f"l1 pricing scan, n=m={n}, d={d}, k={k}", "n": n, "d": d, "topk": k}, extra)
+    _line(args, f"{kind} pricing-scan Gpairs/s (m·n)", n * n / sec / 1e9, "Gpairs/s", sec,
+          {"workload": f"{kind} pricing scan, n=m={n}, d={d}, k={k}", "n": n, "d": d, "topk": k,
+           "median_pair_cost": med}, extra)
 
 
 def run_initial(args, hb, dev, peaks):
