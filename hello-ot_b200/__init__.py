@@ -16,5 +16,6 @@ from .pairs import cost_pairs_lowrank, pair_costs, pair_costs_metric  # noqa: F4
 from .pdlp import NativeRestrictedOTPDLP, SolverResult  # noqa: F401
 from .support import filter_new_candidate_pairs, select_prune_positions, support_filter  # noqa: F401
 from .coarsest import leaf_cost_matrix, solve_leaf_from_cost, solve_leaf_resident  # noqa: F401
+from . import generic_scan, perturb  # noqa: F401
 
 __version__ = "0.1.0"
