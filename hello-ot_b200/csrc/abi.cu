@@ -150,11 +150,13 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (!valid_k(k)) return fail(HB_BAD_ARGUMENT, "k must be in 0..32");
     if (dot_scale != 1.0 && dot_scale != 2.0) return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
     {
-        const int base = precision & ~(HB_L2SQ_TWO_PASS | HB_L2SQ_ONE_PASS);
+        const int base = precision & ~(HB_L2SQ_TWO_PASS | HB_L2SQ_ONE_PASS | HB_L2SQ_CTA_PAIRS | HB_L2SQ_SINGLE_CTA);
         if (base != 1 && base != 3)
             return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32), optionally | a pass flag");
         if ((precision & HB_L2SQ_TWO_PASS) && (precision & HB_L2SQ_ONE_PASS))
             return fail(HB_BAD_ARGUMENT, "HB_L2SQ_ONE_PASS and HB_L2SQ_TWO_PASS are exclusive");
+        if ((precision & HB_L2SQ_CTA_PAIRS) && (precision & HB_L2SQ_SINGLE_CTA))
+            return fail(HB_BAD_ARGUMENT, "HB_L2SQ_CTA_PAIRS and HB_L2SQ_SINGLE_CTA are exclusive");
         if ((precision & HB_L2SQ_ONE_PASS) && (k < 1 || k > 8))
             return fail(HB_BAD_ARGUMENT, "a one-pass scan needs 1 <= k <= 8");
     }

@@ -49,6 +49,13 @@ constexpr int BM = 128, BN = 256, BK = 16;
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
 constexpr int OFF_ALO = A_BYTES, OFF_B = 2 * A_BYTES, OFF_BLO = 2 * A_BYTES + B_BYTES;
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+// CTA pairs (one pass, cta_group::2): each CTA of a pair stages its own 128 query
+// rows and half (128 columns) of the database tile; one M = 256 x N = 256 MMA
+// issued by the even CTA covers both, and each CTA's TMEM receives its 128 rows.
+constexpr int BNH = BN / 2;
+constexpr int BH_BYTES = BNH * BK * 4;
+constexpr int P_OFF_ALO = A_BYTES, P_OFF_B = 2 * A_BYTES, P_OFF_BLO = 2 * A_BYTES + BH_BYTES;
+constexpr int PAIR_STAGE_BYTES = 2 * (A_BYTES + BH_BYTES);
 constexpr int EPI_FIRST = 64;  // warps 0-1: TMA producer, MMA issuer; then EW epilogue warps
 constexpr int MAX_EW = 8;
 // Epilogue warps per CTA: 8 (two per TMEM lane quarter, each on half the
@@ -60,6 +67,7 @@ struct Epi {
 };
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+constexpr uint32_t IDESC_PAIR = idesc_tf32(2 * BM, BN);
 
 struct Params {
     CUtensorMap qmap[2];  // query operand: [0] features (read as tf32 = hi part), [1] low parts
@@ -87,10 +95,10 @@ struct Params {
 
 // Column vectors of a tile (bias, cost, threshold) are bulk-copied by the
 // producer into a ring of CS slots, ahead of the tile's epilogue.
-template <int NST, int NCS, bool ONE>
+template <int NST, int NCS, bool ONE, int STB>
 struct __align__(1024) SmemT {
     static constexpr int STAGES = NST, CS = NCS;
-    uint8_t stage[NST][STAGE_BYTES];
+    uint8_t stage[NST][STB];
     double cbias[NCS][BN];                     // the tile's column biases
     double ccost[NCS][BN];                     // the tile's column costs (cost terms)
     int ckey[ONE ? NCS : 1][ONE ? BN : 4];     // the tile's column thresholds (one pass)
@@ -105,21 +113,24 @@ struct __align__(1024) SmemT {
     uint32_t tmem_base;
     int abort;
 };
-template <bool ONE>
-using Smem = SmemT<ONE ? 3 : 4, 4, ONE>;
-template <bool ONE>
-constexpr size_t smem_bytes() { return sizeof(Smem<ONE>) + 1024; }
-static_assert(smem_bytes<false>() <= 227 * 1024 && smem_bytes<true>() <= 227 * 1024,
-              "dynamic shared memory above the 227 KB a CTA may use");
+template <bool ONE, bool PAIR = false>
+using Smem = SmemT<PAIR ? 4 : (ONE ? 3 : 4), 4, ONE, PAIR ? PAIR_STAGE_BYTES : STAGE_BYTES>;
+template <bool ONE, bool PAIR = false>
+constexpr size_t smem_bytes() { return sizeof(Smem<ONE, PAIR>) + 1024; }
+static_assert(smem_bytes<false>() <= 227 * 1024 && smem_bytes<true>() <= 227 * 1024 &&
+              smem_bytes<true, true>() <= 227 * 1024, "dynamic shared memory above the 227 KB a CTA may use");
 
 // Tile schedule of a CTA: units u = rb * groups + g in [u0, uend) by ustep.
 struct Sched {
     int u0, ustep, uend;
 };
-template <bool ONE>
+// With CTA pairs a unit's row block index counts pairs of row blocks: the CTA of
+// rank r of the pair takes row block 2 * (u / groups) + r.
+template <bool ONE, bool PAIR = false>
 __device__ __forceinline__ Sched schedule(const Params& p) {
     if (!ONE) return {(int)blockIdx.x, (int)gridDim.x, p.units};
-    const int rg = blockIdx.x / p.groups, g = blockIdx.x % p.groups;
+    const int cl = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int rg = cl / p.groups, g = cl % p.groups;
     const int rb0 = rg * p.rbg, rb1 = min(p.rb, rb0 + p.rbg);
     return {rb0 * p.groups + g, p.groups, rb1 > rb0 ? rb1 * p.groups : 0};
 }
@@ -132,31 +143,40 @@ __device__ __forceinline__ Sched schedule(const Params& p) {
 // depends on another one making progress.
 constexpr int PACE = 2, PACE_SPINS = 64;
 
+template <bool PAIR = false>
 __device__ __forceinline__ void pace(const Params& p, int t) {
     volatile int* prog = p.progress;
     prog[blockIdx.x] = t;
-    const int g = blockIdx.x % p.groups, gr = gridDim.x / p.groups;
+    constexpr int W = PAIR ? 2 : 1;  // CTAs per rectangle
+    const int cl = blockIdx.x / W;
+    const int g = cl % p.groups, gr = (gridDim.x / W) / p.groups;
     for (int spin = 0; spin < PACE_SPINS; ++spin) {
         int slow = INT32_MAX;
-        for (int r = 0; r < gr; ++r) slow = min(slow, prog[r * p.groups + g]);
+        for (int r = 0; r < gr; ++r)
+            for (int w = 0; w < W; ++w) slow = min(slow, prog[(r * p.groups + g) * W + w]);
         if (t - slow <= PACE) return;
         __nanosleep(500);
     }
 }
 
-template <bool ONE>
-__device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
-    constexpr int STAGES = Smem<ONE>::STAGES, CSLOTS = Smem<ONE>::CS;
+// CTA pairs: both CTAs load their own A rows and B half into their own shared
+// memory; the completions of both count on the even CTA's full barrier, which
+// the even CTA's producer arms with the bytes of both.
+template <bool ONE, bool PAIR = false>
+__device__ __forceinline__ void producer(const Params& p, Smem<ONE, PAIR>& s) {
+    constexpr int STAGES = Smem<ONE, PAIR>::STAGES, CSLOTS = Smem<ONE, PAIR>::CS;
     uint32_t stage = 0, phase = 0;
-    const uint32_t bytes = p.terms == 3 ? STAGE_BYTES : A_BYTES + B_BYTES;
+    const int rank = PAIR ? (int)cluster_rank() : 0;
+    const uint32_t bytes = PAIR ? (p.terms == 3 ? PAIR_STAGE_BYTES : A_BYTES + BH_BYTES)
+                                : (p.terms == 3 ? STAGE_BYTES : A_BYTES + B_BYTES);
     const uint32_t cbytes = BN * 8 + (p.d_cost ? BN * 8 : 0) + (ONE ? BN * 4 : 0);
     uint32_t t = 0;
-    const Sched sc = schedule<ONE>(p);
+    const Sched sc = schedule<ONE, PAIR>(p);
     for (int u = sc.u0; u < sc.uend; u += sc.ustep) {
-        const int rb = u / p.groups, g = u % p.groups;
+        const int rb = PAIR ? 2 * (u / p.groups) + rank : u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
-            if (ONE) pace(p, (int)t);
+            if (ONE) pace<PAIR>(p, (int)t);
             // the tile's column vectors (the slot was released CSLOTS tiles ago)
             const uint32_t cs = t % CSLOTS;
             if (!mbar_wait(&s.cempty[cs], ((t / CSLOTS) & 1) ^ 1, &s.abort, p.status)) return;
@@ -167,6 +187,18 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
             for (int ks = 0; ks < p.kslabs; ++ks) {
                 if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.abort, p.status)) return;
                 uint8_t* a = s.stage[stage];
+                if constexpr (PAIR) {
+                    const uint32_t fb = peer_smem(&s.full[stage], 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * bytes);
+                    tma_load_2d_pair(a, &p.qmap[0], fb, ks * BK, rb * BM);
+                    tma_load_2d_pair(a + P_OFF_B, &p.dmap[0], fb, ks * BK, ct * BN + rank * BNH);
+                    if (p.terms == 3) {
+                        tma_load_2d_pair(a + P_OFF_ALO, &p.qmap[1], fb, ks * BK, rb * BM);
+                        tma_load_2d_pair(a + P_OFF_BLO, &p.dmap[1], fb, ks * BK, ct * BN + rank * BNH);
+                    }
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    continue;
+                }
                 mbar_arrive_expect_tx(&s.full[stage], bytes);
                 tma_load_2d(a, &p.qmap[0], &s.full[stage], ks * BK, rb * BM);
                 tma_load_2d(a + OFF_B, &p.dmap[0], &s.full[stage], ks * BK, ct * BN);
@@ -184,11 +216,23 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE>& s) {
 // Products per K step of 8: pass 1 (query = x): x*y, x*lo(y), lo(x)*y; pass 2
 // (query = y) issues the same three products with the operands exchanged and
 // in the same order, so both passes accumulate bit-identical dots.
-template <bool SWAP, bool ONE>
-__device__ __forceinline__ void mma_issuer(const Params& p, Smem<ONE>& s, uint32_t tmem) {
-    constexpr int STAGES = Smem<ONE>::STAGES;
+// CTA pairs: issued by the even CTA only (M = 256 over both CTAs' A tiles); the
+// commits arrive on the barriers of both CTAs.
+template <bool SWAP, bool ONE, bool PAIR = false>
+__device__ __forceinline__ void mma_issuer(const Params& p, Smem<ONE, PAIR>& s, uint32_t tmem) {
+    constexpr int STAGES = Smem<ONE, PAIR>::STAGES;
+    constexpr int OA_LO = PAIR ? P_OFF_ALO : OFF_ALO, OB = PAIR ? P_OFF_B : OFF_B, OB_LO = PAIR ? P_OFF_BLO : OFF_BLO;
+    constexpr uint32_t ID = PAIR ? IDESC_PAIR : IDESC;
+    auto mma = [](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+        if constexpr (PAIR) mma_tf32_pair(d, a, b, ID, acc);
+        else mma_tf32(d, a, b, ID, acc);
+    };
+    auto commit = [](uint64_t* bar) {
+        if constexpr (PAIR) mma_commit_pair(bar);
+        else mma_commit(bar);
+    };
     uint32_t stage = 0, phase = 0, t = 0;
-    const Sched sc = schedule<ONE>(p);
+    const Sched sc = schedule<ONE, PAIR>(p);
     for (int u = sc.u0; u < sc.uend; u += sc.ustep) {
         const int g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
@@ -205,19 +249,19 @@ __device__ __forceinline__ void mma_issuer(const Params& p, Smem<ONE>& s, uint32
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
                     const uint32_t o = kk * 32;
-                    const uint64_t ah = smem_desc_sw64(a0 + o), bh = smem_desc_sw64(a0 + OFF_B + o);
-                    mma_tf32(d, ah, bh, IDESC, accumulate);
+                    const uint64_t ah = smem_desc_sw64(a0 + o), bh = smem_desc_sw64(a0 + OB + o);
+                    mma(d, ah, bh, accumulate);
                     accumulate = 1;
                     if (p.terms == 3) {
-                        const uint64_t al = smem_desc_sw64(a0 + OFF_ALO + o), bl = smem_desc_sw64(a0 + OFF_BLO + o);
-                        if (!SWAP) { mma_tf32(d, ah, bl, IDESC, 1); mma_tf32(d, al, bh, IDESC, 1); }
-                        else { mma_tf32(d, al, bh, IDESC, 1); mma_tf32(d, ah, bl, IDESC, 1); }
+                        const uint64_t al = smem_desc_sw64(a0 + OA_LO + o), bl = smem_desc_sw64(a0 + OB_LO + o);
+                        if (!SWAP) { mma(d, ah, bl, 1); mma(d, al, bh, 1); }
+                        else { mma(d, al, bh, 1); mma(d, ah, bl, 1); }
                     }
                 }
-                mma_commit(&s.empty[stage]);
+                commit(&s.empty[stage]);
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }
             }
-            mma_commit(&s.tfull[acc]);
+            commit(&s.tfull[acc]);
         }
     }
 }
@@ -341,8 +385,8 @@ __device__ __forceinline__ void store_list(const Params& p, int64_t base, const 
     }
 }
 
-template <bool ONE>
-__device__ __forceinline__ void column_stage(Smem<ONE>& s, const float (&v)[32], int ew, int lane, double rbias) {
+template <class S>
+__device__ __forceinline__ void column_stage(S& s, const float (&v)[32], int ew, int lane, double rbias) {
     float* T = s.trans + ew * 32 * 33;
 #pragma unroll
     for (int j = 0; j < 32; ++j) T[lane * 33 + j] = v[j];
@@ -350,8 +394,8 @@ __device__ __forceinline__ void column_stage(Smem<ONE>& s, const float (&v)[32],
     __syncwarp();
 }
 
-template <int K, bool ONE>
-__device__ __forceinline__ void column_update(const Params& p, Smem<ONE>& s, uint32_t cmask, int ew, int lane,
+template <int K, class S>
+__device__ __forceinline__ void column_update(const Params& p, S& s, uint32_t cmask, int ew, int lane,
                                               int row0, int col0, double cbias, int64_t list_base) {
     constexpr int KK = K > 0 ? K : 1;
     const float* T = s.trans + ew * 32 * 33;
@@ -385,26 +429,31 @@ __device__ __forceinline__ void column_update(const Params& p, Smem<ONE>& s, uin
 // columns: phase 1 (above), then phase 2 inserts the masked columns into the
 // row's k-list with exact fp64 scores (rare once the list has filled), so
 // reported scores follow the reference arithmetic (dot + qb) + dbb in fp64.
-template <int K, int SM, bool SWAP, bool ONE>
-__device__ __forceinline__ void epilogue(const Params& p, Smem<ONE>& s, uint32_t tmem, double (&acc)[5]) {
+template <int K, int SM, bool SWAP, bool ONE, bool PAIR = false>
+__device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, uint32_t tmem, double (&acc)[5]) {
     constexpr int KK = K > 0 ? K : 1;
     constexpr int EW = Epi<K>::EW;
     constexpr int SLICES = EW / 4;
     constexpr int SLICE = BN / SLICES;
-    constexpr int CSLOTS = Smem<ONE>::CS;
+    constexpr int CSLOTS = Smem<ONE, PAIR>::CS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rank = PAIR ? (int)cluster_rank() : 0;
     const int ew = warp - EPI_FIRST / 32;
     const int quarter = warp & 3;           // TMEM lanes this warp may read
     const int slice = ew / 4;
     const int r = quarter * 32 + lane;      // tile row owned by this thread
     float4* wcol = s.col + ew * SLICE;
-    // one-pass: this warp's column lists (row group of the CTA, TMEM lane quarter)
-    const int64_t list_base = ONE ? (int64_t)((blockIdx.x / p.groups) * 4 + quarter) * p.n : 0;
+    // one-pass: this warp's column lists (row group of the CTA [and its rank in the
+    // pair], TMEM lane quarter)
+    const int rgl = PAIR ? (int)(blockIdx.x >> 1) / p.groups * 2 + rank : (int)blockIdx.x / p.groups;
+    const int64_t list_base = ONE ? (int64_t)(rgl * 4 + quarter) * p.n : 0;
+    // CTA pairs: the accumulator is released on the even CTA's barrier
+    const uint32_t tempty_peer = PAIR ? peer_smem(&s.tempty[0], 0) : 0u;
     TopK<KK> top;
     uint32_t t = 0;
-    const Sched sched = schedule<ONE>(p);
+    const Sched sched = schedule<ONE, PAIR>(p);
     for (int u = sched.u0; u < sched.uend; u += sched.ustep) {
-        const int rb = u / p.groups, g = u % p.groups;
+        const int rb = PAIR ? 2 * (u / p.groups) + rank : u / p.groups, g = u % p.groups;
         const int ct1 = min(p.ct, (g + 1) * p.tpg);
         const int row = rb * BM + r;
         const bool rvalid = row < p.q;
@@ -448,7 +497,7 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE>& s, uint32_t
                     mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, p.scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
                                                                  live, thr, cmask, acc);
                 const bool colwork = ONE && K > 0 && __any_sync(0xffffffffu, cmask != 0u);
-                if (colwork) column_stage<ONE>(s, v, ew, lane, rbias);
+                if (colwork) column_stage(s, v, ew, lane, rbias);
                 // phase 2: exact fp64 scores of the masked columns into the row list
                 while (K > 0 && mask) {
                     const int j = __ffs(mask) - 1;
@@ -462,11 +511,12 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE>& s, uint32_t
                     top.offer(sc, c0 + cb + j);
                 }
                 if (colwork)
-                    column_update<K, ONE>(p, s, cmask, ew, lane, rb * BM + quarter * 32, c0 + cb, wbias[cb + lane],
-                                          list_base);
+                    column_update<K>(p, s, cmask, ew, lane, rb * BM + quarter * 32, c0 + cb, wbias[cb + lane],
+                                     list_base);
             }
             tc_fence_before();
-            mbar_arrive(&s.tempty[buf]);
+            if (PAIR && rank != 0) mbar_arrive_remote(tempty_peer + buf * (uint32_t)sizeof(uint64_t));
+            else mbar_arrive(&s.tempty[buf]);
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.cempty[cs]);  // the warp is done with the tile's column slot
         }
@@ -480,17 +530,24 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE>& s, uint32_t
     }
 }
 
-template <int K, int SM, bool SWAP, bool ONE>
+// CTA pairs (PAIR, launched as clusters of 2): TMEM is allocated in both CTAs by
+// their warp 1 with cta_group::2; the two CTAs synchronise (cluster barrier) after
+// the barrier initialisation and before the TMEM release, and every role of both
+// returns to the end of the kernel, also after an aborted wait, so both always
+// reach both cluster barriers.
+template <int K, int SM, bool SWAP, bool ONE, bool PAIR = false>
 __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_constant__ Params p) {
     constexpr int EW = Epi<K>::EW;
-    constexpr int STAGES = Smem<ONE>::STAGES;
+    using S = Smem<ONE, PAIR>;
+    constexpr int STAGES = S::STAGES;
     extern __shared__ uint8_t smem_raw[];
-    Smem<ONE>& s = *reinterpret_cast<Smem<ONE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], 32 * EW); }
-        for (int i = 0; i < Smem<ONE>::CS; ++i) { mbar_init(&s.cfull[i], 1); mbar_init(&s.cempty[i], EW); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], 32 * EW * (PAIR ? 2 : 1)); }
+        for (int i = 0; i < S::CS; ++i) { mbar_init(&s.cfull[i], 1); mbar_init(&s.cempty[i], EW); }
         s.abort = 0;
         fence_barrier_init();
     }
@@ -498,18 +555,22 @@ __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_c
         prefetch_tmap(&p.qmap[0]); prefetch_tmap(&p.qmap[1]);
         prefetch_tmap(&p.dmap[0]); prefetch_tmap(&p.dmap[1]);
     }
-    if (warp == 1) { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
+    if (warp == 1) {
+        if constexpr (PAIR) { tmem_alloc_pair(&s.tmem_base, TMEM_COLS); tmem_relinquish_pair(); }
+        else { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
+    }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
     if (warp == 0) {
-        if (lane == 0) producer<ONE>(p, s);
+        if (lane == 0) producer<ONE, PAIR>(p, s);
     } else if (warp == 1) {
-        if (lane == 0) mma_issuer<SWAP, ONE>(p, s, tmem);
+        if (lane == 0 && rank == 0) mma_issuer<SWAP, ONE, PAIR>(p, s, tmem);
     } else {
         double acc[5] = {0, 0, 0, 0, 0};
-        epilogue<K, SM, SWAP, ONE>(p, s, tmem, acc);
+        epilogue<K, SM, SWAP, ONE, PAIR>(p, s, tmem, acc);
         if (SM) {  // warp totals in a fixed shuffle order
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) {
@@ -526,9 +587,11 @@ __global__ void __launch_bounds__(Epi<K>::THREADS, 1) scan_kernel(const __grid_c
     }
     tc_fence_before();
     __syncthreads();  // every role returns here, also after an aborted wait
+    if constexpr (PAIR) cluster_sync();  // the pair is done with each other's barriers and TMEM
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
+        else tmem_dealloc(tmem, TMEM_COLS);
     }
     if (SM && threadIdx.x == EPI_FIRST) {
         double a[5] = {0, 0, 0, 0, 0};
@@ -618,10 +681,10 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int dp, int box_r
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int K, int SM, bool SWAP, bool ONE = false>
+template <int K, int SM, bool SWAP, bool ONE = false, bool PAIR = false>
 cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
-    auto fn = l2sq::scan_kernel<K, SM, SWAP, ONE>;
-    constexpr size_t smem = l2sq::smem_bytes<ONE>();
+    auto fn = l2sq::scan_kernel<K, SM, SWAP, ONE, PAIR>;
+    constexpr size_t smem = l2sq::smem_bytes<ONE, PAIR>();
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -629,10 +692,50 @@ cudaError_t launch_pass(const l2sq::Params& p, int grid, cudaStream_t st) {
         configured = true;
     }
     timing_mark(st);
+    if constexpr (PAIR) {  // clusters of two CTAs (grid is even)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(l2sq::Epi<K>::THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
+        timing_mark(st);
+        count_launches(1);
+        return e != cudaSuccess ? e : cudaGetLastError();
+    }
     fn<<<grid, l2sq::Epi<K>::THREADS, smem, st>>>(p);
     timing_mark(st);
     count_launches(1);
     return cudaGetLastError();
+}
+
+// Clusters of two CTAs of the paired one-pass kernel that fit on the device at once.
+int pair_clusters() {
+    static int cached = -1;
+    if (cached >= 0) return cached;
+    auto fn = l2sq::scan_kernel<8, l2sq::kScoreStats | l2sq::kCostStats, false, true, true>;
+    constexpr size_t smem = l2sq::smem_bytes<true, true>();
+    int n = 0;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(l2sq::Epi<8>::THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();  // clear a failed query
+    cached = n;
+    return n;
 }
 
 template <int SM, bool SWAP>
@@ -648,13 +751,13 @@ cudaError_t launch_k(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
     }
 }
 
-template <int SM>
+template <int SM, bool PAIR = false>
 cudaError_t launch_one(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
     switch (K) {
-        case 1: return launch_pass<1, SM, false, true>(p, grid, st);
-        case 2: return launch_pass<2, SM, false, true>(p, grid, st);
-        case 4: return launch_pass<4, SM, false, true>(p, grid, st);
-        case 8: return launch_pass<8, SM, false, true>(p, grid, st);
+        case 1: return launch_pass<1, SM, false, true, PAIR>(p, grid, st);
+        case 2: return launch_pass<2, SM, false, true, PAIR>(p, grid, st);
+        case 4: return launch_pass<4, SM, false, true, PAIR>(p, grid, st);
+        case 8: return launch_pass<8, SM, false, true, PAIR>(p, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -705,27 +808,47 @@ constexpr int ONE_PASS_ROW_GROUPS = 8;
 // Automatic choice: the one-pass epilogue costs about the same per pair at any
 // d (list upkeep), the tensor-core work grows with d, and the column lists see
 // more rows (fewer insertions) as q grows.
+// CTA pairs for the one-pass kernel: forced by HB_L2SQ_CTA_PAIRS or HB_L2SQ_SINGLE_CTA,
+// else chosen for wide features (needs clusters of two to fit on the device).  Measured
+// on one B200, same data, alternating runs: d = 2048 (131072^2) 50.8 Gpairs/s paired
+// against 46.9 single; d = 256 (1048576^2) 304.9 against 309.5, where the 1 kW power cap
+// sets the clock and the halved column-tile traffic buys nothing.
+constexpr int64_t PAIRS_MIN_D = 1024;
+inline bool use_pairs(int precision, int64_t d) {
+    if (precision & HB_L2SQ_SINGLE_CTA) return false;
+    if (!(precision & HB_L2SQ_CTA_PAIRS) && d < PAIRS_MIN_D) return false;
+    return pair_clusters() > 0;
+}
 inline bool use_one_pass(int K, int precision, int64_t q, int64_t d) {
     if (K < 1 || K > 8 || (precision & (HB_L2SQ_TWO_PASS | L2SQ_ROWS_ONLY))) return false;
     if (precision & HB_L2SQ_ONE_PASS) return true;
     return d >= 128 || (d >= 64 && q >= (int64_t(1) << 19));
 }
 
+// CTA pairs: a rectangle is a cluster of two CTAs whose units are pairs of row
+// blocks (rb counts them); half as many row groups keep the same number of column
+// lists per column (4 x 2 ranks x 4 quarters), and each column tile is read by
+// half as many rectangles.
 struct OnePlan {
     int rb, ct, gr, rbg, gc, tpg, grid;
+    bool pair;
+    int lists_per_col() const { return gr * (pair ? 2 : 1) * 4; }
 };
-inline OnePlan one_plan(int64_t q, int64_t n, int sms, int min_groups) {
+inline OnePlan one_plan(int64_t q, int64_t n, int sms, int min_groups, bool pair = false, int clusters = 0) {
     OnePlan o{};
-    o.rb = (int)((q + l2sq::BM - 1) / l2sq::BM);
+    o.pair = pair;
+    const int rows_per_unit = l2sq::BM * (pair ? 2 : 1);
+    o.rb = (int)((q + rows_per_unit - 1) / rows_per_unit);
     o.ct = (int)((n + l2sq::BN - 1) / l2sq::BN);
-    o.gr = std::min(ONE_PASS_ROW_GROUPS, o.rb);
+    o.gr = std::min(ONE_PASS_ROW_GROUPS / (pair ? 2 : 1), o.rb);
     o.rbg = (o.rb + o.gr - 1) / o.gr;
     o.gr = (o.rb + o.rbg - 1) / o.rbg;
-    int gc = std::max(1, std::max(sms / o.gr, min_groups));
+    const int slots = pair ? clusters : sms;  // rectangles that run at once
+    int gc = std::max(1, std::max(slots / o.gr, min_groups));
     gc = std::min(gc, o.ct);
     o.tpg = (o.ct + gc - 1) / gc;
     o.gc = (o.ct + o.tpg - 1) / o.tpg;
-    o.grid = o.gr * o.gc;
+    o.grid = o.gr * o.gc * (pair ? 2 : 1);
     return o;
 }
 
@@ -774,8 +897,9 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     need(!L.one_pass && !rows_only && K > 0, L.xbp, qpad);
     need(!L.one_pass && !rows_only && K > 0, L.xcp, qpad);
     if (L.one_pass) {
-        L.one = one_plan(q, n, sms, min_groups);
-        const size_t lists = (size_t)L.one.gr * 4 * n;
+        const bool pair = use_pairs(precision, d);
+        L.one = one_plan(q, n, sms, min_groups, pair, pair ? pair_clusters() : 0);
+        const size_t lists = (size_t)L.one.lists_per_col() * n;
         need(true, L.pv1, (size_t)L.one.gc * slices * q * K);
         need(true, L.pi1, (size_t)L.one.gc * slices * q * K);
         need(true, L.cval, lists * K);
@@ -838,8 +962,10 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     }
     l2sq::Params p;
     std::memset(&p, 0, sizeof(p));
-    bool maps = make_map(&p.qmap[0], xs, q, dp, l2sq::BM) && make_map(&p.dmap[0], ys, n, dp, l2sq::BN);
-    if (prec == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, l2sq::BN);
+    const bool pair = L.one_pass && L.one.pair;
+    const int brows = pair ? l2sq::BNH : l2sq::BN;  // database box: half a column tile per CTA of a pair
+    bool maps = make_map(&p.qmap[0], xs, q, dp, l2sq::BM) && make_map(&p.dmap[0], ys, n, dp, brows);
+    if (prec == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, brows);
     else { p.qmap[1] = p.qmap[0]; p.dmap[1] = p.dmap[0]; }
     if (!maps) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
     p.terms = prec == 3 ? 3 : 1;
@@ -853,7 +979,7 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (L.one_pass) {
         // one pass: row lists in registers, column lists per (row group, lane quarter) in HBM
         const OnePlan& o = L.one;
-        const int64_t lists = (int64_t)o.gr * 4 * n;
+        const int64_t lists = (int64_t)o.lists_per_col() * n;
         l2sq::init_columns<<<prep_blocks, 256, 0, st>>>(L.cval, L.cidx, L.ckey, lists, npad, K);
         count_launches(1);
         p.groups = o.gc; p.tpg = o.tpg; p.ct = o.ct; p.units = o.rb * o.gc;
@@ -863,11 +989,15 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         e = cudaMemsetAsync(L.progress, 0, sizeof(int) * o.grid, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
         if (!want_stats) p.d_cost = nullptr;  // the cost vector is staged only for the cost terms
-        e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats>(K, p, o.grid, st)
-                       : launch_one<0>(K, p, o.grid, st);
+        if (o.pair)
+            e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats, true>(K, p, o.grid, st)
+                           : launch_one<0, true>(K, p, o.grid, st);
+        else
+            e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats>(K, p, o.grid, st)
+                           : launch_one<0>(K, p, o.grid, st);
         if (e != cudaSuccess) { err = std::string("l2sq scan: ") + cudaGetErrorString(e); return 6; }
         e = merge_any(K, L.pv1, L.pi1, o.gc * l2sq_slices(K), q, k, rv, ri, st);
-        if (e == cudaSuccess) e = merge_any(K, L.cval, L.cidx, o.gr * 4, n, k, cv, ci, st);
+        if (e == cudaSuccess) e = merge_any(K, L.cval, L.cidx, o.lists_per_col(), n, k, cv, ci, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
         if (want_stats) {
             finalize_stats<<<1, 32, 0, st>>>(L.cta, o.grid, stats5);

@@ -71,14 +71,16 @@ def _c(t):
 
 
 L2SQ_PASS_FLAGS = {None: 0, 2: 0x10, 1: 0x20}
+L2SQ_CTA_FLAGS = {None: 0, 2: 0x100, 1: 0x200}  # HB_L2SQ_CTA_PAIRS, HB_L2SQ_SINGLE_CTA
 
 
 def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute_stats=True, precision="fp32",
-              min_groups=0, passes=None):
+              min_groups=0, passes=None, ctas=None):
     """Bidirectional ℓ2² scan on the tensor cores.
 
     passes: 1 (k <= 8 only), 2, or None to let the library choose; both give the
-    same lists bit for bit.  Returns (row_vals q x k fp64, row_idx q x k int32,
+    same lists bit for bit.  ctas (one-pass kernel): 2 runs it as CTA pairs sharing
+    each column tile, 1 as single CTAs, None the library's choice.  Returns (row_vals q x k fp64, row_idx q x k int32,
     col_vals n x k, col_idx n x k, stats [sum s+^2, sum c^2, max s+, max |c|, count]
     fp64 on the device)."""
     x, y = _c(x), _c(y)
@@ -86,7 +88,7 @@ def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute
     q, d = x.shape
     n = y.shape[0]
     prec = PRECISION[precision] if isinstance(precision, str) else int(precision)
-    prec |= L2SQ_PASS_FLAGS[passes]
+    prec |= L2SQ_PASS_FLAGS[passes] | L2SQ_CTA_FLAGS[ctas]
     L = lib()
     dev = x.device
     kk = int(k)

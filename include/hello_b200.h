@@ -76,10 +76,15 @@ int hb_last_kernel_times(double* ms, int capacity);
  * order only).  Without a flag the scan picks one pass when k <= 8 and the
  * tensor-core work per pair dominates the list upkeep (d >= 128, or d >= 64
  * with q >= 2^19), else two.
+ * The one-pass kernel runs either one CTA per rectangle of the pair space or
+ * CTA pairs (clusters of two sharing each column tile through a cta_group::2
+ * MMA); OR HB_L2SQ_CTA_PAIRS or HB_L2SQ_SINGLE_CTA to force either (same lists).
  * min_groups: column groups (0 = automatic).
  * ------------------------------------------------------------------------- */
 #define HB_L2SQ_TWO_PASS 0x10
 #define HB_L2SQ_ONE_PASS 0x20
+#define HB_L2SQ_CTA_PAIRS 0x100
+#define HB_L2SQ_SINGLE_CTA 0x200
 size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
 int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_cost,
                  const double* y_cost, const double* x_bias, const double* y_bias, int k, double dot_scale,

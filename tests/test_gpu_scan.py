@@ -205,6 +205,25 @@ def test_norm_scan_bit_exact(hb, cuda, oracle, kind, q, n, d, k):
 
 
 # (q, n, d, k): several row blocks per row group, ragged tiles, k > n, one feature
+@pytest.mark.parametrize("q,n,d,k,groups,precision", ONE_PASS_CASES)
+def test_l2sq_cta_pairs_equal_single_ctas(hb, cuda, q, n, d, k, groups, precision):
+    """The one-pass kernel run as CTA pairs (one M = 256 cta_group::2 MMA over both
+    CTAs' rows, each CTA staging half of the column tile) reports the same lists as
+    the single-CTA kernel: the same dots in the same fp32 order feed the same
+    epilogue.  The certificate differs only in the order of its partial sums."""
+    x, y, a, b, f, g = _cloud(q, n, d, seed=q + 5 * n + d)
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    args = (T(x, torch.float32), T(y, torch.float32), T(a, torch.float64), T(b, torch.float64),
+            T(f - a, torch.float64), T(g - b, torch.float64), k)
+    pair = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups, passes=1, ctas=2)]
+    single = [t.clone() for t in hb.l2sq_scan(*args, precision=precision, min_groups=groups, passes=1, ctas=1)]
+    for u, v in zip(pair[:4], single[:4]):
+        assert torch.equal(u, v)
+    s1, s2 = pair[4].cpu().numpy(), single[4].cpu().numpy()
+    assert s1[2] == s2[2] and s1[3] == s2[3] and s1[4] == s2[4]
+    assert s1[0] == pytest.approx(s2[0], rel=4 * CERT_REL) and s1[1] == pytest.approx(s2[1], rel=4 * CERT_REL)
+
+
 NORM_ONE_PASS_CASES = [(3000, 777, 20, 8), (130, 2600, 3, 4), (5, 3, 2, 8), (1100, 900, 1, 1), (2049, 2050, 64, 2)]
 
 
