@@ -134,3 +134,61 @@ class ShardedPricingScan:
                 cols = torch.cat((pairs[1], d_local.to(torch.int64)))
         return ShardedScanResult(rows=rows, cols=cols, stats=total, col_vals=cv_m, col_idx=ci_m, row_vals=rv,
                                  row_idx=ri)
+
+
+class ShardedPairCosts:
+    """Pair costs (the SDDMM of new or initial edges) with source rows sharded like the
+    scan: each rank evaluates the edges whose source row lies in its block from its
+    local rows and the replicated target cloud, then an all-gather of (edge position,
+    cost) gives every rank the costs of all edges in the callers' order (exact: each
+    edge is evaluated by exactly one rank).  The reference evaluates them on one GPU
+    (src/hello_ot/costs/pairs.py:221-440 `_cost_pairs_lowrank_batched`).
+
+    ``local_costs(kind, x_block, y, rows_local, cols, a_block, b, dot_scale)`` -> fp64
+    costs defaults to the CUDA pair-cost kernel; tests inject a CPU version under gloo.
+    """
+
+    def __init__(self, group=None, *, local_costs: Optional[Callable] = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if local_costs is None:
+            from .pairs import pair_costs
+
+            def local_costs(kind, x, y, rows, cols, a, b, dot_scale):
+                return pair_costs(kind, x, y, rows, cols, a=a, b=b, dot_scale=dot_scale)
+        self.local_costs = local_costs
+
+    def costs(self, rows, cols, x_block, y, *, row_offset: int, a_block=None, b=None, kind: int = 3,
+              dot_scale: float = 2.0) -> torch.Tensor:
+        """fp64 cost of every (rows[e], cols[e]) (global source indices), on every rank."""
+        world, group = self.world, self.group
+        rows = rows.to(torch.int64).view(-1)
+        cols = cols.to(torch.int64).view(-1)
+        if rows.numel() != cols.numel():
+            raise ValueError("rows and cols must have the same length")
+        lo, hi = int(row_offset), int(row_offset) + int(x_block.shape[0])
+        mine = torch.nonzero((rows >= lo) & (rows < hi), as_tuple=False).view(-1)
+        vals = self.local_costs(kind, x_block, y, rows[mine] - lo, cols[mine], a_block, b, dot_scale)
+        vals = vals.to(torch.float64).view(-1)
+        out = torch.empty(rows.numel(), dtype=torch.float64, device=rows.device)
+        if world == 1:
+            if mine.numel() != rows.numel():
+                raise ValueError("edge source rows outside this rank's block")
+            out[mine] = vals
+            return out
+        count = torch.tensor([mine.numel()], dtype=torch.int64, device=rows.device)
+        counts = _all_gather(count, world, group).view(-1)
+        if int(counts.sum().item()) != rows.numel():
+            raise ValueError("every edge's source row must lie in exactly one rank's block")
+        width = max(int(counts.max().item()), 1)
+        pos = torch.full((width,), -1, dtype=torch.int64, device=rows.device)
+        val = torch.zeros(width, dtype=torch.float64, device=rows.device)
+        pos[:mine.numel()] = mine
+        val[:mine.numel()] = vals
+        all_pos = _all_gather(pos, world, group)
+        all_val = _all_gather(val, world, group)
+        for r in range(world):
+            c = int(counts[r])
+            out[all_pos[r, :c]] = all_val[r, :c]
+        return out

@@ -187,3 +187,16 @@ def test_pdlp_input_errors(hb, cuda):
             bad.solve_restricted(rows=rows, cols=cols, costs=costs, source_mass=[0.4, 0.6], target_mass=[0.5, 0.5])
     finally:
         del hb.pdlp.SUMMATION["invalid"]
+
+
+def test_sharded_pair_costs_single_rank(hb, cuda):
+    """World size 1 (no process group): the sharded pair costs are the kernel's."""
+    from hello_ot_b200.sharded import ShardedPairCosts
+    rng = np.random.default_rng(2)
+    x = torch.as_tensor(rng.normal(size=(300, 40)).astype(np.float32), device=cuda)
+    y = torch.as_tensor(rng.normal(size=(500, 40)).astype(np.float32), device=cuda)
+    a, b = (x.double() ** 2).sum(1), (y.double() ** 2).sum(1)
+    rows = torch.as_tensor(rng.integers(0, 300, 4000), device=cuda)
+    cols = torch.as_tensor(rng.integers(0, 500, 4000), device=cuda)
+    got = ShardedPairCosts().costs(rows, cols, x, y, row_offset=0, a_block=a, b=b)
+    assert torch.equal(got, hb.pair_costs(3, x, y, rows, cols, a=a, b=b, dot_scale=2.0))

@@ -97,6 +97,48 @@ def test_sharded_scan_matches_single_process(oracle, tmp_path, world):
     np.testing.assert_allclose(got["stats"], st, rtol=1e-12)
 
 
+def _pairs_worker(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    sys.path.insert(0, str(REPO))
+    sys.path.insert(0, str(REPO / "tests"))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import oracle
+        import __graft_entry__ as entry
+        entry.load_package()
+        from hello_ot_b200.sharded import ShardedPairCosts, row_partition
+
+        x, y, a, b, _, _ = _problem()
+        rng = np.random.default_rng(11)
+        rows = rng.integers(0, len(x), 200)
+        cols = rng.integers(0, len(y), 200)
+
+        names = {0: "l1", 1: "linf", 2: "l2", 3: "raw"}
+
+        def local_costs(kind, xs, ys, r, c, as_, bs, dot_scale):
+            return torch.from_numpy(oracle.pair_costs(names[kind], xs.numpy(), ys.numpy(), r.numpy(), c.numpy(),
+                                                      as_.numpy(), bs.numpy(), dot_scale=dot_scale))
+
+        lo, hi = row_partition(len(x), world, rank)
+        T = torch.from_numpy
+        got = ShardedPairCosts(local_costs=local_costs).costs(T(rows), T(cols), T(x[lo:hi]), T(y), row_offset=lo,
+                                                             a_block=T(a[lo:hi]), b=T(b))
+        if rank == 0:
+            np.savez(out_path, costs=got.numpy(), rows=rows, cols=cols)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_pair_costs_match_single_process(oracle, tmp_path):
+    out = tmp_path / "pairs.npz"
+    mp.spawn(_pairs_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    got = np.load(out)
+    x, y, a, b, _, _ = _problem()
+    want = oracle.pair_costs("raw", x, y, got["rows"], got["cols"], a, b, dot_scale=2.0)
+    assert np.array_equal(got["costs"], want)
+
+
 def test_row_partition_covers_rows(hb):
     from hello_ot_b200.sharded import row_partition
     for total in (1, 7, 100, 1_048_576):
