@@ -176,6 +176,8 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (e != cudaSuccess) return fail(HB_CUDA, std::string("l2sq scan: ") + cudaGetErrorString(e));
     collect_timing();
     if (status_host & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, "l2sq scan: a device-side wait timed out");
+    if (status_host & hb::kErrBadInput)
+        return fail(HB_BAD_INPUT, "l2sq scan: a feature magnitude of 2^75 or more (or a non-finite one)");
     g_error.clear();
     return HB_OK;
 }
@@ -244,6 +246,8 @@ int hb_l2sq_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (e != cudaSuccess) return fail(HB_CUDA, std::string("l2sq top-k: ") + cudaGetErrorString(e));
     collect_timing();
     if (status_host & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, "l2sq top-k: a device-side wait timed out");
+    if (status_host & hb::kErrBadInput)
+        return fail(HB_BAD_INPUT, "l2sq top-k: a feature magnitude of 2^75 or more (or a non-finite one)");
     g_error.clear();
     return HB_OK;
 }

@@ -13,9 +13,14 @@
 //
 // Score arithmetic follows the reference raw path (matrix_selection.cuh:20-26):
 //   dot = fp32(s * <x,y>);  cost = (a_i + b_j) - dot;  score = (dot + qb_i) + dbb_j
-// in fp64.  <x,y> is computed either with one TF32 product ("tf32") or as the
-// 3-term split hi*hi + hi*lo + lo*hi ("3xtf32"), hi = x with the low 13
-// mantissa bits dropped and lo = x - hi (exact), which gives an fp32-class dot.
+// in fp64.  <x,y> is computed either with one TF32 product ("tf32", kind::tf32 on
+// the fp32 features) or as the 3-term split hi*hi + hi*lo + lo*hi on fp16 halves
+// (kind::f16): each cloud is scaled by one power of two 2^e so that its largest
+// |x| lies in [2^14, 2^15), hi = fp16(x 2^e), lo = fp16(x 2^e - hi) (22 bits of
+// every element kept, products exact, fp32 accumulation), and the epilogue
+// multiplies the accumulated dot by 2^-(e_x + e_y), exactly: an fp32-class dot
+// (each product within 3 2^-22 |x||y|) at the fp16 tensor-core rate and with
+// 4 bytes per element of operand traffic.
 //
 // Warp roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, 4 or 8
 // epilogue warps (thread = tile row = TMEM lane).
@@ -30,6 +35,8 @@
 // column's candidates with exact fp64 scores.  A merge combines the lists.
 // Two-pass mode: a second pass with the clouds' roles exchanged computes the
 // column lists as row lists (same products, same order, same scores).
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cstring>
 #include <string>
@@ -68,12 +75,17 @@ struct Epi {
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 constexpr uint32_t IDESC_PAIR = idesc_tf32(2 * BM, BN);
+constexpr uint32_t IDESC_F16 = idesc_f16(BM, BN);
+constexpr uint32_t IDESC_F16_PAIR = idesc_f16(2 * BM, BN);
+// fp16 operands: 32 halves per 64-byte slab row (the same bytes as 16 fp32), K = 16 per MMA
+constexpr int BK16 = 32;
 
 struct Params {
     CUtensorMap qmap[2];  // query operand: [0] features (read as tf32 = hi part), [1] low parts
     CUtensorMap dmap[2];  // database operand
-    int terms;            // 1: x*y (TF32); 3: x*y + x*lo(y) + lo(x)*y (3xTF32)
+    int terms;            // 1: x*y (TF32, fp32 operands); 3: hi*hi + hi*lo + lo*hi (fp16 halves)
     int kslabs;
+    const int* exps;      // terms == 3: the clouds' power-of-two scales e_query, e_database
     int q, n;
     int groups, tpg, ct, units;
     const double* q_cost;  // a_i  (certificate only)
@@ -170,6 +182,7 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE, PAIR>& s) {
     const uint32_t bytes = PAIR ? (p.terms == 3 ? PAIR_STAGE_BYTES : A_BYTES + BH_BYTES)
                                 : (p.terms == 3 ? STAGE_BYTES : A_BYTES + B_BYTES);
     const uint32_t cbytes = BN * 8 + (p.d_cost ? BN * 8 : 0) + (ONE ? BN * 4 : 0);
+    const int kw = p.terms == 3 ? BK16 : BK;  // elements per 64-byte slab row
     uint32_t t = 0;
     const Sched sc = schedule<ONE, PAIR>(p);
     for (int u = sc.u0; u < sc.uend; u += sc.ustep) {
@@ -190,21 +203,21 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE, PAIR>& s) {
                 if constexpr (PAIR) {
                     const uint32_t fb = peer_smem(&s.full[stage], 0);
                     if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * bytes);
-                    tma_load_2d_pair(a, &p.qmap[0], fb, ks * BK, rb * BM);
-                    tma_load_2d_pair(a + P_OFF_B, &p.dmap[0], fb, ks * BK, ct * BN + rank * BNH);
+                    tma_load_2d_pair(a, &p.qmap[0], fb, ks * kw, rb * BM);
+                    tma_load_2d_pair(a + P_OFF_B, &p.dmap[0], fb, ks * kw, ct * BN + rank * BNH);
                     if (p.terms == 3) {
-                        tma_load_2d_pair(a + P_OFF_ALO, &p.qmap[1], fb, ks * BK, rb * BM);
-                        tma_load_2d_pair(a + P_OFF_BLO, &p.dmap[1], fb, ks * BK, ct * BN + rank * BNH);
+                        tma_load_2d_pair(a + P_OFF_ALO, &p.qmap[1], fb, ks * kw, rb * BM);
+                        tma_load_2d_pair(a + P_OFF_BLO, &p.dmap[1], fb, ks * kw, ct * BN + rank * BNH);
                     }
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                     continue;
                 }
                 mbar_arrive_expect_tx(&s.full[stage], bytes);
-                tma_load_2d(a, &p.qmap[0], &s.full[stage], ks * BK, rb * BM);
-                tma_load_2d(a + OFF_B, &p.dmap[0], &s.full[stage], ks * BK, ct * BN);
+                tma_load_2d(a, &p.qmap[0], &s.full[stage], ks * kw, rb * BM);
+                tma_load_2d(a + OFF_B, &p.dmap[0], &s.full[stage], ks * kw, ct * BN);
                 if (p.terms == 3) {
-                    tma_load_2d(a + OFF_ALO, &p.qmap[1], &s.full[stage], ks * BK, rb * BM);
-                    tma_load_2d(a + OFF_BLO, &p.dmap[1], &s.full[stage], ks * BK, ct * BN);
+                    tma_load_2d(a + OFF_ALO, &p.qmap[1], &s.full[stage], ks * kw, rb * BM);
+                    tma_load_2d(a + OFF_BLO, &p.dmap[1], &s.full[stage], ks * kw, ct * BN);
                 }
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }
             }
@@ -223,9 +236,16 @@ __device__ __forceinline__ void mma_issuer(const Params& p, Smem<ONE, PAIR>& s, 
     constexpr int STAGES = Smem<ONE, PAIR>::STAGES;
     constexpr int OA_LO = PAIR ? P_OFF_ALO : OFF_ALO, OB = PAIR ? P_OFF_B : OFF_B, OB_LO = PAIR ? P_OFF_BLO : OFF_BLO;
     constexpr uint32_t ID = PAIR ? IDESC_PAIR : IDESC;
-    auto mma = [](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-        if constexpr (PAIR) mma_tf32_pair(d, a, b, ID, acc);
-        else mma_tf32(d, a, b, ID, acc);
+    constexpr uint32_t ID16 = PAIR ? IDESC_F16_PAIR : IDESC_F16;
+    const bool f16 = p.terms == 3;  // fp16 halves (kind::f16), else fp32 features (kind::tf32)
+    auto mma = [f16](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+        if constexpr (PAIR) {
+            if (f16) mma_f16_pair(d, a, b, ID16, acc);
+            else mma_tf32_pair(d, a, b, ID, acc);
+        } else {
+            if (f16) mma_f16(d, a, b, ID16, acc);
+            else mma_tf32(d, a, b, ID, acc);
+        }
     };
     auto commit = [](uint64_t* bar) {
         if constexpr (PAIR) mma_commit_pair(bar);
@@ -396,7 +416,7 @@ __device__ __forceinline__ void column_stage(S& s, const float (&v)[32], int ew,
 
 template <int K, class S>
 __device__ __forceinline__ void column_update(const Params& p, S& s, uint32_t cmask, int ew, int lane,
-                                              int row0, int col0, double cbias, int64_t list_base) {
+                                              int row0, int col0, double cbias, int64_t list_base, float scale) {
     constexpr int KK = K > 0 ? K : 1;
     const float* T = s.trans + ew * 32 * 33;
     const double* RB = s.rbx + ew * 32;
@@ -416,7 +436,7 @@ __device__ __forceinline__ void column_update(const Params& p, S& s, uint32_t cm
         while (mine) {
             const int r = __ffs(mine) - 1;
             mine &= mine - 1;
-            const double dot = (double)(p.scale * T[r * 33 + lane]);
+            const double dot = (double)(scale * T[r * 33 + lane]);
             ct.offer((dot + RB[r]) + cbias, row0 + r);
         }
         store_list<KK>(p, base, ct);
@@ -449,6 +469,8 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
     const int64_t list_base = ONE ? (int64_t)(rgl * 4 + quarter) * p.n : 0;
     // CTA pairs: the accumulator is released on the even CTA's barrier
     const uint32_t tempty_peer = PAIR ? peer_smem(&s.tempty[0], 0) : 0u;
+    // dot = dot_scale * 2^-(e_x + e_y) * (accumulated dot of the scaled halves): exact
+    const float scale = p.terms == 3 ? ldexpf(p.scale, -(p.exps[0] + p.exps[1])) : p.scale;
     TopK<KK> top;
     uint32_t t = 0;
     const Sched sched = schedule<ONE, PAIR>(p);
@@ -491,10 +513,10 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                 const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY : __double2float_rd(top.v[KK - 1]);
                 uint32_t mask, cmask;
                 if (__all_sync(0xffffffffu, live == 32))
-                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, p.scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
+                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
                                                                 live, thr, cmask, acc);
                 else
-                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, p.scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
+                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
                                                                  live, thr, cmask, acc);
                 const bool colwork = ONE && K > 0 && __any_sync(0xffffffffu, cmask != 0u);
                 if (colwork) column_stage(s, v, ew, lane, rbias);
@@ -505,14 +527,14 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                     float vj = 0.0f;
 #pragma unroll
                     for (int t2 = 0; t2 < 32; ++t2) vj = t2 == j ? v[t2] : vj;
-                    const double dot = (double)(p.scale * vj);
+                    const double dot = (double)(scale * vj);
                     const double cbias = wbias[cb + j];
                     const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
                     top.offer(sc, c0 + cb + j);
                 }
                 if (colwork)
                     column_update<K>(p, s, cmask, ew, lane, rb * BM + quarter * 32, c0 + cb, wbias[cb + lane],
-                                     list_base);
+                                     list_base, scale);
             }
             tc_fence_before();
             if (PAIR && rank != 0) mbar_arrive_remote(tempty_peer + buf * (uint32_t)sizeof(uint64_t));
@@ -630,21 +652,55 @@ __global__ void init_columns(double* cval, int* cidx, int* ckey, int64_t lists, 
     }
 }
 
-// Copy features into a TMA-legal layout when needed (row stride a multiple
-// of 16 B) and/or write the low parts x - hi(x), hi(x) = x with its 13 low
-// mantissa bits cleared (the part a kind::tf32 MMA consumes).
-__global__ void prep_kernel(const float* __restrict__ x, int64_t rows, int d, int dp, float* __restrict__ xpad,
-                            float* __restrict__ xlo) {
+// Largest |x| of a cloud (rows x d contiguous fp32) as its bit pattern (atomicMax on
+// non-negative floats orders like the values); *out must start at 0.
+__global__ void absmax_kernel(const float* __restrict__ x, int64_t total, unsigned* out) {
+    unsigned m = 0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x)
+        m = max(m, __float_as_uint(fabsf(x[e])));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((threadIdx.x & 31) == 0 && m) atomicMax(out, m);
+}
+
+// The cloud's power-of-two scale: max |x| 2^e in [2^14, 2^15), e clamped to [-60, 60] so
+// that 2^-(e_x + e_y) stays a normal fp32 number (clouds below 2^-46 lose low bits to
+// fp16 subnormals).  A largest |x| of 2^75 or more (or a non-finite one) cannot be
+// represented and is reported as bad input.
+__device__ __forceinline__ int cloud_exponent(unsigned bits, int* status) {
+    if (bits == 0u) return 0;  // an all-zero cloud
+    const float m = __uint_as_float(bits);
+    if (!(m < 0x1p75f)) { atomicOr(status, kErrBadInput); return 0; }  // too large, infinite or NaN
+    int ex = 0;
+    frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1)
+    return max(-60, min(60, 15 - ex));
+}
+
+// fp16 halves of a cloud, rows padded to dp16 (a multiple of 8) with zeros:
+// hi = fp16(x 2^e), lo = fp16(x 2^e - hi); block 0 also records e.
+__global__ void prep_f16(const float* __restrict__ x, int64_t rows, int d, int dp16, const unsigned* amax,
+                         int* exp_out, int* status, __half* __restrict__ hi, __half* __restrict__ lo) {
+    const int e = cloud_exponent(*amax, status);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *exp_out = e;
+    const int64_t total = rows * dp16;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / dp16;
+        const int c = (int)(i - r * dp16);
+        const float v = c < d ? ldexpf(x[r * d + c], e) : 0.0f;
+        const __half h = __float2half_rn(v);
+        hi[i] = h;
+        lo[i] = __float2half_rn(v - __half2float(h));
+    }
+}
+
+// One-product (TF32) mode: copy fp32 features into a TMA-legal layout (row stride a
+// multiple of 16 B, zero padded) when d is not a multiple of 4.
+__global__ void prep_kernel(const float* __restrict__ x, int64_t rows, int d, int dp, float* __restrict__ xpad) {
     const int64_t total = rows * dp;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = e / dp;
         const int c = (int)(e - r * dp);
-        const float v = c < d ? x[r * d + c] : 0.0f;
-        if (xpad) xpad[e] = v;
-        if (xlo) {
-            const float hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-            xlo[e] = v - hi;
-        }
+        xpad[e] = c < d ? x[r * d + c] : 0.0f;
     }
 }
 
@@ -669,16 +725,19 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-bool make_map(CUtensorMap* m, const float* base, int64_t rows, int dp, int box_rows) {
+// 2-D map of a row-major [rows][dp] operand read in 64-byte slab rows (16 fp32 or
+// 32 fp16 elements) with the 64-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int dp, int box_rows, bool f16 = false) {
     EncodeTiled enc = encode_fn();
     if (!enc) return false;
+    const size_t es = f16 ? 2 : 4;
     cuuint64_t dims[2] = {(cuuint64_t)dp, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)dp * sizeof(float)};
-    cuuint32_t box[2] = {(cuuint32_t)l2sq::BK, (cuuint32_t)box_rows};  // 64-byte rows
+    cuuint64_t strides[1] = {(cuuint64_t)dp * es};
+    cuuint32_t box[2] = {(cuuint32_t)(f16 ? l2sq::BK16 : l2sq::BK), (cuuint32_t)box_rows};  // 64-byte rows
     cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base),
+               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int K, int SM, bool SWAP, bool ONE = false, bool PAIR = false>
@@ -854,7 +913,10 @@ inline OnePlan one_plan(int64_t q, int64_t n, int sms, int min_groups, bool pair
 
 // Scratch layout of one ℓ2² scan call.  With base == nullptr only sizes it.
 struct L2sqLayout {
-    float *xpad = nullptr, *ypad = nullptr, *xlo = nullptr, *ylo = nullptr;
+    float *xpad = nullptr, *ypad = nullptr;
+    __half *xh = nullptr, *xl = nullptr, *yh = nullptr, *yl = nullptr;  // 3-term split: fp16 halves
+    unsigned* amax = nullptr;  // [2] largest |x|, |y| (bit patterns)
+    int* exps = nullptr;       // [2] the clouds' power-of-two scales
     double *pv1 = nullptr, *pv2 = nullptr, *cta = nullptr;
     int *pi1 = nullptr, *pi2 = nullptr, *status = nullptr;
     int* ckey = nullptr;  // one-pass column lists and thresholds
@@ -875,7 +937,8 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     const int K = k > 0 ? bucket_of(k) : 0;
     const int prec = precision & 0xF;
     const int dp = (int)((d + 3) / 4 * 4);
-    const bool pad = dp != d;
+    const int dp16 = (int)((d + 7) / 8 * 8);
+    const bool pad = prec != 3 && dp != d;
     Arena ar{static_cast<char*>(base), size, 0};
     auto need = [&](bool cond, auto*& ptr, size_t count) {
         using T = std::remove_pointer_t<std::remove_reference_t<decltype(ptr)>>;
@@ -885,8 +948,12 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     };
     need(pad, L.xpad, (size_t)q * dp);
     need(pad, L.ypad, (size_t)n * dp);
-    need(prec == 3, L.xlo, (size_t)q * dp);
-    need(prec == 3, L.ylo, (size_t)n * dp);
+    need(prec == 3, L.xh, (size_t)q * dp16);
+    need(prec == 3, L.xl, (size_t)q * dp16);
+    need(prec == 3, L.yh, (size_t)n * dp16);
+    need(prec == 3, L.yl, (size_t)n * dp16);
+    need(prec == 3, L.amax, 2);
+    need(prec == 3, L.exps, 2);
     const int slices = K > 0 ? l2sq_slices(K) : 1;
     const size_t npad = (size_t)(n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     const size_t qpad = (size_t)(q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
@@ -938,16 +1005,25 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     const bool rows_only = (precision & L2SQ_ROWS_ONLY) != 0;
     if (rows_only) want_stats = 0;
     const int dp = (int)((d + 3) / 4 * 4);
+    const int dp16 = (int)((d + 7) / 8 * 8);
     cudaError_t e = cudaMemsetAsync(L.status, 0, sizeof(int), st);
     if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
     const float* xs = x;
     const float* ys = y;
     const int prep_blocks = device_sms() * 8;
-    if (L.xpad || L.xlo) {
-        l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(x, q, (int)d, dp, L.xpad, L.xlo);
-        l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(y, n, (int)d, dp, L.ypad, L.ylo);
+    if (prec == 3) {  // fp16 halves of both clouds, each scaled by its power of two
+        e = cudaMemsetAsync(L.amax, 0, 2 * sizeof(unsigned), st);
+        if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
+        l2sq::absmax_kernel<<<prep_blocks, 256, 0, st>>>(x, q * d, L.amax);
+        l2sq::absmax_kernel<<<prep_blocks, 256, 0, st>>>(y, n * d, L.amax + 1);
+        l2sq::prep_f16<<<prep_blocks, 256, 0, st>>>(x, q, (int)d, dp16, L.amax, L.exps, L.status, L.xh, L.xl);
+        l2sq::prep_f16<<<prep_blocks, 256, 0, st>>>(y, n, (int)d, dp16, L.amax + 1, L.exps + 1, L.status, L.yh, L.yl);
+        count_launches(4);
+    } else if (L.xpad) {
+        l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(x, q, (int)d, dp, L.xpad);
+        l2sq::prep_kernel<<<prep_blocks, 256, 0, st>>>(y, n, (int)d, dp, L.ypad);
         count_launches(2);
-        if (L.xpad) { xs = L.xpad; ys = L.ypad; }
+        xs = L.xpad; ys = L.ypad;
     }
     const int64_t npad = (n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     const int64_t qpad = (q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
@@ -964,12 +1040,18 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     std::memset(&p, 0, sizeof(p));
     const bool pair = L.one_pass && L.one.pair;
     const int brows = pair ? l2sq::BNH : l2sq::BN;  // database box: half a column tile per CTA of a pair
-    bool maps = make_map(&p.qmap[0], xs, q, dp, l2sq::BM) && make_map(&p.dmap[0], ys, n, dp, brows);
-    if (prec == 3) maps = maps && make_map(&p.qmap[1], L.xlo, q, dp, l2sq::BM) && make_map(&p.dmap[1], L.ylo, n, dp, brows);
-    else { p.qmap[1] = p.qmap[0]; p.dmap[1] = p.dmap[0]; }
+    bool maps;
+    if (prec == 3) {
+        maps = make_map(&p.qmap[0], L.xh, q, dp16, l2sq::BM, true) && make_map(&p.dmap[0], L.yh, n, dp16, brows, true) &&
+               make_map(&p.qmap[1], L.xl, q, dp16, l2sq::BM, true) && make_map(&p.dmap[1], L.yl, n, dp16, brows, true);
+    } else {
+        maps = make_map(&p.qmap[0], xs, q, dp, l2sq::BM) && make_map(&p.dmap[0], ys, n, dp, brows);
+        p.qmap[1] = p.qmap[0]; p.dmap[1] = p.dmap[0];
+    }
     if (!maps) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
     p.terms = prec == 3 ? 3 : 1;
-    p.kslabs = (dp + l2sq::BK - 1) / l2sq::BK;
+    p.kslabs = prec == 3 ? (dp16 + l2sq::BK16 - 1) / l2sq::BK16 : (dp + l2sq::BK - 1) / l2sq::BK;
+    p.exps = L.exps;
     p.scale = (float)dot_scale;
     p.status = L.status;
     p.cta_stats = L.cta;
@@ -1022,10 +1104,16 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         // pass 2: y rows are the queries, same products in the same order;
         // the maps are rebuilt because a map fixes its box height (A 128 rows, B 256 rows)
         l2sq::Params p2 = p;
-        bool maps2 = make_map(&p2.qmap[0], ys, n, dp, l2sq::BM) && make_map(&p2.dmap[0], xs, q, dp, l2sq::BN);
-        if (prec == 3)
-            maps2 = maps2 && make_map(&p2.qmap[1], L.ylo, n, dp, l2sq::BM) && make_map(&p2.dmap[1], L.xlo, q, dp, l2sq::BN);
-        else { p2.qmap[1] = p2.qmap[0]; p2.dmap[1] = p2.dmap[0]; }
+        bool maps2;
+        if (prec == 3) {
+            maps2 = make_map(&p2.qmap[0], L.yh, n, dp16, l2sq::BM, true) &&
+                    make_map(&p2.dmap[0], L.xh, q, dp16, l2sq::BN, true) &&
+                    make_map(&p2.qmap[1], L.yl, n, dp16, l2sq::BM, true) &&
+                    make_map(&p2.dmap[1], L.xl, q, dp16, l2sq::BN, true);
+        } else {
+            maps2 = make_map(&p2.qmap[0], ys, n, dp, l2sq::BM) && make_map(&p2.dmap[0], xs, q, dp, l2sq::BN);
+            p2.qmap[1] = p2.qmap[0]; p2.dmap[1] = p2.dmap[0];
+        }
         if (!maps2) { err = "cuTensorMapEncodeTiled failed (alignment or driver entry point)"; return 5; }
         p2.q = (int)n; p2.n = (int)q;
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;

@@ -37,7 +37,8 @@ def _cloud(q, n, d, seed):
 
 def _bound(x, y, r, c, scale, biases, precision):
     """Per-pair error bound of the tensor-core score.
-    3xTF32: dropped lo*lo term and truncation of lo parts ~ 2^-20 |x||y| per product,
+    fp32 mode (3-term split on fp16 halves of the power-of-two scaled clouds): the
+    dropped lo*lo term and the rounding of lo, within 3 2^-22 |x||y| per product,
     plus fp32 accumulation (d+2)u (any order).  TF32: 2^-9 per product."""
     x64, y64 = np.asarray(x, np.float64), np.asarray(y, np.float64)
     d = x64.shape[1]
@@ -205,6 +206,35 @@ def test_norm_scan_bit_exact(hb, cuda, oracle, kind, q, n, d, k):
 
 
 # (q, n, d, k): several row blocks per row group, ragged tiles, k > n, one feature
+@pytest.mark.parametrize("shift", [-20, 20])
+@pytest.mark.parametrize("passes", [1, 2])
+def test_l2sq_power_of_two_scaling(hb, cuda, shift, passes):
+    """Each cloud's fp16 halves are taken after scaling it by a power of two, so a
+    cloud scaled by 2^s gives the same halves: the lists of the clouds scaled by 2^s
+    (costs and biases by 2^2s) are the unscaled lists, with every score times 2^2s
+    exactly."""
+    x, y, a, b, f, g = _cloud(700, 900, 40, seed=31)
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    c = 2.0 ** shift
+
+    def run(sx, sc):
+        return [t.clone() for t in hb.l2sq_scan(T(x * sx, torch.float32), T(y * sx, torch.float32), T(a * sc, torch.float64),
+                                               T(b * sc, torch.float64), T((f - a) * sc, torch.float64),
+                                               T((g - b) * sc, torch.float64), 8, passes=passes)]
+    base, scaled = run(1.0, 1.0), run(c, c * c)
+    assert torch.equal(base[1], scaled[1]) and torch.equal(base[3], scaled[3])
+    assert torch.equal(base[0] * (c * c), scaled[0]) and torch.equal(base[2] * (c * c), scaled[2])
+
+
+def test_l2sq_rejects_non_finite_features(hb, cuda):
+    x, y, a, b, f, g = _cloud(64, 80, 8, seed=2)
+    x[3, 2] = np.inf
+    T = lambda v, dt: torch.as_tensor(v, dtype=dt, device=cuda)  # noqa: E731
+    with pytest.raises(ValueError, match="magnitude"):
+        hb.l2sq_scan(T(x, torch.float32), T(y, torch.float32), T(a, torch.float64), T(b, torch.float64),
+                     T(f - a, torch.float64), T(g - b, torch.float64), 4)
+
+
 @pytest.mark.parametrize("q,n,d,k,groups,precision", ONE_PASS_CASES)
 def test_l2sq_cta_pairs_equal_single_ctas(hb, cuda, q, n, d, k, groups, precision):
     """The one-pass kernel run as CTA pairs (one M = 256 cta_group::2 MMA over both
