@@ -45,11 +45,9 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per pair of one pass-1 launch, from an ncu capture of the
-# scan kernel scaled by the pairs it processed (see profiles/ for the capture and command).
-# DRAM bytes (read + write) per pair of the scan kernel from ncu captures (profiles/l2sq_scan_kernel_c5_d256.md):
-# one-pass measured on the full C5 launch, two-pass (pass 1) on a 131072^2 launch
-DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 2.379, (256, "fp32", "two-pass"): 0.1357}
+# DRAM bytes (read + write) per pair of the scan kernel from ncu captures
+# (profiles/l2sq_scan_kernel_c5_d256.md), scaled by the pairs of the launch
+DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 1.1672}
 
 
 # per-path default sizes: config 5 (m = n = 2^20, d = 256) for the l2sq scans, pair costs and
@@ -279,7 +277,7 @@ def scan_mode(args):
 def workload_config(args):
     return {"workload": f"C5 isolated pricing scan, l2sq, m=n={args.n}, d={args.d}, k={args.k}",
             "n": args.n, "m": args.n, "d": args.d, "topk": args.k, "cost": "l2sq", "dot_scale": 2.0,
-            "precision": {"fp32": "3xTF32 (fp32-class dot)", "tf32": "1xTF32"}[args.precision],
+            "precision": {"fp32": "3-term fp16 split (fp32-class dot)", "tf32": "1xTF32"}[args.precision],
             "scan_mode": scan_mode(args),
             "parallelism": f"source-row shards x{args.gpus}",
             "l2_policy": "inputs (2 GB clouds) larger than L2; no flush"}
@@ -364,7 +362,7 @@ def run_ours(args):
         out = {
             "metric": "pricing-scan Gpairs/s (m·n)", "value": value, "unit": "Gpairs/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "tf32x3/f64" if args.precision == "fp32" else "tf32/f64",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16x3/f64" if args.precision == "fp32" else "tf32/f64",
             "data": "synthetic (seeded N(0,I) clouds, Gaussian duals scaled by the median cost)",
             "config": workload_config(args),
             "gpu_launches": int(launches),
@@ -374,8 +372,8 @@ def run_ours(args):
                                     if mode == "one-pass" else
                                     "hb::l2sq::scan_kernel (pass 1 of 2: source rows, score terms)"),
                          "pass_ms": times, "peak_source": f"{peak_kind} bf16 dense (sustained)",
-                         "note": ("algorithmic flops 2*d per pair; the 3xTF32 split issues 3 tf32 products "
-                                  "per pair on a pipe with half the bf16 rate")},
+                         "note": ("algorithmic flops 2*d per pair; the fp32-class split issues 3 fp16 "
+                                  "products per pair (3x the algorithmic tensor work)")},
             "clocks": clocks.summary(),
             "median_pair_cost": med,
         }
@@ -629,11 +627,11 @@ def run_initial(args, hb, dev, peaks):
     hb.set_kernel_timing(False)
     peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
     achieved = 2.0 * d * n * n / (kms[0] / 1e3) / 1e12 if kms else float("nan")
-    extra = {"dtype": "tf32x3/f64" if args.precision == "fp32" else "tf32/f64", "roofline": {
+    extra = {"dtype": "f16x3/f64" if args.precision == "fp32" else "tf32/f64", "roofline": {
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "traffic": None, "kernel": "hb::l2sq::scan_kernel<16, 0, 0, 0> (row lists only)",
         "peak_source": "measured bf16 dense (sustained)",
-        "note": "algorithmic flops 2*d per pair; 3xTF32 issues 3 tf32 products per pair at half the bf16 rate"}}
+        "note": "algorithmic flops 2*d per pair; the fp32-class split issues 3 fp16 products per pair"}}
     if not args.no_cpu:  # the reference's CPU directional scan is torch tiles + topk; the oracle port stands in
         import oracle
         rows = 32

@@ -152,7 +152,7 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     {
         const int base = precision & ~(HB_L2SQ_TWO_PASS | HB_L2SQ_ONE_PASS | HB_L2SQ_CTA_PAIRS | HB_L2SQ_SINGLE_CTA);
         if (base != 1 && base != 3)
-            return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32), optionally | a pass flag");
+            return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (fp32-class split), optionally | a pass flag");
         if ((precision & HB_L2SQ_TWO_PASS) && (precision & HB_L2SQ_ONE_PASS))
             return fail(HB_BAD_ARGUMENT, "HB_L2SQ_ONE_PASS and HB_L2SQ_TWO_PASS are exclusive");
         if ((precision & HB_L2SQ_CTA_PAIRS) && (precision & HB_L2SQ_SINGLE_CTA))
@@ -231,7 +231,7 @@ int hb_l2sq_topk(const float* x, const float* y, int64_t q, int64_t n, int64_t d
         return fail(HB_BAD_ARGUMENT, "q, n, d must be in [1, 2^31)");
     if (k < 1 || k > 32) return fail(HB_BAD_ARGUMENT, "k must be in 1..32");
     if (dot_scale != 1.0 && dot_scale != 2.0) return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
-    if (precision != 1 && precision != 3) return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (3xtf32)");
+    if (precision != 1 && precision != 3) return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (fp32-class split)");
     const int flags = precision | hb::L2SQ_ROWS_ONLY;
     if (workspace_bytes < hb::l2sq_bytes(q, n, d, k, flags, 0))
         return fail(HB_WORKSPACE, "workspace smaller than hb_l2sq_topk_workspace()");

@@ -50,7 +50,7 @@ namespace hb {
 namespace l2sq {
 
 // K slab of 16 fp32 (64-byte rows, 64-byte swizzle).  A stage holds the query
-// and database tiles and, for the 3xTF32 split, their low parts, so all three
+// and database tiles and, for the 3-term split, their low parts, so all three
 // products of a slab come from one fetch: [A | A_lo | B | B_lo] = 8+8+16+16 KB.
 constexpr int BM = 128, BN = 256, BK = 16;
 constexpr int A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;

@@ -30,7 +30,7 @@ from ._lib import Workspace, check, lib, ptr, stream_handle
 from .perturb import make_perturbation
 
 BUCKETS = (1, 2, 4, 8, 16, 32)
-PRECISION = {"fp32": 3, "3xtf32": 3, "tf32": 1}
+PRECISION = {"fp32": 3, "3xtf32": 3, "f16x3": 3, "tf32": 1}  # "3xtf32": the former name of 3
 _ROUTES = Counter()
 
 
@@ -362,7 +362,7 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
     if str(compute_precision) not in {"fp32", "fp64", "tf32"}:
         raise ValueError("compute_precision must be one of: fp32, fp64")
     if str(compute_precision) == "fp64":
-        raise NotImplementedError("hello_ot_b200 computes the bilinear dot on tensor cores (fp32-class 3xTF32); "
+        raise NotImplementedError("hello_ot_b200 computes the bilinear dot on tensor cores (fp32-class 3-term fp16 split); "
                                   "compute_precision='fp64' is not implemented")
     if col_kernel not in ("auto", "current", "warp2", "warp4"):
         raise ValueError("col_kernel must be one of {auto, current, warp2, warp4}")

@@ -68,7 +68,9 @@ int hb_last_kernel_times(double* ms, int capacity);
  * missing slots (-inf, -1).  k in 0..32 (0: certificate only, outputs unused).
  * stats5 (device, 5 doubles): [sum max(s,0)^2, sum cost^2, max s+, max |cost|,
  * count s>0] over all q*n pairs; written when compute_stats != 0.
- * precision: 1 = one TF32 tensor-core product, 3 = 3xTF32 split (fp32-class),
+ * precision: 1 = one TF32 tensor-core product, 3 = 3-term split hi*hi + hi*lo + lo*hi
+ * on fp16 halves of the clouds scaled by powers of two (fp32-class dots; feature
+ * magnitudes must be finite and below 2^75, else HB_BAD_INPUT),
  * optionally OR one of HB_L2SQ_ONE_PASS / HB_L2SQ_TWO_PASS.  A one-pass scan
  * (k <= 8) keeps row lists in registers and column lists in the workspace; a
  * two-pass scan runs the row pass again with the clouds' roles exchanged.  Both

@@ -2,7 +2,7 @@
 
 The reference computes the ℓ2² dot products in fp32 (cuBLAS SGEMM on the GPU,
 torch.mm on the CPU) and norm distances in fp32; this build computes them on
-tcgen05 tensor cores (3×TF32 split) or fp32 CUDA cores.  None of these agree
+tcgen05 tensor cores (3-term fp16 split) or fp32 CUDA cores.  None of these agree
 bit for bit, so candidate lists are compared against the exact fp64 scores of
 the oracle with a stated per-pair error bound ``eps``: an index set must match
 exactly wherever the exact score gap at the selection boundary exceeds

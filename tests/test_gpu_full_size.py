@@ -45,7 +45,7 @@ def _exact_rows(x, y, a, b, f, g, idx):
 
 
 def _bound_rows(x, y, idx, cols):
-    """3xTF32 + fp32-accumulation bound s (2^-19 + 2 (d+2) u) sum |x y| per pair."""
+    """3-term fp16 split + fp32-accumulation bound s (2^-19 + 2 (d+2) u) sum |x y| per pair."""
     ax = x[idx].abs().double()
     sabs = torch.stack([(ax[i] * y[cols[i]].abs().double()).sum(-1) for i in range(len(idx))])
     return 2.0 * (2.0 ** -19 + 2 * (D + 2) * U32) * sabs + 1e-9
