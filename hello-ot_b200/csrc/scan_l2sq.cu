@@ -115,8 +115,8 @@ struct __align__(1024) SmemT {
     double ccost[NCS][BN];                     // the tile's column costs (cost terms)
     int ckey[ONE ? NCS : 1][ONE ? BN : 4];     // the tile's column thresholds (one pass)
     // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all), fp32
-    // constants read once per pair: x = bias, y = 2^-21 |bias| (the bias part of the
-    // screening margin), z = |y|^2, w = column threshold (one pass)
+    // constants read once per pair: x = bias, y = the column's screening threshold (one
+    // pass; threshold less the rounding margin), z = column cost (cost terms), w unused
     float4 col[4 * BN];
     float trans[ONE ? MAX_EW * 32 * 33 : 1];   // per warp: 32 x 32 chunk, transposed
     double rbx[ONE ? MAX_EW * 32 : 1];         // per warp: the chunk rows' biases
@@ -294,12 +294,13 @@ enum : int { kScoreStats = 1, kCostStats = 2 };
 // Phase 1 of one 32-column chunk, branch-free and in fp32: fp32 score / cost
 // of every pair (within 2^-22 (|dot| + |a| + |b| + |biases|) of the fp64
 // values for the same dot), certificate partials (fp32 over 8 terms, then
-// fp64), and the candidate mask: columns whose fp32 score plus the rounding
-// margin 2^-21 (|dot| + |biases|) reaches the row's k-th score rounded down.
+// fp64), and the candidate masks: columns whose fp32 score reaches the row's
+// screening threshold (its k-th score rounded down, less the rounding margin,
+// screen_threshold) and, one pass, the column's screening threshold.
 // FULL: all 32 columns are valid for the whole warp (no per-column masking).
 template <int K, int SM, bool SWAP, bool FULL, bool ONE>
 __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float scale, const float4* col,
-                                                 float rbias_f, float rmarg_f, float rcost_f, int live, float thr,
+                                                 float rbias_f, float rcost_f, int live, float thr,
                                                  uint32_t& cmask, double (&acc)[5]) {
     uint32_t mask = 0, cm = 0;
     float num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
@@ -319,9 +320,8 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
                 cnt += pos ? 1 : 0;
             }
             if (K > 0) {
-                const float m = fmaf(fabsf(dotf), 0x1p-21f, cc.y + rmarg_f);
-                mask |= (ok && sf + m >= thr) ? (1u << j) : 0u;
-                if (ONE) cm |= (ok && sf + m >= cc.w) ? (1u << j) : 0u;
+                mask |= (ok && sf >= thr) ? (1u << j) : 0u;
+                if (ONE) cm |= (ok && sf >= cc.y) ? (1u << j) : 0u;
             }
         }
         if (SM & kCostStats) {
@@ -341,6 +341,16 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
     }
     cmask = cm;
     return mask;
+}
+
+// Screening threshold with the rounding margin folded in: a pair whose exact score
+// reaches t has an fp32 score of at least t - (2^-21 |t| + 2^-20 (|cbias| + |rbias|));
+// b = 2^-20 (|cbias| + |rbias|) bounded over the tile; inflated by 2^-20 for the fp32
+// evaluation of the margin itself and rounded down.
+__device__ __forceinline__ float screen_threshold(float t, float b) {
+    if (!(t > -INFINITY) || !(t < INFINITY)) return t;
+    const float m = fmaf(fabsf(t), 0x1p-21f, b) * (1.0f + 0x1p-20f);
+    return __fsub_rd(t, m);
 }
 
 // Column thresholds.  Every full column list's k-th score is a lower bound on
@@ -481,7 +491,8 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
         const bool rvalid = row < p.q;
         const double rbias = rvalid ? p.q_bias[row] : 0.0;
         const float rbias_f = (float)rbias;
-        const float rmarg_f = 0x1p-21f * fabsf(rbias_f);
+        const float rmarg_f = 0x1p-20f * fabsf(rbias_f);
+        const float rbmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(rbias_f))));
         const float rcost_f = ((SM & kCostStats) && rvalid) ? (float)p.q_cost[row] : 0.0f;
         top.reset();
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
@@ -492,14 +503,20 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
             if (!mbar_wait(&s.cfull[cs], (t / CSLOTS) & 1, &s.abort, p.status)) return;
             const double* wbias = s.cbias[cs] + slice * SLICE;  // exact column biases of the slice
             __syncwarp();  // the warp is done reading the previous tile's constants
+            unsigned cbm = 0u;
             for (int c = lane; c < SLICE; c += 32) {
                 const bool ok = c < ncols;
                 const float bf = ok ? (float)wbias[c] : 0.0f;
                 float cf = 0.0f, th = 0.0f;
                 if constexpr ((SM & kCostStats) != 0) cf = ok ? (float)s.ccost[cs][slice * SLICE + c] : 0.0f;
-                if constexpr (ONE) th = ok ? order_value(s.ckey[cs][slice * SLICE + c]) : INFINITY;
-                wcol[c] = make_float4(bf, 0x1p-21f * fabsf(bf), cf, th);
+                if constexpr (ONE) {
+                    th = ok ? order_value(s.ckey[cs][slice * SLICE + c]) : INFINITY;
+                    th = screen_threshold(th, 0x1p-20f * (fabsf(bf) + rbmax));
+                }
+                cbm = max(cbm, __float_as_uint(fabsf(bf)));
+                wcol[c] = make_float4(bf, th, cf, 0.0f);
             }
+            const float cbmax = __uint_as_float(__reduce_max_sync(0xffffffffu, cbm));
             __syncwarp();
             if (!mbar_wait(&s.tfull[buf], aph, &s.abort, p.status)) return;
             tc_fence_after();
@@ -510,13 +527,14 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                 tmem_wait_ld(v);
                 const int cb = ch * 32;
                 const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
-                const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY : __double2float_rd(top.v[KK - 1]);
+                const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY
+                                  : screen_threshold(__double2float_rd(top.v[KK - 1]), 0x1p-20f * cbmax + rmarg_f);
                 uint32_t mask, cmask;
                 if (__all_sync(0xffffffffu, live == 32))
-                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
+                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcol + cb, rbias_f, rcost_f,
                                                                 live, thr, cmask, acc);
                 else
-                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, scale, wcol + cb, rbias_f, rmarg_f, rcost_f,
+                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, scale, wcol + cb, rbias_f, rcost_f,
                                                                  live, thr, cmask, acc);
                 const bool colwork = ONE && K > 0 && __any_sync(0xffffffffu, cmask != 0u);
                 if (colwork) column_stage(s, v, ew, lane, rbias);
