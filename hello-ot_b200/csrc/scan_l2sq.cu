@@ -899,7 +899,8 @@ inline bool use_pairs(int precision, int64_t d) {
 inline bool use_one_pass(int K, int precision, int64_t q, int64_t d) {
     if (K < 1 || K > 8 || (precision & (HB_L2SQ_TWO_PASS | L2SQ_ROWS_ONLY))) return false;
     if (precision & HB_L2SQ_ONE_PASS) return true;
-    return d >= 128 || (d >= 64 && q >= (int64_t(1) << 19));
+    (void)q;
+    return d >= 128;
 }
 
 // CTA pairs: a rectangle is a cluster of two CTAs whose units are pairs of row

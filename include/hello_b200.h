@@ -76,8 +76,7 @@ int hb_last_kernel_times(double* ms, int capacity);
  * two-pass scan runs the row pass again with the clouds' roles exchanged.  Both
  * give the same lists bit for bit (the certificate sums differ in summation
  * order only).  Without a flag the scan picks one pass when k <= 8 and the
- * tensor-core work per pair dominates the list upkeep (d >= 128, or d >= 64
- * with q >= 2^19), else two.
+ * tensor-core work per pair dominates the list upkeep (d >= 128), else two.
  * The one-pass kernel runs either one CTA per rectangle of the pair space or
  * CTA pairs (clusters of two sharing each column tile through a cta_group::2
  * MMA); OR HB_L2SQ_CTA_PAIRS or HB_L2SQ_SINGLE_CTA to force either (same lists).
