@@ -117,7 +117,9 @@ struct __align__(1024) SmemT {
     // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all), fp32
     // constants read once per pair: x = bias, y = the column's screening threshold (one
     // pass; threshold less the rounding margin), z = column cost (cost terms), w unused
-    float4 col[4 * BN];
+    __align__(16) float colx[4 * BN];  // bias
+    __align__(16) float coly[4 * BN];  // column screening threshold (one pass)
+    __align__(16) float colz[4 * BN];  // column cost (cost terms)
     float trans[ONE ? MAX_EW * 32 * 33 : 1];   // per warp: 32 x 32 chunk, transposed
     double rbx[ONE ? MAX_EW * 32 : 1];         // per warp: the chunk rows' biases
     double red[MAX_EW * 5];
@@ -298,38 +300,75 @@ enum : int { kScoreStats = 1, kCostStats = 2 };
 // screening threshold (its k-th score rounded down, less the rounding margin,
 // screen_threshold) and, one pass, the column's screening threshold.
 // FULL: all 32 columns are valid for the whole warp (no per-column masking).
+// Two adjacent columns per instruction where the arithmetic allows it (fma / add
+// .rn.f32x2: each lane of the pair rounds like the scalar instruction).
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t r) {
+    float2 f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(r));
+    return f;
+}
+__device__ __forceinline__ uint64_t add_x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma_x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 template <int K, int SM, bool SWAP, bool FULL, bool ONE>
-__device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float scale, const float4* col,
-                                                 float rbias_f, float rcost_f, int live, float thr,
+__device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float scale, const float* cx, const float* cy,
+                                                 const float* cz, float rbias_f, float rcost_f, int live, float thr,
                                                  uint32_t& cmask, double (&acc)[5]) {
     uint32_t mask = 0, cm = 0;
-    float num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
+    uint64_t num2[2] = {0, 0}, den2[2] = {0, 0};  // partial sums of columns j & 3 = (0, 1) and (2, 3)
     float mpos = 0.0f, mcost = 0.0f;
     int cnt = 0;
+    const uint64_t sc2 = pk2(scale, scale), nsc2 = pk2(-scale, -scale);
+    const uint64_t rb2 = pk2(rbias_f, rbias_f), rc2 = pk2(rcost_f, rcost_f);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const bool ok = FULL || j < live;
-        const float dotf = scale * v[j];
-        const float4 cc = col[j];  // broadcast
+    for (int j = 0; j < 32; j += 2) {
+        const bool ok0 = FULL || j < live, ok1 = FULL || j + 1 < live;
+        const uint64_t v2 = pk2(v[j], v[j + 1]);
+        // scale * v is exact (scale is a power of two), so each fma rounds like the add it replaces
         if (K > 0 || (SM & kScoreStats)) {
-            const float sf = SWAP ? ((dotf + cc.x) + rbias_f) : ((dotf + rbias_f) + cc.x);
+            const uint64_t cx2 = *reinterpret_cast<const uint64_t*>(cx + j);  // broadcast
+            const uint64_t sf2 = SWAP ? add_x2(fma_x2(sc2, v2, cx2), rb2) : add_x2(fma_x2(sc2, v2, rb2), cx2);
+            const float2 sf = upk2(sf2);
             if (SM & kScoreStats) {
-                const bool pos = ok && sf > 0.0f;
-                num4[j & 3] = fmaf(sf, pos ? sf : 0.0f, num4[j & 3]);
-                mpos = fmaxf(mpos, FULL ? sf : (ok ? sf : 0.0f));
-                cnt += pos ? 1 : 0;
+                const bool pos0 = ok0 && sf.x > 0.0f, pos1 = ok1 && sf.y > 0.0f;
+                num2[(j >> 1) & 1] = fma_x2(sf2, pk2(pos0 ? sf.x : 0.0f, pos1 ? sf.y : 0.0f), num2[(j >> 1) & 1]);
+                mpos = fmaxf(mpos, FULL ? sf.x : (ok0 ? sf.x : 0.0f));
+                mpos = fmaxf(mpos, FULL ? sf.y : (ok1 ? sf.y : 0.0f));
+                cnt += (pos0 ? 1 : 0) + (pos1 ? 1 : 0);
             }
             if (K > 0) {
-                mask |= (ok && sf >= thr) ? (1u << j) : 0u;
-                if (ONE) cm |= (ok && sf >= cc.y) ? (1u << j) : 0u;
+                mask |= ((ok0 && sf.x >= thr) ? (1u << j) : 0u) | ((ok1 && sf.y >= thr) ? (2u << j) : 0u);
+                if (ONE) {
+                    const float2 cyy = *reinterpret_cast<const float2*>(cy + j);
+                    cm |= ((ok0 && sf.x >= cyy.x) ? (1u << j) : 0u) | ((ok1 && sf.y >= cyy.y) ? (2u << j) : 0u);
+                }
             }
         }
         if (SM & kCostStats) {
-            const float cf = (rcost_f + cc.z) - dotf;
-            den4[j & 3] = fmaf(cf, ok ? cf : 0.0f, den4[j & 3]);
-            mcost = fmaxf(mcost, ok ? fabsf(cf) : 0.0f);
+            const uint64_t cz2 = *reinterpret_cast<const uint64_t*>(cz + j);
+            const uint64_t cf2 = fma_x2(nsc2, v2, add_x2(rc2, cz2));
+            const float2 cf = upk2(cf2);
+            const uint64_t m2 = FULL ? cf2 : pk2(ok0 ? cf.x : 0.0f, ok1 ? cf.y : 0.0f);
+            den2[(j >> 1) & 1] = fma_x2(cf2, m2, den2[(j >> 1) & 1]);
+            mcost = fmaxf(mcost, ok0 ? fabsf(cf.x) : 0.0f);
+            mcost = fmaxf(mcost, ok1 ? fabsf(cf.y) : 0.0f);
         }
     }
+    const float2 n01 = upk2(num2[0]), n23 = upk2(num2[1]), d01 = upk2(den2[0]), d23 = upk2(den2[1]);
+    const float num4[4] = {n01.x, n01.y, n23.x, n23.y}, den4[4] = {d01.x, d01.y, d23.x, d23.y};
     if (SM & kScoreStats) {
         acc[0] += ((double)num4[0] + (double)num4[1]) + ((double)num4[2] + (double)num4[3]);
         acc[2] = fmax(acc[2], (double)mpos);
@@ -472,7 +511,9 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
     const int quarter = warp & 3;           // TMEM lanes this warp may read
     const int slice = ew / 4;
     const int r = quarter * 32 + lane;      // tile row owned by this thread
-    float4* wcol = s.col + ew * SLICE;
+    float* wcx = s.colx + ew * SLICE;
+    float* wcy = s.coly + ew * SLICE;
+    float* wcz = s.colz + ew * SLICE;
     // one-pass: this warp's column lists (row group of the CTA [and its rank in the
     // pair], TMEM lane quarter)
     const int rgl = PAIR ? (int)(blockIdx.x >> 1) / p.groups * 2 + rank : (int)blockIdx.x / p.groups;
@@ -514,7 +555,7 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                     th = screen_threshold(th, 0x1p-20f * (fabsf(bf) + rbmax));
                 }
                 cbm = max(cbm, __float_as_uint(fabsf(bf)));
-                wcol[c] = make_float4(bf, th, cf, 0.0f);
+                wcx[c] = bf; wcy[c] = th; wcz[c] = cf;
             }
             const float cbmax = __uint_as_float(__reduce_max_sync(0xffffffffu, cbm));
             __syncwarp();
@@ -531,10 +572,10 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                                   : screen_threshold(__double2float_rd(top.v[KK - 1]), 0x1p-20f * cbmax + rmarg_f);
                 uint32_t mask, cmask;
                 if (__all_sync(0xffffffffu, live == 32))
-                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcol + cb, rbias_f, rcost_f,
+                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcx + cb, wcy + cb, wcz + cb, rbias_f, rcost_f,
                                                                 live, thr, cmask, acc);
                 else
-                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, scale, wcol + cb, rbias_f, rcost_f,
+                    mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, scale, wcx + cb, wcy + cb, wcz + cb, rbias_f, rcost_f,
                                                                  live, thr, cmask, acc);
                 const bool colwork = ONE && K > 0 && __any_sync(0xffffffffu, cmask != 0u);
                 if (colwork) column_stage(s, v, ew, lane, rbias);
