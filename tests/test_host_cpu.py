@@ -112,3 +112,17 @@ def test_l2sq_pass_flags_are_validated_before_launch(hb):
 def test_coarsest_rejects_cpu_device(hb):
     with pytest.raises(ValueError, match="CUDA"):
         hb.solve_leaf_from_cost(cost=np.ones((2, 2)), source_mass=[0.5, 0.5], target_mass=[0.5, 0.5], device="cpu")
+
+
+def test_python_flags_match_the_header(hb):
+    """The binding's flag values are the header's (a mismatch would silently select
+    another pass mode, CTA layout or node-sum order)."""
+    header = (REPO / "include" / "hello_b200.h").read_text()
+    defs = {m.group(1): int(m.group(2), 0) for m in re.finditer(r"#define (HB_\w+) (0x[0-9a-fA-F]+|\d+)\b", header)}
+    enums = {m.group(1): int(m.group(2)) for m in re.finditer(r"(HB_PDLP_SUMS_\w+) = (\d+)", header)}
+    scan = hb.scan
+    assert scan.L2SQ_PASS_FLAGS[2] == defs["HB_L2SQ_TWO_PASS"] and scan.L2SQ_PASS_FLAGS[1] == defs["HB_L2SQ_ONE_PASS"]
+    assert scan.L2SQ_CTA_FLAGS[2] == defs["HB_L2SQ_CTA_PAIRS"] and scan.L2SQ_CTA_FLAGS[1] == defs["HB_L2SQ_SINGLE_CTA"]
+    assert scan.NORM_TWO_PASS == defs["HB_NORM_TWO_PASS"]
+    assert hb.pdlp.SUMMATION == {"ordered": enums["HB_PDLP_SUMS_ORDERED"], "atomic": enums["HB_PDLP_SUMS_ATOMIC"],
+                                 "tree": enums["HB_PDLP_SUMS_TREE"]}
