@@ -4,8 +4,10 @@
 // (src/hello_ot/_native/generic_scan/pricing_small.cu:230-304, pricing.cu,
 // matrix_selection.cuh) with one fused persistent kernel per pass:
 //
-//   TMA (64B-swizzled fp32 slabs, local HBM only, no multicast)
-//     -> tcgen05.mma kind::tf32, 128x256 tile, fp32 accumulator in TMEM
+//   TMA (64B-swizzled slabs of fp16 halves, or of fp32 features in the TF32
+//   mode; local HBM only, no multicast load)
+//     -> tcgen05.mma kind::f16 (kind::tf32), 128x256 tile (256x256 over a CTA
+//        pair with cta_group::2), fp32 accumulator in TMEM
 //        (two accumulators: the MMA of tile t+1 overlaps the epilogue of t)
 //     -> epilogue warps: tcgen05.ld, score, certificate sums, row top-k in
 //        registers and (one-pass mode) column top-k in per-warp HBM lists.
