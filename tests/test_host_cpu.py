@@ -126,3 +126,27 @@ def test_python_flags_match_the_header(hb):
     assert scan.NORM_TWO_PASS == defs["HB_NORM_TWO_PASS"]
     assert hb.pdlp.SUMMATION == {"ordered": enums["HB_PDLP_SUMS_ORDERED"], "atomic": enums["HB_PDLP_SUMS_ATOMIC"],
                                  "tree": enums["HB_PDLP_SUMS_TREE"]}
+
+
+def test_generic_scan_validates_before_launch(hb):
+    """The module-level scan entry points reject bad buckets, kinds and non-CUDA inputs
+    with the reference's ValueError before anything reaches the library."""
+    gs = hb.generic_scan
+    x = torch.zeros((4, 3))
+    v = torch.zeros(4, dtype=torch.float64)
+    with pytest.raises(ValueError, match="power-of-two bucket"):
+        gs.bidirectional(x, x, v, v, 3, 0)
+    with pytest.raises(ValueError, match="CUDA"):
+        gs.bidirectional(x, x, v, v, 4, 0)
+    with pytest.raises(ValueError, match="CUDA"):
+        gs.directional(x, x, v, 4, 0)
+    with pytest.raises(ValueError, match="CUDA"):
+        gs.certificate_only(x, x, v, v, 3, raw_costs=(v, v))
+
+
+def test_leaf_cost_matrix_validates_kind(hb):
+    x = torch.zeros((4, 3))
+    with pytest.raises(ValueError, match="kind"):
+        hb.leaf_cost_matrix(x, x, "cosine")
+    with pytest.raises(ValueError, match="offset"):
+        hb.leaf_cost_matrix(x, x, "l2^2")
