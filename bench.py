@@ -45,8 +45,8 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per pair of the scan kernel from ncu captures
-# (profiles/l2sq_scan_kernel_c5_d256.md), scaled by the pairs of the launch
+# DRAM bytes (read + write) per pair of the scan kernel from an ncu capture of the full
+# config-5 launch, scaled by the pairs of the launch
 DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 1.1672}
 
 
@@ -54,7 +54,7 @@ DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 1.1672}
 # the PDHG; config 3 (n = m = 262144, d = 128) for the l1 scan
 PATH_SIZES = {"scan": (1_048_576, 256), "initial": (1_048_576, 256), "pairs": (1_048_576, 256),
               "pdlp": (1_048_576, 256), "norm": (262_144, 128), "support": (1_048_576, 256),
-              "prune": (1_048_576, 256), "coarsest": (1024, 32)}
+              "prune": (1_048_576, 256), "coarsest": (1024, 32), "solve": (0, 0)}
 
 
 def parse_args():
@@ -64,12 +64,14 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--path", default="scan", choices=["scan", "norm", "pairs", "pdlp", "initial", "support", "prune",
-                                                   "coarsest"],
+                                                   "coarsest", "solve"],
                    help="scan (default, the headline): l2sq pricing scan; norm: l1 scan (config 3 shape); "
                         "pairs: active-support pair costs; pdlp: restricted-OT PDHG iterations; "
                         "initial: l2sq directional top-16 scan (config 5 shape); "
                         "support: active-support candidate filter; prune: budgeted pruning selection; "
-                        "coarsest: dense exact transport of a coarsest level (n = m = 1024, d = 32)")
+                        "coarsest: dense exact transport of a coarsest level (n = m = 1024, d = 32); "
+                        "solve: end-to-end hello_ot.solve through the plug-in (--config)")
+    p.add_argument("--config", default="C2", choices=sorted(SOLVE_CONFIGS), help="configuration of --path solve")
     p.add_argument("--cost", default="l2sq", choices=["l2sq"])
     p.add_argument("--norm-kind", default="l1", choices=["l1", "linf", "l2"], help="cost of --path norm")
     p.add_argument("--n", type=int, default=None, help="points per side (default: the path's config)")
@@ -130,6 +132,39 @@ def make_workload(n, d, seed, device, rows=None):
     f = torch.randn(x.shape[0], device=device, dtype=torch.float64, generator=gs) * med
     gd = torch.randn(n, device=device, dtype=torch.float64, generator=gs) * med
     return x, y, a, b, f, gd, med
+
+
+SOLVE_CONFIGS = {"C1": (2048, 32, "l2^2"), "C2": (32768, 3, "l2"), "C3": (262144, 128, "l1")}
+
+
+def solve_config(name, seed=42, n=None):
+    """Inputs of the baseline's end-to-end configurations, numpy fp32 points and fp64
+    masses (None = uniform): C1 Brenier map (x ~ N(0, I), y = x + 2 tanh(x) row-permuted,
+    the reference's examples/quickstart.py), C2 x ~ U[0,1]^3, y ~ U[0,1]^3 + 0.1 N(0, I),
+    masses U(0.5, 1.5) normalised, C3 independent 16-component Gaussian mixtures
+    (means N(0, 4I), per-component std U(0.5, 1.5), equal weights).  Returns
+    (x, y, source_mass, target_mass, cost)."""
+    n0, d, cost = SOLVE_CONFIGS[name]
+    n = n0 if n is None else int(n)
+    rng = np.random.default_rng(seed)
+    if name == "C1":
+        x = rng.normal(size=(n, d)).astype(np.float32)
+        y = x + 2 * np.tanh(x)
+        return x, y[rng.permutation(n)], None, None, cost
+    if name == "C2":
+        x = rng.uniform(size=(n, d)).astype(np.float32)
+        y = (rng.uniform(size=(n, d)) + 0.1 * rng.normal(size=(n, d))).astype(np.float32)
+        a, b = rng.uniform(0.5, 1.5, n), rng.uniform(0.5, 1.5, n)
+        return x, y, a / a.sum(), b / b.sum(), cost
+
+    def mixture():
+        means = rng.normal(scale=2.0, size=(16, d))
+        stds = rng.uniform(0.5, 1.5, 16)
+        comp = rng.integers(0, 16, n)
+        return (means[comp] + stds[comp, None] * rng.normal(size=(n, d))).astype(np.float32)
+
+    x = mixture()
+    return x, mixture(), None, None, cost
 
 
 # ------------------------------------------------------------------ clocks
@@ -798,6 +833,94 @@ def run_coarsest(args, hb, dev, peaks):
            "n": n, "d": d, "edges": e}, extra)
 
 
+def import_reference(cpp=False):
+    """The unmodified reference package, pip-installed into baseline/_ref; cpp=True also
+    puts its C++ CPU backend (oracle/_ref, built from its sources) on the path and the
+    ot.emd stand-in in place of the absent POT."""
+    for p in (REPO / "baseline" / "_ref", REPO / "oracle" / "_ref"):
+        if str(p) not in sys.path:
+            sys.path.insert(0, str(p))
+    if cpp:
+        from oracle import pot_emd
+        pot_emd.install()
+    import hello_ot
+    return hello_ot
+
+
+def reference_solve(name, threads):
+    """The reference's own end-to-end solve on its C++ CPU backend (backend="cpp")."""
+    hello_ot = import_reference(cpp=True)
+    from hello_ot.progress import final_metrics
+
+    x, y, a, b, cost = solve_config(name)
+    t0 = time.perf_counter()
+    r = hello_ot.solve(x, y, source_mass=a, target_mass=b, cost=cost,
+                       options=hello_ot.SolverOptions(backend="cpp", num_threads=threads, verbose="off",
+                                                      cost_perturbation="off"))
+    return time.perf_counter() - t0, r, final_metrics(r)
+
+
+def run_solve(args, hb, dev, peaks):
+    """End-to-end solve to relative KKT 1e-6: the reference's hello_ot.solve(backend="native")
+    with this library bound by hello_ot_b200.plugin, host arrays in, host plan and duals out
+    (every host-device copy inside the timed region); metric seconds per solve."""
+    from hello_ot_b200 import plugin
+
+    hello_ot = import_reference()
+    from hello_ot.progress import final_metrics
+
+    plugin.install(hello_ot)
+    name = args.config
+    x, y, a, b, cost = solve_config(name)
+    opts = hello_ot.SolverOptions(backend="native", verbose="off", cost_perturbation="off")
+    out = {}
+
+    def step():
+        out["r"] = hello_ot.solve(x, y, source_mass=a, target_mass=b, cost=cost, options=opts)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    plugin.routes(reset=True)
+    launches0 = hb.kernel_launch_count()
+    times = []
+    with ClockSampler(dev.index or 0) as clocks:
+        for _ in range(args.steps):
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            step()
+            torch.cuda.synchronize(dev)
+            times.append(time.perf_counter() - t0)
+    launches = hb.kernel_launch_count() - launches0
+    routes = plugin.routes()
+    sec = sum(times) / len(times)
+    r = out["r"]
+    pfeas, dfeas, gap, kkt = final_metrics(r)
+    n, d = x.shape
+    h2d = x.nbytes + y.nbytes + (0 if a is None else a.nbytes + b.nbytes)
+    d2h = r.solution.values.size * 24 + 8 * (x.shape[0] + y.shape[0])
+    extra = {"higher_is_better": False, "scaling": "none (one GPU)",
+             "dtype": "f16x3/f64" if cost == "l2^2" else "f32/f64", "objective": r.objective,
+             "relative_kkt": kkt, "primal_feasibility": pfeas, "dual_feasibility": dfeas, "gap": gap,
+             "refinement_iterations": r.metadata.get("total_refinement_iterations"),
+             "gpu_launches": int(launches),
+             "routes_per_step": {k: v / args.steps for k, v in sorted(routes.items())},
+             "clocks": clocks.summary(),
+             "e2e": {"value": sec, "unit": "s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                     "api": "hello_ot.solve(backend='native') with hello_ot_b200.plugin (host numpy in and out)"}}
+    if not args.no_cpu and name in ("C1", "C2"):
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        dt, ref, (rp, rd, rg, rk) = reference_solve(name, threads)
+        extra["cpu_baseline"] = {"value": dt, "unit": "s", "cores": threads, "kind": "reference",
+                                 "sample": f"one full {name} solve by the reference, backend='cpp' (its C++ "
+                                           f"CPU backend), objective {ref.objective!r}, relative KKT {rk:.3g}",
+                                 "objective_rel_diff": abs(r.objective - ref.objective) / abs(ref.objective)}
+    _line(args, "end-to-end solve time to rel-KKT 1e-6", sec, "s", sec,
+          {"workload": f"{name}: {cost}, n=m={n}, d={d}, hello_ot.solve native + hello_ot_b200 plug-in, "
+                       "cost_perturbation off", "n": n, "m": int(y.shape[0]), "d": d, "cost": cost}, extra)
+
+
 def run_other(args):
     import __graft_entry__ as entry
 
@@ -806,12 +929,40 @@ def run_other(args):
     torch.cuda.set_device(dev)
     peaks, _ = load_peaks()
     {"pairs": run_pairs, "pdlp": run_pdlp, "norm": run_norm, "initial": run_initial,
-     "support": run_support, "prune": run_prune, "coarsest": run_coarsest}[args.path](args, hb, dev, peaks)
+     "support": run_support, "prune": run_prune, "coarsest": run_coarsest,
+     "solve": run_solve}[args.path](args, hb, dev, peaks)
+
+
+def run_solve_reference(args):
+    """--path solve --impl reference: the reference's own solve on its C++ CPU backend."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt, r, (rp, rd, rg, rk) = reference_solve(args.config, threads)
+        if i >= args.warmup:
+            times.append(dt)
+    sec = sum(times) / len(times)
+    x, y, _, _, cost = solve_config(args.config)
+    print(json.dumps({
+        "impl": "reference", "metric": "end-to-end solve time to rel-KKT 1e-6", "value": sec, "unit": "s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": False, "scaling": "none", "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {cost}, n=m={x.shape[0]}, d={x.shape[1]}, hello_ot.solve "
+                               "backend='cpp'", "n": x.shape[0], "d": x.shape[1], "cost": cost},
+        "objective": r.objective, "relative_kkt": rk,
+        "cpu_baseline": {"value": sec, "unit": "s", "cores": threads, "kind": "reference",
+                         "sample": f"whole {args.config} solves, reference C++ CPU backend"},
+        "e2e": {"value": sec, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
 def main():
     args = parse_args()
-    if args.path != "scan":
+    if args.path == "solve" and args.impl == "reference":
+        run_solve_reference(args)
+    elif args.path != "scan":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference arm is defined for the default "
                                                                   "scan path; other paths report cpu_baseline"}))

@@ -156,6 +156,10 @@ class NativeRestrictedOTPDLP:
             "termination_rel_dual_res": info.rel_dual_residual,
             "termination_objective_vector_norm": info.cost_norm,
             "termination_constraint_bound_norm": info.mass_norm,
+            "algorithm_abs_primal_res_l2": info.abs_primal_residual,
+            "algorithm_rel_primal_res_l2": info.rel_primal_residual,
+            "algorithm_abs_dual_res_l2": info.abs_dual_residual,
+            "algorithm_rel_dual_res_l2": info.rel_dual_residual,
             "relative_primal_dual_gap": info.rel_gap, "primal_weight": info.primal_weight,
             "restart_count": int(info.restarts), "runtime_sec": duration,
             "setup_time_sec": info.setup_seconds, "iteration_time_sec": info.iteration_seconds,

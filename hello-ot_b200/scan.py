@@ -12,7 +12,9 @@ Differences from the reference, all deliberate:
     validated like the reference but the fused kernels plan their own tiles;
   * both clouds stay resident in HBM (a B200 holds a 1.28M x 8192 cloud pair),
     so the scan is one call with no host streaming;
-  * cost perturbation (sigma > 0) is not implemented and raises.
+  * the norm scans take the index-hash / rank-2 cost perturbation (sigma > 0) in
+    the kernels; the ℓ2² perturbation arrives as two appended feature columns,
+    as the reference builds it.
 """
 from __future__ import annotations
 
@@ -177,12 +179,6 @@ def norm_topk(x, y, g, k, cost_type, *, compute_stats=False, perturbation=None):
                                stream_handle(dev), ctypes.byref(perturbation[0]) if perturbation else None)
     check(rc)
     return vals, idx, stats
-
-
-def _no_perturbation(sigma, query_global_index=None, database_global_index=None):
-    if sigma is not None and float(sigma) != 0.0:
-        raise NotImplementedError("hello_ot_b200 does not implement cost perturbation (sigma > 0); "
-                                  "run with cost_perturbation='off'")
 
 
 class ScanExtension:

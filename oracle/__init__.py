@@ -43,13 +43,15 @@ class PdlpInfo(ctypes.Structure):
 
 
 def build(force: bool = False) -> Path:
-    """Compile liboracle.so (and the reference's CPU build when its sources exist)."""
+    """Compile liboracle.so, and the reference's CPU build when the environment variable
+    HELLO_REF names a checkout of the reference project (its sources are not in this
+    repository)."""
     lib = HERE / "liboracle.so"
     if force or not lib.exists() or lib.stat().st_mtime < (HERE / "oracle.c").stat().st_mtime:
         subprocess.run(["make", "-C", str(HERE), f"PYTHON={sys.executable}"], check=True,
                        stdout=subprocess.DEVNULL)
-    ref = Path(os.environ.get("HELLO_REF", "/root/reference"))
-    if (ref / "src/hello_ot/_native/cpp/scan.cpp").exists():
+    ref = Path(os.environ["HELLO_REF"]) if os.environ.get("HELLO_REF") else None
+    if ref is not None and (ref / "src/hello_ot/_native/cpp/scan.cpp").exists():
         subprocess.run(["make", "-C", str(HERE), "ref", f"REF={ref}", f"PYTHON={sys.executable}"],
                        check=True, stdout=subprocess.DEVNULL)
     return lib

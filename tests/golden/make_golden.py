@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the reference implementation.
 
-Run in a checkout that has the reference project (default /root/reference,
-override with HELLO_REF) after ``make -C oracle ref``:
+Run with HELLO_REF naming a checkout of the reference project, after
+``make -C oracle ref REF=$HELLO_REF``:
 
-    python tests/golden/make_golden.py
+    HELLO_REF=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's Python package with its C++ CPU backend
 (``oracle/_ref/hello_ot_cpp``, compiled from the reference sources) and records
@@ -34,7 +34,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("HELLO_REF", "/root/reference"))
+if not os.environ.get("HELLO_REF"):
+    raise SystemExit("set HELLO_REF to a checkout of the reference project")
+REF = Path(os.environ["HELLO_REF"])
 sys.path.insert(0, str(REF / "src"))
 sys.path.insert(0, str(REPO / "oracle" / "_ref"))
 
