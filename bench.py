@@ -78,6 +78,8 @@ def parse_args():
     p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
     p.add_argument("--k", type=int, default=8)
     p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
+    p.add_argument("--exact", type=int, choices=[0, 1], default=0,
+                   help="1: the fp64 re-check of the l2sq lists (HB_L2SQ_EXACT)")
     p.add_argument("--passes", type=int, choices=[1, 2], default=None,
                    help="force a one-pass (k <= 8) or two-pass scan (default: the library's choice)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
@@ -341,7 +343,7 @@ def run_ours(args):
     if world > 1:  # the target cloud is replicated from rank 0 (once per solve)
         dist.broadcast(y, 0)
         dist.broadcast(b, 0)
-    sharded = ShardedPricingScan(precision=args.precision, passes=args.passes)
+    sharded = ShardedPricingScan(precision=args.precision, passes=args.passes, exact=bool(args.exact))
     g_step = g.clone()
 
     def step():
@@ -412,6 +414,8 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "median_pair_cost": med,
         }
+        if args.exact:
+            out["exact_rescans"] = dict(zip(("row_lists", "column_lists"), hb.l2sq_last_rescans()))
     # ---- end to end through the host-facing API (pinned host inputs, candidates back to host)
     if not args.no_e2e:
         xh = x.cpu().pin_memory(); yh = y.cpu().pin_memory()

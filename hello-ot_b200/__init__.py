@@ -10,8 +10,9 @@ Import name: ``hello_ot_b200`` (the folder is ``hello-ot_b200``; see
 """
 from ._lib import (HBError, Workspace, kernel_launch_count, last_kernel_times, lib, load_library,  # noqa: F401
                    set_kernel_timing)
-from .scan import (ScanExtension, LowrankBidirScanResult, flatten_candidates, l2sq_scan, l2sq_topk,  # noqa: F401
-                   norm_scan, norm_topk, raw_lowrank_bidir_feasibility_pricing_scan, scan_routes, topk_bucket)
+from .scan import (ScanExtension, LowrankBidirScanResult, flatten_candidates, l2sq_last_rescans, l2sq_scan,  # noqa: F401
+                   l2sq_topk, norm_scan, norm_topk, raw_lowrank_bidir_feasibility_pricing_scan, scan_routes,
+                   topk_bucket)
 from .pairs import cost_pairs_lowrank, pair_costs, pair_costs_metric  # noqa: F401
 from .pdlp import NativeRestrictedOTPDLP, SolverResult  # noqa: F401
 from .support import filter_new_candidate_pairs, select_prune_positions, support_filter  # noqa: F401

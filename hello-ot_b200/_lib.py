@@ -24,7 +24,7 @@ EXPORTS = ("hb_abi_version", "hb_last_error", "hb_kernel_launch_count", "hb_set_
            "hb_norm_scan", "hb_norm_scan_noalloc", "hb_merge_topk", "hb_pair_costs_workspace", "hb_pair_costs", "hb_restricted_ot_workspace",
            "hb_restricted_ot_solve", "hb_filter_new_pairs_workspace", "hb_filter_new_pairs",
            "hb_prune_select_workspace", "hb_prune_select", "hb_norm_scan_ex", "hb_norm_topk_ex",
-           "hb_pair_costs_ex")
+           "hb_pair_costs_ex", "hb_l2sq_last_rescans")
 
 
 class HBError(RuntimeError):
@@ -88,6 +88,8 @@ def load_library(path: Path | str = LIB_PATH):
     lib.hb_l2sq_scan.restype = c_int
     lib.hb_l2sq_scan.argtypes = [P, P, c_int64, c_int64, c_int64, P, P, P, P, c_int, c_double, c_int, c_int, c_int,
                                  P, P, P, P, P, P, c_size_t, P]
+    lib.hb_l2sq_last_rescans.restype = c_int
+    lib.hb_l2sq_last_rescans.argtypes = [POINTER(c_int64)]
     lib.hb_l2sq_topk_workspace.restype = c_size_t
     lib.hb_l2sq_topk_workspace.argtypes = [c_int64, c_int64, c_int64, c_int, c_int]
     lib.hb_l2sq_topk.restype = c_int

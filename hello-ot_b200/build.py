@@ -5,7 +5,8 @@
 Each CUDA source compiles to an object under hello-ot_b200/_build/ (in
 parallel) and the objects link into hello-ot_b200/libhello_b200.so with the
 CUDA runtime linked statically.  pdlp.cu is compiled without fma contraction
-so the PDHG update arithmetic matches the reference operation by operation.
+so the PDHG update arithmetic matches the reference operation by operation;
+exact.cu likewise, so its fp64 scores round like the written expressions.
 """
 from __future__ import annotations
 
@@ -21,11 +22,11 @@ CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "libhello_b200.so"
 INCLUDE = HERE.parent / "include"
-SOURCES = ["abi.cu", "scan_l2sq.cu", "scan_norm.cu", "pairs.cu", "pdlp.cu", "support.cu"]
+SOURCES = ["abi.cu", "scan_l2sq.cu", "scan_norm.cu", "pairs.cu", "pdlp.cu", "support.cu", "exact.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + str(INCLUDE), "-Xptxas", "-warn-spills"]
-PER_FILE = {"pdlp.cu": ["-fmad=false"]}
+PER_FILE = {"pdlp.cu": ["-fmad=false"], "exact.cu": ["-fmad=false"]}
 
 
 def nvcc() -> str:

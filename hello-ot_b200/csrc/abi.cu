@@ -17,6 +17,7 @@
 
 namespace {
 thread_local std::string g_error;
+thread_local int64_t g_rescans[2] = {0, 0};  // row and column lists the last exact l2sq scan rescanned
 std::atomic<unsigned long long> g_launches{0};
 
 // Per-thread event timing of the kernels of the last call.
@@ -150,7 +151,8 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (!valid_k(k)) return fail(HB_BAD_ARGUMENT, "k must be in 0..32");
     if (dot_scale != 1.0 && dot_scale != 2.0) return fail(HB_BAD_ARGUMENT, "dot_scale must be exactly 1 or 2");
     {
-        const int base = precision & ~(HB_L2SQ_TWO_PASS | HB_L2SQ_ONE_PASS | HB_L2SQ_CTA_PAIRS | HB_L2SQ_SINGLE_CTA);
+        const int base =
+            precision & ~(HB_L2SQ_TWO_PASS | HB_L2SQ_ONE_PASS | HB_L2SQ_CTA_PAIRS | HB_L2SQ_SINGLE_CTA | HB_L2SQ_EXACT);
         if (base != 1 && base != 3)
             return fail(HB_BAD_ARGUMENT, "precision must be 1 (tf32) or 3 (fp32-class split), optionally | a pass flag");
         if ((precision & HB_L2SQ_TWO_PASS) && (precision & HB_L2SQ_ONE_PASS))
@@ -168,9 +170,10 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     std::string err;
     int status_host = 0;
+    int rescans[2] = {0, 0};
     int rc = hb::l2sq_scan(x, y, q, n, d, x_cost, y_cost, x_bias, y_bias, k, dot_scale, compute_stats, precision,
                            min_groups, row_vals, row_idx, col_vals, col_idx, stats5, workspace, workspace_bytes,
-                           &status_host, st, err);
+                           &status_host, st, err, rescans);
     if (rc) return fail(rc == 3 ? HB_WORKSPACE : rc == 5 ? HB_TENSOR_MAP : HB_LAUNCH, err);
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(HB_CUDA, std::string("l2sq scan: ") + cudaGetErrorString(e));
@@ -178,7 +181,16 @@ int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d
     if (status_host & hb::kErrWaitTimeout) return fail(HB_DEVICE_TIMEOUT, "l2sq scan: a device-side wait timed out");
     if (status_host & hb::kErrBadInput)
         return fail(HB_BAD_INPUT, "l2sq scan: a feature magnitude of 2^75 or more (or a non-finite one)");
+    g_rescans[0] = rescans[0];
+    g_rescans[1] = rescans[1];
     g_error.clear();
+    return HB_OK;
+}
+
+int hb_l2sq_last_rescans(int64_t* out2) {
+    if (!out2) return fail(HB_BAD_ARGUMENT, "null output pointer");
+    out2[0] = g_rescans[0];
+    out2[1] = g_rescans[1];
     return HB_OK;
 }
 

@@ -52,6 +52,16 @@ struct TopK {
         if (!placed) { v[0] = a; i[0] = ai; }
     }
     __device__ __forceinline__ void offer(double a, int ai) { if (admits(a, ai)) push(a, ai); }
+    // offer() that also keeps `run`, the largest score ever offered to the list that
+    // is not in it: a rejected score, or the last entry a push evicts.
+    __device__ __forceinline__ void offer_track(double a, int ai, double& run) {
+        if (admits(a, ai)) {
+            if (i[K - 1] != INT32_MAX) run = fmax(run, v[K - 1]);
+            push(a, ai);
+        } else {
+            run = fmax(run, a);
+        }
+    }
 };
 
 // ---------------------------------------------------------------- mbarrier

@@ -27,7 +27,7 @@ size_t l2sq_bytes(int64_t q, int64_t n, int64_t d, int k, int precision, int min
 int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* nx, const double* ny,
               const double* qb, const double* dbb, int k, double dot_scale, int want_stats, int precision,
               int min_groups, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws, size_t ws_bytes,
-              int* status_out, cudaStream_t st, std::string& err);
+              int* status_out, cudaStream_t st, std::string& err, int* rescans_out = nullptr);
 
 // norm scans (scan_norm.cu).  f == nullptr: no query bias (the score is g - c
 // exactly); rows_only: no column lists (cv/ci unused).
@@ -37,11 +37,37 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
               size_t ws_bytes, cudaStream_t st, std::string& err, bool rows_only = false,
               const struct Perturb* pert = nullptr);
 
-// partial top-k merge (scan_l2sq.cu): lists of `width` entries, bucket K >= width
+// fp64 re-check of the ℓ2² lists (exact.cu).  exact_bounds writes the per-row error
+// bounds of both clouds (y_err padded with zeros to n_pad); exact_finish re-scores one
+// side's K-wide approximate lists in fp64, writes the exact top k_out and rescans the
+// lists whose runner-up lies within the bound of the k-th exact score.
+struct ExactSide {
+    const float* qf;       // the lists' own rows (x for row lists, y for column lists)
+    const float* dbf;      // the other cloud
+    int64_t nq, ndb;
+    const double* qbias;   // bias of the lists' own rows
+    const double* dbias;   // bias of the other cloud
+    const double* lv;      // [nq][K] approximate lists and their runner-ups
+    const int* li;
+    const double* run;
+    const float* qerr;     // [nq] error bound of each list's approximate scores
+    double* ov;            // [nq][k_out] exact top-k
+    int* oi;
+    int* flags;            // [nq] scratch: lists to rescan
+    int* nflag;            // [1] scratch
+    bool swap;             // the lists' rows are y: score (dot + dbias) + qbias
+};
+cudaError_t exact_bounds(const float* x, const float* y, int64_t q, int64_t n, int d, int64_t n_pad, int precision,
+                         const int* exps, double dot_scale, float* norms_x, float* norms_y, unsigned* maxes,
+                         float* x_err, float* y_err, int sms, cudaStream_t st);
+cudaError_t exact_finish(int K, const ExactSide& side, int d, double dot_scale, int k_out, int sms, cudaStream_t st);
+
+// partial top-k merge (scan_l2sq.cu): lists of `width` entries, bucket K >= width;
+// pr / run_out: the partial lists' runner-ups in, the merged list's runner-up out (optional)
 cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out,
-                        double* ov, int* oi, cudaStream_t st);
+                        double* ov, int* oi, cudaStream_t st, const double* pr = nullptr, double* run_out = nullptr);
 cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
-                      cudaStream_t st);
+                      cudaStream_t st, const double* pr = nullptr, double* run_out = nullptr);
 
 // pair costs (pairs.cu)
 int pair_costs(int kind, const float* x, const float* y, int64_t nx, int64_t ny, int64_t d, const double* a,

@@ -43,29 +43,37 @@ inline ScanPlan scan_plan(int64_t q, int64_t n, int bm, int bn, int ctas_per_sm,
 // Merge the `parts` partial lists of each row (rows x width per part, parts
 // stored part-major, width <= K) into the first `k_out` entries of the final
 // list.  Slots with index INT32_MAX or negative are empty; empty output slots
-// come out as (-inf, -1).  Thread per row.
+// come out as (-inf, -1).  Thread per row.  With `run_out`, also the row's
+// runner-up: the largest score offered to any of its lists (pr: the partial
+// lists' runner-ups, parts x rows) that is not among the k_out entries.
 template <int K>
 __global__ void merge_partials(const double* __restrict__ pv, const int* __restrict__ pi, int parts, int64_t rows,
-                               int width, int k_out, double* __restrict__ out_v, int* __restrict__ out_i) {
+                               int width, int k_out, double* __restrict__ out_v, int* __restrict__ out_i,
+                               const double* __restrict__ pr, double* __restrict__ run_out) {
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     TopK<K> top;
     top.reset();
+    double run = -INFINITY;
     for (int c = 0; c < parts; ++c) {
         const double* v = pv + ((int64_t)c * rows + r) * width;
         const int* ix = pi + ((int64_t)c * rows + r) * width;
         for (int s = 0; s < width; ++s) {
             const int id = ix[s];
-            if (id != INT32_MAX && id >= 0) top.offer(v[s], id);
+            if (id != INT32_MAX && id >= 0) top.offer_track(v[s], id, run);
         }
+        if (pr) run = fmax(run, pr[(int64_t)c * rows + r]);
     }
 #pragma unroll
     for (int s = 0; s < K; ++s) {
         if (s < k_out) {
             out_v[r * k_out + s] = top.v[s];
             out_i[r * k_out + s] = top.i[s] == INT32_MAX ? -1 : top.i[s];
+        } else if (top.i[s] != INT32_MAX) {
+            run = fmax(run, top.v[s]);
         }
     }
+    if (run_out) run_out[r] = run;
 }
 
 // Sum the per-CTA certificate partials in CTA order (deterministic for a

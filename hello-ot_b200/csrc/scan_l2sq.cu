@@ -71,7 +71,7 @@ constexpr int MAX_EW = 8;
 // columns) when the row list is small enough for the register budget, else 4.
 template <int K>
 struct Epi {
-    static constexpr int EW = K <= 8 ? 8 : 4;
+    static constexpr int EW = K <= 10 ? 8 : 4;
     static constexpr int THREADS = EPI_FIRST + 32 * EW;
 };
 constexpr uint32_t TMEM_COLS = 512;
@@ -105,6 +105,16 @@ struct Params {
     int* ckey;     // [ct * BN] screening threshold of each column (ordered-int fp32 image), see below
     double* cval;  // [row groups * 4][n][K]
     int* cidx;
+    // fp64 re-check (HB_L2SQ_EXACT; null pointers: off).  row_err: bound E of the error of each
+    // query row's approximate scores (over all columns); col_err (one pass): each column's,
+    // padded to whole tiles.  Screens drop a pair only when its approximate score is more
+    // than 2E below the list's k-th, and every list records its runner-up (the largest
+    // approximate score offered to it and not kept): part_run per partial row list,
+    // crun per column list ([row groups * 4][n]).
+    const float* row_err;
+    const float* col_err;
+    double* part_run;
+    double* crun;
 };
 
 // Column vectors of a tile (bias, cost, threshold) are bulk-copied by the
@@ -116,6 +126,7 @@ struct __align__(1024) SmemT {
     double cbias[NCS][BN];                     // the tile's column biases
     double ccost[NCS][BN];                     // the tile's column costs (cost terms)
     int ckey[ONE ? NCS : 1][ONE ? BN : 4];     // the tile's column thresholds (one pass)
+    __align__(16) float cerr[ONE ? NCS : 1][ONE ? BN : 4];  // the tile's column error bounds (one pass, exact)
     // per epilogue warp, its column slice (EW x BN/(EW/4) = 4 BN entries in all), fp32
     // constants read once per pair: x = bias, y = the column's screening threshold (one
     // pass; threshold less the rounding margin), z = column cost (cost terms), w unused
@@ -185,7 +196,7 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE, PAIR>& s) {
     const int rank = PAIR ? (int)cluster_rank() : 0;
     const uint32_t bytes = PAIR ? (p.terms == 3 ? PAIR_STAGE_BYTES : A_BYTES + BH_BYTES)
                                 : (p.terms == 3 ? STAGE_BYTES : A_BYTES + B_BYTES);
-    const uint32_t cbytes = BN * 8 + (p.d_cost ? BN * 8 : 0) + (ONE ? BN * 4 : 0);
+    const uint32_t cbytes = BN * 8 + (p.d_cost ? BN * 8 : 0) + (ONE ? BN * 4 : 0) + (ONE && p.col_err ? BN * 4 : 0);
     const int kw = p.terms == 3 ? BK16 : BK;  // elements per 64-byte slab row
     uint32_t t = 0;
     const Sched sc = schedule<ONE, PAIR>(p);
@@ -201,6 +212,7 @@ __device__ __forceinline__ void producer(const Params& p, Smem<ONE, PAIR>& s) {
             bulk_load_1d(s.cbias[cs], p.d_bias + (size_t)ct * BN, BN * 8, &s.cfull[cs]);
             if (p.d_cost) bulk_load_1d(s.ccost[cs], p.d_cost + (size_t)ct * BN, BN * 8, &s.cfull[cs]);
             if (ONE) bulk_load_1d(s.ckey[cs], p.ckey + (size_t)ct * BN, BN * 4, &s.cfull[cs]);
+            if (ONE && p.col_err) bulk_load_1d(s.cerr[cs], p.col_err + (size_t)ct * BN, BN * 4, &s.cfull[cs]);
             for (int ks = 0; ks < p.kslabs; ++ks) {
                 if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.abort, p.status)) return;
                 uint8_t* a = s.stage[stage];
@@ -414,7 +426,8 @@ __device__ __forceinline__ float order_value(int key) { return __int_as_float(ke
 // scores (dot + qb_row) + dbb_col.  The list is read from and written back to
 // HBM only when the lane has a candidate, and a full list raises the column
 // threshold.
-// A column list (K scores, K indices) in HBM, moved with 16-byte accesses.
+// A column list (K scores, K indices) in HBM, moved with 16-byte accesses where the
+// list size allows (an even size for the scores, a multiple of four for the indices).
 template <int KK>
 __device__ __forceinline__ void load_list(const Params& p, int64_t base, TopK<KK>& ct) {
     if constexpr (KK % 2 == 0) {
@@ -424,7 +437,8 @@ __device__ __forceinline__ void load_list(const Params& p, int64_t base, TopK<KK
             ct.v[t] = w.x; ct.v[t + 1] = w.y;
         }
     } else {
-        ct.v[0] = p.cval[base];
+#pragma unroll
+        for (int t = 0; t < KK; ++t) ct.v[t] = p.cval[base + t];
     }
     if constexpr (KK % 4 == 0) {
 #pragma unroll
@@ -444,7 +458,8 @@ __device__ __forceinline__ void store_list(const Params& p, int64_t base, const 
         for (int t = 0; t < KK; t += 2)
             *reinterpret_cast<double2*>(p.cval + base + t) = make_double2(ct.v[t], ct.v[t + 1]);
     } else {
-        p.cval[base] = ct.v[0];
+#pragma unroll
+        for (int t = 0; t < KK; ++t) p.cval[base + t] = ct.v[t];
     }
     if constexpr (KK % 4 == 0) {
 #pragma unroll
@@ -484,13 +499,15 @@ __device__ __forceinline__ void column_update(const Params& p, S& s, uint32_t cm
         const int64_t base = (list_base + col0 + lane) * KK;
         TopK<KK> ct;
         load_list<KK>(p, base, ct);
+        double run = p.crun ? p.crun[list_base + col0 + lane] : -INFINITY;
         while (mine) {
             const int r = __ffs(mine) - 1;
             mine &= mine - 1;
             const double dot = (double)(scale * T[r * 33 + lane]);
-            ct.offer((dot + RB[r]) + cbias, row0 + r);
+            ct.offer_track((dot + RB[r]) + cbias, row0 + r, run);
         }
         store_list<KK>(p, base, ct);
+        if (p.crun) p.crun[list_base + col0 + lane] = run;
         if (ct.i[KK - 1] != INT32_MAX) atomicMax(p.ckey + col0 + lane, order_key(__double2float_rd(ct.v[KK - 1])));
     }
     __syncwarp();
@@ -537,6 +554,8 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
         const float rmarg_f = 0x1p-20f * fabsf(rbias_f);
         const float rbmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(rbias_f))));
         const float rcost_f = ((SM & kCostStats) && rvalid) ? (float)p.q_cost[row] : 0.0f;
+        const float rband = (p.row_err && rvalid) ? 2.0f * p.row_err[row] : 0.0f;  // 2E: the re-check band
+        double run = -INFINITY;
         top.reset();
         for (int ct = g * p.tpg; ct < ct1; ++ct, ++t) {
             const uint32_t buf = t & 1, aph = (t >> 1) & 1;
@@ -554,6 +573,7 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                 if constexpr ((SM & kCostStats) != 0) cf = ok ? (float)s.ccost[cs][slice * SLICE + c] : 0.0f;
                 if constexpr (ONE) {
                     th = ok ? order_value(s.ckey[cs][slice * SLICE + c]) : INFINITY;
+                    if (p.col_err && ok) th = __fsub_rd(th, 2.0f * s.cerr[cs][slice * SLICE + c]);
                     th = screen_threshold(th, 0x1p-20f * (fabsf(bf) + rbmax));
                 }
                 cbm = max(cbm, __float_as_uint(fabsf(bf)));
@@ -571,7 +591,8 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                 const int cb = ch * 32;
                 const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
                 const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY
-                                  : screen_threshold(__double2float_rd(top.v[KK - 1]), 0x1p-20f * cbmax + rmarg_f);
+                                  : screen_threshold(__fsub_rd(__double2float_rd(top.v[KK - 1]), rband),
+                                                     0x1p-20f * cbmax + rmarg_f);
                 uint32_t mask, cmask;
                 if (__all_sync(0xffffffffu, live == 32))
                     mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcx + cb, wcy + cb, wcz + cb, rbias_f, rcost_f,
@@ -591,7 +612,7 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                     const double dot = (double)(scale * vj);
                     const double cbias = wbias[cb + j];
                     const double sc = SWAP ? ((dot + cbias) + rbias) : ((dot + rbias) + cbias);
-                    top.offer(sc, c0 + cb + j);
+                    top.offer_track(sc, c0 + cb + j, run);
                 }
                 if (colwork)
                     column_update<K>(p, s, cmask, ew, lane, rb * BM + quarter * 32, c0 + cb, wbias[cb + lane],
@@ -609,6 +630,7 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
             int* pi = p.part_i + ((int64_t)part * p.q + row) * KK;
 #pragma unroll
             for (int j = 0; j < KK; ++j) { pv[j] = top.v[j]; pi[j] = top.i[j]; }
+            if (p.part_run) p.part_run[(int64_t)part * p.q + row] = run;
         }
     }
 }
@@ -703,12 +725,13 @@ __global__ void pad_columns(const PadJob job) {
     }
 }
 
-// Empty one-pass column lists: (-inf, no index), thresholds -inf.
-__global__ void init_columns(double* cval, int* cidx, int* ckey, int64_t lists, int64_t n, int K) {
+// Empty one-pass column lists: (-inf, no index), thresholds -inf, runner-ups -inf.
+__global__ void init_columns(double* cval, int* cidx, int* ckey, int64_t lists, int64_t n, int K, double* crun) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t total = lists * K > n ? lists * K : n;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
         if (e < lists * K) { cval[e] = -INFINITY; cidx[e] = INT32_MAX; }
+        if (crun && e < lists) crun[e] = -INFINITY;
         if (e < n) ckey[e] = order_key(-INFINITY);
     }
 }
@@ -867,6 +890,12 @@ cudaError_t launch_k(int K, const l2sq::Params& p, int grid, cudaStream_t st) {
         case 8: return launch_pass<8, SM, SWAP>(p, grid, st);
         case 16: return launch_pass<16, SM, SWAP>(p, grid, st);
         case 32: return launch_pass<32, SM, SWAP>(p, grid, st);
+        // list sizes of the fp64 re-check (bucket + EXACT_EXTRA)
+        case 3: return launch_pass<3, SM, SWAP>(p, grid, st);
+        case 6: return launch_pass<6, SM, SWAP>(p, grid, st);
+        case 10: return launch_pass<10, SM, SWAP>(p, grid, st);
+        case 18: return launch_pass<18, SM, SWAP>(p, grid, st);
+        case 34: return launch_pass<34, SM, SWAP>(p, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -878,6 +907,9 @@ cudaError_t launch_one(int K, const l2sq::Params& p, int grid, cudaStream_t st) 
         case 2: return launch_pass<2, SM, false, true, PAIR>(p, grid, st);
         case 4: return launch_pass<4, SM, false, true, PAIR>(p, grid, st);
         case 8: return launch_pass<8, SM, false, true, PAIR>(p, grid, st);
+        case 3: return launch_pass<3, SM, false, true, PAIR>(p, grid, st);
+        case 6: return launch_pass<6, SM, false, true, PAIR>(p, grid, st);
+        case 10: return launch_pass<10, SM, false, true, PAIR>(p, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -893,32 +925,45 @@ int device_sms() {
 
 template <int K>
 cudaError_t launch_merge(const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out, double* ov,
-                         int* oi, cudaStream_t st) {
-    merge_partials<K><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(pv, pi, parts, rows, width, k_out, ov, oi);
+                         int* oi, cudaStream_t st, const double* pr, double* run_out) {
+    merge_partials<K><<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(pv, pi, parts, rows, width, k_out, ov, oi, pr,
+                                                                       run_out);
     count_launches(1);
     return cudaGetLastError();
 }
 
 cudaError_t merge_any(int K, const double* pv, const int* pi, int parts, int64_t rows, int k_out, double* ov, int* oi,
-                      cudaStream_t st) {
-    return merge_lists(K, pv, pi, parts, rows, K, k_out, ov, oi, st);
+                      cudaStream_t st, const double* pr, double* run_out) {
+    return merge_lists(K, pv, pi, parts, rows, K, k_out, ov, oi, st, pr, run_out);
 }
 
 cudaError_t merge_lists(int K, const double* pv, const int* pi, int parts, int64_t rows, int width, int k_out,
-                        double* ov, int* oi, cudaStream_t st) {
+                        double* ov, int* oi, cudaStream_t st, const double* pr, double* run_out) {
     switch (K) {
-        case 1: return launch_merge<1>(pv, pi, parts, rows, width, k_out, ov, oi, st);
-        case 2: return launch_merge<2>(pv, pi, parts, rows, width, k_out, ov, oi, st);
-        case 4: return launch_merge<4>(pv, pi, parts, rows, width, k_out, ov, oi, st);
-        case 8: return launch_merge<8>(pv, pi, parts, rows, width, k_out, ov, oi, st);
-        case 16: return launch_merge<16>(pv, pi, parts, rows, width, k_out, ov, oi, st);
-        case 32: return launch_merge<32>(pv, pi, parts, rows, width, k_out, ov, oi, st);
+        case 1: return launch_merge<1>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 2: return launch_merge<2>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 4: return launch_merge<4>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 8: return launch_merge<8>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 16: return launch_merge<16>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 32: return launch_merge<32>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        // list sizes of the fp64 re-check (bucket + EXACT_EXTRA)
+        case 3: return launch_merge<3>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 6: return launch_merge<6>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 10: return launch_merge<10>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 18: return launch_merge<18>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
+        case 34: return launch_merge<34>(pv, pi, parts, rows, width, k_out, ov, oi, st, pr, run_out);
         default: return cudaErrorInvalidValue;
     }
 }
 
 // Column slices per tile (= row partial lists per unit) of the bucket-K kernel.
-inline int l2sq_slices(int K) { return (K <= 8 ? 8 : 4) / 4; }
+inline int l2sq_slices(int K) { return (K <= 10 ? 8 : 4) / 4; }
+// The fp64 re-check keeps EXACT_EXTRA more entries than the bucket in every list: the
+// re-scored candidates then include the bucket's next entries, so a list needs a full
+// rescan only when EXACT_EXTRA + 1 approximate scores fall within the error band of the
+// k-th (a near tie of the k-th and the (k+1)-th alone is settled by the re-score).
+constexpr int EXACT_EXTRA = 2;
+inline int list_size(int K, bool exact) { return exact ? K + EXACT_EXTRA : K; }
 
 // One-pass rectangle plan: GR row groups x GC column groups, one CTA each.
 // Few row groups keep the number of column partial lists (4 GR per column)
@@ -986,6 +1031,13 @@ struct L2sqLayout {
     double *ybp = nullptr, *ycp = nullptr, *xbp = nullptr, *xcp = nullptr;  // padded column vectors
     double* cval = nullptr;
     int* cidx = nullptr;
+    // fp64 re-check (HB_L2SQ_EXACT): error bounds, runner-ups, list-size approximate lists, flags
+    bool exact = false;
+    float *xnorm = nullptr, *ynorm = nullptr, *xerr = nullptr, *yerr = nullptr;
+    unsigned* nmax = nullptr;
+    double *prun1 = nullptr, *prun2 = nullptr, *crun = nullptr, *run1 = nullptr, *run2 = nullptr;
+    double *tv1 = nullptr, *tv2 = nullptr;
+    int *ti1 = nullptr, *ti2 = nullptr, *flag1 = nullptr, *flag2 = nullptr, *nflag = nullptr;
     ScanPlan p1{}, p2{};
     OnePlan one{};
     bool one_pass = false;
@@ -1016,11 +1068,27 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
     need(prec == 3, L.yl, (size_t)n * dp16);
     need(prec == 3, L.amax, 2);
     need(prec == 3, L.exps, 2);
-    const int slices = K > 0 ? l2sq_slices(K) : 1;
     const size_t npad = (size_t)(n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     const size_t qpad = (size_t)(q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     L.one_pass = use_one_pass(K, precision, q, d);
     const bool rows_only = (precision & L2SQ_ROWS_ONLY) != 0;
+    L.exact = (precision & HB_L2SQ_EXACT) && K > 0 && !rows_only;
+    const int LK = list_size(K, L.exact);  // entries per list
+    const int slices = K > 0 ? l2sq_slices(LK) : 1;
+    need(L.exact, L.xnorm, (size_t)2 * q);
+    need(L.exact, L.ynorm, (size_t)2 * n);
+    need(L.exact, L.xerr, (size_t)q);
+    need(L.exact, L.yerr, npad > qpad ? npad : qpad);
+    need(L.exact, L.nmax, 4);
+    need(L.exact, L.run1, (size_t)q);
+    need(L.exact, L.run2, (size_t)n);
+    need(L.exact, L.tv1, (size_t)q * LK);
+    need(L.exact, L.ti1, (size_t)q * LK);
+    need(L.exact, L.tv2, (size_t)n * LK);
+    need(L.exact, L.ti2, (size_t)n * LK);
+    need(L.exact, L.flag1, (size_t)q);
+    need(L.exact, L.flag2, (size_t)n);
+    need(L.exact, L.nflag, 2);
     need(true, L.ybp, npad);
     need(!rows_only, L.ycp, npad);
     need(!L.one_pass && !rows_only && K > 0, L.xbp, qpad);
@@ -1029,23 +1097,27 @@ L2sqLayout l2sq_layout(void* base, size_t size, int64_t q, int64_t n, int64_t d,
         const bool pair = use_pairs(precision, d);
         L.one = one_plan(q, n, sms, min_groups, pair, pair ? pair_clusters() : 0);
         const size_t lists = (size_t)L.one.lists_per_col() * n;
-        need(true, L.pv1, (size_t)L.one.gc * slices * q * K);
-        need(true, L.pi1, (size_t)L.one.gc * slices * q * K);
-        need(true, L.cval, lists * K);
-        need(true, L.cidx, lists * K);
+        need(true, L.pv1, (size_t)L.one.gc * slices * q * LK);
+        need(true, L.pi1, (size_t)L.one.gc * slices * q * LK);
+        need(true, L.cval, lists * LK);
+        need(true, L.cidx, lists * LK);
         need(true, L.ckey, npad);
         need(true, L.progress, (size_t)L.one.grid);
         need(true, L.cta, (size_t)L.one.grid * 5);
+        need(L.exact, L.prun1, (size_t)L.one.gc * slices * q);
+        need(L.exact, L.crun, lists);
     } else {
         // features wider than ~1k keep more column groups so the row-block slabs in flight fit in L2
         const int wide = (int)(d / 1024) + 1;
         L.p1 = scan_plan(q, n, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
         L.p2 = scan_plan(n, q, l2sq::BM, l2sq::BN, 1, sms, min_groups > 0 ? min_groups : wide);
-        need(K > 0, L.pv1, (size_t)L.p1.groups * slices * q * K);
-        need(K > 0, L.pi1, (size_t)L.p1.groups * slices * q * K);
-        need(K > 0 && !rows_only, L.pv2, (size_t)L.p2.groups * slices * n * K);
-        need(K > 0 && !rows_only, L.pi2, (size_t)L.p2.groups * slices * n * K);
+        need(K > 0, L.pv1, (size_t)L.p1.groups * slices * q * LK);
+        need(K > 0, L.pi1, (size_t)L.p1.groups * slices * q * LK);
+        need(K > 0 && !rows_only, L.pv2, (size_t)L.p2.groups * slices * n * LK);
+        need(K > 0 && !rows_only, L.pi2, (size_t)L.p2.groups * slices * n * LK);
         need(true, L.cta, (size_t)(L.p1.grid + L.p2.grid) * 5);
+        need(L.exact, L.prun1, (size_t)L.p1.groups * slices * q);
+        need(L.exact, L.prun2, (size_t)L.p2.groups * slices * n);
     }
     need(true, L.status, 1);
     L.bytes = ar.used + 256;
@@ -1059,10 +1131,11 @@ size_t l2sq_bytes(int64_t q, int64_t n, int64_t d, int k, int precision, int min
 int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* nx, const double* ny,
               const double* qb, const double* dbb, int k, double dot_scale, int want_stats, int precision,
               int min_groups, double* rv, int* ri, double* cv, int* ci, double* stats5, void* ws, size_t ws_bytes,
-              int* status_out, cudaStream_t st, std::string& err) {
+              int* status_out, cudaStream_t st, std::string& err, int* rescans_out) {
     L2sqLayout L = l2sq_layout(ws, ws_bytes, q, n, d, k, precision, min_groups);
     if (!L.ok) { err = "workspace too small for the l2sq scan"; return 3; }
     const int K = k > 0 ? bucket_of(k) : 0;
+    const int LK = list_size(K, L.exact);  // entries per list (the kernels' K)
     const int prec = precision & 0xF;
     const bool rows_only = (precision & L2SQ_ROWS_ONLY) != 0;
     if (rows_only) want_stats = 0;
@@ -1089,6 +1162,11 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     }
     const int64_t npad = (n + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
     const int64_t qpad = (q + l2sq::BN - 1) / l2sq::BN * l2sq::BN;
+    if (L.exact) {  // error bounds of both clouds' approximate scores (y's padded to whole tiles)
+        e = exact_bounds(x, y, q, n, (int)d, npad, prec, prec == 3 ? L.exps : nullptr, dot_scale, L.xnorm, L.ynorm,
+                         L.nmax, L.xerr, L.yerr, device_sms(), st);
+        if (e != cudaSuccess) { err = std::string("l2sq exact bounds: ") + cudaGetErrorString(e); return 6; }
+    }
     {
         l2sq::PadJob job{};
         job.src[0] = dbb; job.dst[0] = L.ybp; job.n[0] = n; job.npad[0] = npad;
@@ -1120,34 +1198,58 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     p.q = (int)q; p.n = (int)n;
     p.q_cost = nx; p.d_cost = L.ycp; p.q_bias = qb; p.d_bias = L.ybp;
     p.part_v = L.pv1; p.part_i = L.pi1;
+    if (L.exact) { p.row_err = L.xerr; p.part_run = L.prun1; }
+    // the exact lists of one side: list-size approximate lists with runner-ups re-scored in fp64
+    auto finish_side = [&](bool cols) -> cudaError_t {
+        ExactSide sd{};
+        sd.qf = cols ? y : x; sd.dbf = cols ? x : y;
+        sd.nq = cols ? n : q; sd.ndb = cols ? q : n;
+        sd.qbias = cols ? dbb : qb; sd.dbias = cols ? qb : dbb;
+        sd.lv = cols ? L.tv2 : L.tv1; sd.li = cols ? L.ti2 : L.ti1; sd.run = cols ? L.run2 : L.run1;
+        sd.qerr = cols ? L.yerr : L.xerr;
+        sd.ov = cols ? cv : rv; sd.oi = cols ? ci : ri;
+        sd.flags = cols ? L.flag2 : L.flag1; sd.nflag = L.nflag + (cols ? 1 : 0);
+        sd.swap = cols;
+        return exact_finish(LK, sd, (int)d, dot_scale, k, device_sms(), st);
+    };
     if (L.one_pass) {
         // one pass: row lists in registers, column lists per (row group, lane quarter) in HBM
         const OnePlan& o = L.one;
         const int64_t lists = (int64_t)o.lists_per_col() * n;
-        l2sq::init_columns<<<prep_blocks, 256, 0, st>>>(L.cval, L.cidx, L.ckey, lists, npad, K);
+        l2sq::init_columns<<<prep_blocks, 256, 0, st>>>(L.cval, L.cidx, L.ckey, lists, npad, LK, L.crun);
         count_launches(1);
         p.groups = o.gc; p.tpg = o.tpg; p.ct = o.ct; p.units = o.rb * o.gc;
         p.rb = o.rb; p.rbg = o.rbg;
         p.ckey = L.ckey; p.cval = L.cval; p.cidx = L.cidx;
         p.progress = L.progress;
+        if (L.exact) { p.col_err = L.yerr; p.crun = L.crun; }
         e = cudaMemsetAsync(L.progress, 0, sizeof(int) * o.grid, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 4; }
         if (!want_stats) p.d_cost = nullptr;  // the cost vector is staged only for the cost terms
         if (o.pair)
-            e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats, true>(K, p, o.grid, st)
-                           : launch_one<0, true>(K, p, o.grid, st);
+            e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats, true>(LK, p, o.grid, st)
+                           : launch_one<0, true>(LK, p, o.grid, st);
         else
-            e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats>(K, p, o.grid, st)
-                           : launch_one<0>(K, p, o.grid, st);
+            e = want_stats ? launch_one<l2sq::kScoreStats | l2sq::kCostStats>(LK, p, o.grid, st)
+                           : launch_one<0>(LK, p, o.grid, st);
         if (e != cudaSuccess) { err = std::string("l2sq scan: ") + cudaGetErrorString(e); return 6; }
-        e = merge_any(K, L.pv1, L.pi1, o.gc * l2sq_slices(K), q, k, rv, ri, st);
-        if (e == cudaSuccess) e = merge_any(K, L.cval, L.cidx, o.lists_per_col(), n, k, cv, ci, st);
+        if (L.exact) {
+            e = merge_any(LK, L.pv1, L.pi1, o.gc * l2sq_slices(LK), q, LK, L.tv1, L.ti1, st, L.prun1, L.run1);
+            if (e == cudaSuccess)
+                e = merge_any(LK, L.cval, L.cidx, o.lists_per_col(), n, LK, L.tv2, L.ti2, st, L.crun, L.run2);
+            if (e == cudaSuccess) e = finish_side(false);
+            if (e == cudaSuccess) e = finish_side(true);
+        } else {
+            e = merge_any(K, L.pv1, L.pi1, o.gc * l2sq_slices(K), q, k, rv, ri, st);
+            if (e == cudaSuccess) e = merge_any(K, L.cval, L.cidx, o.lists_per_col(), n, k, cv, ci, st);
+        }
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
         if (want_stats) {
             finalize_stats<<<1, 32, 0, st>>>(L.cta, o.grid, stats5);
             count_launches(1);
         }
         if (status_out) cudaMemcpyAsync(status_out, L.status, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (rescans_out && L.exact) cudaMemcpyAsync(rescans_out, L.nflag, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
         return 0;
     }
     // pass 1: x rows are the queries (row top-k + certificate)
@@ -1156,10 +1258,12 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     // certificate: score terms in the row pass, cost terms in the column pass
     // (a certificate-only call has no column pass and takes all terms here)
     if (K == 0) e = launch_pass<0, l2sq::kScoreStats | l2sq::kCostStats, false>(p, L.p1.grid, st);
-    else e = want_stats ? launch_k<l2sq::kScoreStats, false>(K, p, L.p1.grid, st) : launch_k<0, false>(K, p, L.p1.grid, st);
+    else e = want_stats ? launch_k<l2sq::kScoreStats, false>(LK, p, L.p1.grid, st)
+                        : launch_k<0, false>(LK, p, L.p1.grid, st);
     if (e != cudaSuccess) { err = std::string("l2sq pass 1: ") + cudaGetErrorString(e); return 6; }
     if (K > 0) {
-        e = merge_any(K, L.pv1, L.pi1, L.p1.groups * l2sq_slices(K), q, k, rv, ri, st);
+        e = L.exact ? merge_any(LK, L.pv1, L.pi1, L.p1.groups * l2sq_slices(LK), q, LK, L.tv1, L.ti1, st, L.prun1, L.run1)
+                    : merge_any(K, L.pv1, L.pi1, L.p1.groups * l2sq_slices(K), q, k, rv, ri, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
     }
     if (K > 0 && !rows_only) {
@@ -1181,17 +1285,25 @@ int l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
         p2.groups = L.p2.groups; p2.tpg = L.p2.tpg; p2.ct = L.p2.ct; p2.units = L.p2.units;
         p2.q_cost = ny; p2.d_cost = want_stats ? L.xcp : nullptr; p2.q_bias = dbb; p2.d_bias = L.xbp;
         p2.part_v = L.pv2; p2.part_i = L.pi2;
+        if (L.exact) { p2.row_err = L.yerr; p2.part_run = L.prun2; }
         p2.cta_stats = L.cta + (size_t)L.p1.grid * 5;
-        e = want_stats ? launch_k<l2sq::kCostStats, true>(K, p2, L.p2.grid, st) : launch_k<0, true>(K, p2, L.p2.grid, st);
+        e = want_stats ? launch_k<l2sq::kCostStats, true>(LK, p2, L.p2.grid, st) : launch_k<0, true>(LK, p2, L.p2.grid, st);
         if (e != cudaSuccess) { err = std::string("l2sq pass 2: ") + cudaGetErrorString(e); return 6; }
-        e = merge_any(K, L.pv2, L.pi2, L.p2.groups * l2sq_slices(K), n, k, cv, ci, st);
+        e = L.exact ? merge_any(LK, L.pv2, L.pi2, L.p2.groups * l2sq_slices(LK), n, LK, L.tv2, L.ti2, st, L.prun2, L.run2)
+                    : merge_any(K, L.pv2, L.pi2, L.p2.groups * l2sq_slices(K), n, k, cv, ci, st);
         if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        if (L.exact) {
+            e = finish_side(false);
+            if (e == cudaSuccess) e = finish_side(true);
+            if (e != cudaSuccess) { err = cudaGetErrorString(e); return 6; }
+        }
     }
     if (want_stats) {  // per-CTA partials of both passes, unused terms are zero
         finalize_stats<<<1, 32, 0, st>>>(L.cta, L.p1.grid + (K > 0 ? L.p2.grid : 0), stats5);
         count_launches(1);
     }
     if (status_out) cudaMemcpyAsync(status_out, L.status, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (rescans_out && L.exact) cudaMemcpyAsync(rescans_out, L.nflag, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
     return 0;
 }
 

@@ -15,7 +15,6 @@
 // handed through shared memory to a row-per-thread epilogue (two threads per
 // row, one per half of the columns) that keeps the row top-k in registers.
 #include <algorithm>
-#include <mutex>
 #include <string>
 
 #include "../../include/hello_b200.h"
@@ -515,28 +514,18 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
 // certificate partials) lives in this file-scope device array instead of a
 // caller-provided workspace; every GPU that loads the library holds it until
 // the process exits.  In host code `g_norm_scratch` is only a host-side stand-in
-// for the symbol, so its device address is looked up once per device (with that
-// device current) and passed to the kernels.
+// for the symbol, so every call looks up its device address on the current
+// device and passes that to the kernels.  The address is not cached: after a
+// cudaDeviceReset the module is loaded again and the array may move.
 static __device__ __align__(256) unsigned char g_norm_scratch[HB_NORM_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-std::mutex g_norm_scratch_mutex;
-void* g_norm_scratch_ptr[256] = {};
-
-// Device address of g_norm_scratch on the current device (looked up on first use).
+// Device address of g_norm_scratch on the current device.
 cudaError_t norm_scratch_address(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_norm_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 256) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(g_norm_scratch_mutex);
-    if (!g_norm_scratch_ptr[dev]) {
-        void* ptr = nullptr;
-        e = cudaGetSymbolAddress(&ptr, g_norm_scratch);
-        if (e != cudaSuccess) return e;
-        g_norm_scratch_ptr[dev] = ptr;
-    }
-    *out = g_norm_scratch_ptr[dev];
+    *out = ptr;
     return cudaSuccess;
 }
 }  // namespace

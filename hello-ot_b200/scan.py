@@ -76,21 +76,25 @@ L2SQ_PASS_FLAGS = {None: 0, 2: 0x10, 1: 0x20}
 L2SQ_CTA_FLAGS = {None: 0, 2: 0x100, 1: 0x200}  # HB_L2SQ_CTA_PAIRS, HB_L2SQ_SINGLE_CTA
 
 
+L2SQ_EXACT = 0x400  # HB_L2SQ_EXACT
+
+
 def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute_stats=True, precision="fp32",
-              min_groups=0, passes=None, ctas=None):
+              min_groups=0, passes=None, ctas=None, exact=False):
     """Bidirectional ℓ2² scan on the tensor cores.
 
     passes: 1 (k <= 8 only), 2, or None to let the library choose; both give the
     same lists bit for bit.  ctas (one-pass kernel): 2 runs it as CTA pairs sharing
-    each column tile, 1 as single CTAs, None the library's choice.  Returns (row_vals q x k fp64, row_idx q x k int32,
-    col_vals n x k, col_idx n x k, stats [sum s+^2, sum c^2, max s+, max |c|, count]
-    fp64 on the device)."""
+    each column tile, 1 as single CTAs, None the library's choice.  exact: the fp64
+    re-check (HB_L2SQ_EXACT): lists are the exact fp64 top-k, values exact fp64 scores.
+    Returns (row_vals q x k fp64, row_idx q x k int32, col_vals n x k, col_idx n x k,
+    stats [sum s+^2, sum c^2, max s+, max |c|, count] fp64 on the device)."""
     x, y = _c(x), _c(y)
     x_cost, y_cost, x_bias, y_bias = map(_c, (x_cost, y_cost, x_bias, y_bias))
     q, d = x.shape
     n = y.shape[0]
     prec = PRECISION[precision] if isinstance(precision, str) else int(precision)
-    prec |= L2SQ_PASS_FLAGS[passes] | L2SQ_CTA_FLAGS[ctas]
+    prec |= L2SQ_PASS_FLAGS[passes] | L2SQ_CTA_FLAGS[ctas] | (L2SQ_EXACT if exact and int(k) > 0 else 0)
     L = lib()
     dev = x.device
     kk = int(k)
@@ -107,6 +111,14 @@ def l2sq_scan(x, y, x_cost, y_cost, x_bias, y_bias, k, *, dot_scale=2.0, compute
                             ptr(cv), ptr(ci), ptr(stats), ptr(ws), ws.numel(), stream_handle(dev))
     check(rc)
     return rv[:, :kk], ri[:, :kk], cv[:, :kk], ci[:, :kk], stats
+
+
+def l2sq_last_rescans() -> tuple:
+    """(row lists, column lists) the calling thread's last exact l2sq scan recomputed in
+    fp64 against every column because a near tie fell within the error bound."""
+    out = (ctypes.c_int64 * 2)()
+    check(lib().hb_l2sq_last_rescans(out))
+    return int(out[0]), int(out[1])
 
 
 NORM_KIND = {"l1": 0, "linf": 1, "l2": 2, 0: 0, 1: 1, 2: 2}

@@ -80,7 +80,8 @@ class ShardedPricingScan:
     """
 
     def __init__(self, group=None, *, local_scan: Optional[Callable] = None, merge: Optional[Callable] = None,
-                 dot_scale: float = 2.0, precision: str = "fp32", passes: Optional[int] = None):
+                 dot_scale: float = 2.0, precision: str = "fp32", passes: Optional[int] = None,
+                 exact: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -89,7 +90,7 @@ class ShardedPricingScan:
 
             def local_scan(x, y, a, b, qb, dbb, k):
                 return l2sq_scan(x, y, a, b, qb, dbb, k, dot_scale=dot_scale, precision=precision,
-                                 passes=passes)
+                                 passes=passes, exact=exact)
         self.local_scan = local_scan
         self.merge = merge or merge_topk
 

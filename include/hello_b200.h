@@ -80,18 +80,30 @@ int hb_last_kernel_times(double* ms, int capacity);
  * The one-pass kernel runs either one CTA per rectangle of the pair space or
  * CTA pairs (clusters of two sharing each column tile through a cta_group::2
  * MMA); OR HB_L2SQ_CTA_PAIRS or HB_L2SQ_SINGLE_CTA to force either (same lists).
+ * OR HB_L2SQ_EXACT for the fp64 re-check: the lists are then the exact top-k of
+ * score = (dot_scale <x_i, y_j> + x_bias_i) + y_bias_j with the dot in fp64 from the
+ * fp32 features (values reported in that arithmetic): each list's candidates are
+ * re-scored in fp64, and a list whose runner-up lies within a rigorous bound of the
+ * approximate dot's error of its k-th exact score is recomputed in fp64 against every
+ * column (index sets equal the exact fp64 top-k wherever the k-th/(k+1)-th gap exceeds
+ * the fp64 rounding of the scores).  The certificate sums stay fp32-class.
  * min_groups: column groups (0 = automatic).
  * ------------------------------------------------------------------------- */
 #define HB_L2SQ_TWO_PASS 0x10
 #define HB_L2SQ_ONE_PASS 0x20
 #define HB_L2SQ_CTA_PAIRS 0x100
 #define HB_L2SQ_SINGLE_CTA 0x200
+#define HB_L2SQ_EXACT 0x400
 size_t hb_l2sq_scan_workspace(int64_t q, int64_t n, int64_t d, int k, int precision, int min_groups);
 int hb_l2sq_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, const double* x_cost,
                  const double* y_cost, const double* x_bias, const double* y_bias, int k, double dot_scale,
                  int compute_stats, int precision, int min_groups, double* row_vals, int32_t* row_idx,
                  double* col_vals, int32_t* col_idx, double* stats5, void* workspace, size_t workspace_bytes,
                  void* stream);
+/* Lists the calling thread's last HB_L2SQ_EXACT scan recomputed against every column
+ * (out2[0]: row lists, out2[1]: column lists; zeros after a scan without the flag).
+ * Instrumentation of the fp64 re-check; no counterpart in the reference. */
+int hb_l2sq_last_rescans(int64_t* out2);
 
 /* ---------------------------------------------------------------------------
  * Cost perturbation of the norm costs (the _ex entry points below).
@@ -194,9 +206,11 @@ int hb_norm_scan_ex(const float* x, const float* y, int64_t q, int64_t n, int64_
  * loads the library holds until the process exits.  Problems whose scratch
  * (hb_norm_scan_workspace(q, n, k)) exceeds that size are rejected with
  * HB_WORKSPACE and a message; use hb_norm_scan for them.  It calls no
- * cudaMalloc/cudaFree or other allocating routine.  The first call on a device
- * looks up the array's device address and should come before any stream
- * capture.  All calls on a device share the one array, so calls that overlap
+ * cudaMalloc/cudaFree or other allocating routine.  Every call looks up the
+ * array's device address on the current device (nothing is cached, so a device
+ * reset is harmless); the first call on a device also loads the library's
+ * module there and should come before any stream capture.  All calls on a
+ * device share the one array, so calls that overlap
  * on the GPU (other streams, other host threads) race; serialise them.
  * Arguments and results as hb_norm_scan; the stream is synchronised.
  * ------------------------------------------------------------------------- */

@@ -45,10 +45,13 @@ def _exact_rows(x, y, a, b, f, g, idx):
 
 
 def _bound_rows(x, y, idx, cols):
-    """3-term fp16 split + fp32-accumulation bound s (2^-19 + 2 (d+2) u) sum |x y| per pair."""
+    """3-term fp16 split + fp32-accumulation bound s (2^-19 + 2 (d+2) u) sum |x y| per pair,
+    plus the fp16-subnormal floor s 2^-38 (max|x| sum|y_k| + max|y| sum|x_k|)."""
     ax = x[idx].abs().double()
     sabs = torch.stack([(ax[i] * y[cols[i]].abs().double()).sum(-1) for i in range(len(idx))])
-    return 2.0 * (2.0 ** -19 + 2 * (D + 2) * U32) * sabs + 1e-9
+    mx, my = float(x.abs().max()), float(y.abs().max())
+    floor = torch.stack([mx * y[cols[i]].abs().double().sum(-1) + my * ax[i].sum() for i in range(len(idx))])
+    return 2.0 * ((2.0 ** -19 + 2 * (D + 2) * U32) * sabs + 2.0 ** -38 * floor) + 1e-9
 
 
 def test_l2sq_full_size_properties(hb, c5):

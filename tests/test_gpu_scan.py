@@ -39,13 +39,19 @@ def _bound(x, y, r, c, scale, biases, precision):
     """Per-pair error bound of the tensor-core score.
     fp32 mode (3-term split on fp16 halves of the power-of-two scaled clouds): the
     dropped lo*lo term and the rounding of lo, within 3 2^-22 |x||y| per product,
-    plus fp32 accumulation (d+2)u (any order).  TF32: 2^-9 per product."""
+    plus fp32 accumulation (d+2)u (any order), plus the fp16-subnormal floor of
+    elements far below their cloud's largest: lo keeps an absolute 2^-25 of the
+    scaled value, 2^-39 max|x| per element of x in real units, doubled
+    (tests/test_split_model.py restates the split).  TF32: 2^-9 per product."""
     x64, y64 = np.asarray(x, np.float64), np.asarray(y, np.float64)
     d = x64.shape[1]
     absdot = np.einsum("ij,ij->i", np.abs(x64[r]), np.abs(y64[c]))
     prod = 2.0 ** -9 if precision == "tf32" else 2.0 ** -19
     mag = sum(np.abs(v) for v in biases) + scale * absdot
-    return scale * (prod + 2 * (d + 2) * U32) * absdot + 16 * 2.0 ** -53 * mag
+    floor = 0.0
+    if precision != "tf32":
+        floor = 2.0 ** -38 * (np.abs(x64).max() * np.abs(y64[c]).sum(1) + np.abs(y64).max() * np.abs(x64[r]).sum(1))
+    return scale * ((prod + 2 * (d + 2) * U32) * absdot + floor) + 16 * 2.0 ** -53 * mag
 
 
 def _cert_bounds(x, y, r, c, scale, a, b, qb, dbb, precision):
