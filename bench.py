@@ -78,8 +78,8 @@ def parse_args():
     p.add_argument("--d", type=int, default=None, help="feature dimension (default: the path's config)")
     p.add_argument("--k", type=int, default=8)
     p.add_argument("--precision", default="fp32", choices=["fp32", "tf32"])
-    p.add_argument("--exact", type=int, choices=[0, 1], default=0,
-                   help="1: the fp64 re-check of the l2sq lists (HB_L2SQ_EXACT)")
+    p.add_argument("--exact", type=int, choices=[0, 1], default=1,
+                   help="1 (default): the fp64 re-check of the l2sq lists (HB_L2SQ_EXACT); 0: fp32-class lists")
     p.add_argument("--passes", type=int, choices=[1, 2], default=None,
                    help="force a one-pass (k <= 8) or two-pass scan (default: the library's choice)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
@@ -315,6 +315,7 @@ def workload_config(args):
     return {"workload": f"C5 isolated pricing scan, l2sq, m=n={args.n}, d={args.d}, k={args.k}",
             "n": args.n, "m": args.n, "d": args.d, "topk": args.k, "cost": "l2sq", "dot_scale": 2.0,
             "precision": {"fp32": "3-term fp16 split (fp32-class dot)", "tf32": "1xTF32"}[args.precision],
+            "lists": "exact fp64 top-k (fp64 re-check)" if args.exact else "fp32-class top-k",
             "scan_mode": scan_mode(args),
             "parallelism": f"source-row shards x{args.gpus}",
             "l2_policy": "inputs (2 GB clouds) larger than L2; no flush"}
@@ -431,7 +432,8 @@ def run_ours(args):
             t0 = time.perf_counter()
             if world == 1:
                 r = hb.raw_lowrank_bidir_feasibility_pricing_scan(xh, yh, ah, bh, fh, gh, topk=k, dot_scale=2.0,
-                                                                  compute_precision=args.precision)
+                                                                  compute_precision=args.precision,
+                                                                  exact=bool(args.exact))
                 h2d = sum(v.numel() * v.element_size() for v in (xh, yh, ah, bh, fh, gh))
                 d2h = (r.rows.size + r.cols.size) * 8 + 5 * 8
             else:

@@ -201,10 +201,13 @@ class ScanExtension:
     supports_fp64_accumulation = True
     index_hash_arithmetic = None
 
-    def __init__(self, *, precision: str = "fp32"):
+    def __init__(self, *, precision: str = "fp32", exact: bool = True):
+        """precision: "fp32" (3-term fp16 split) or "tf32"; exact: the fp64 re-check of
+        the ℓ2² lists (HB_L2SQ_EXACT), so the lists are the exact fp64 top-k."""
         self.routes = Counter()
         self.last_backend = "hello_b200"
         self.precision = precision
+        self.exact = bool(exact)
 
     def _record(self, name):
         key = name + ":hello_b200"
@@ -225,7 +228,8 @@ class ScanExtension:
             raise ValueError("invalid raw pricing tile, scale or column mode")
         self._record("raw_pricing")
         rv, ri, cv, ci, s = l2sq_scan(x, y, nx, ny, qb, dbb, k, dot_scale=dot_scale,
-                                      compute_stats=bool(compute_stats), precision=self.precision)
+                                      compute_stats=bool(compute_stats), precision=self.precision,
+                                      exact=self.exact)
         stats = torch.stack((s[0], s[1], s[4], s[3] if collect_linf_stats else s[3].new_zeros(())))
         if not compute_stats:
             stats.zero_()
@@ -357,12 +361,14 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
                                                target_dual, *, topk, theta=0.0, gpu_id=0, memory_floor_mib=768.0,
                                                resident_multiplier=1.10, col_reduce_tile=256, col_kernel="auto",
                                                collect_timing=False, collect_linf_diagnostics=False, dot_scale=1.0,
-                                               compute_precision="fp32", return_device=False):
+                                               compute_precision="fp32", return_device=False, exact=True):
     """Full bidirectional ℓ2² pricing scan + dual-feasibility certificate with the
     signature of bilinear_topk.raw_lowrank_bidir_feasibility_pricing_scan.
 
     Score of pair (i, j): (s<x_i,y_j> + (f_i - a_i)) + (g_j - b_j); candidates are the
-    top-k of every source row and every target column with score > theta."""
+    top-k of every source row and every target column with score > theta.  exact (the
+    default): the lists are the exact fp64 top-k (the fp64 re-check, HB_L2SQ_EXACT);
+    exact=False keeps the fp32-class ranking of the tensor-core dot."""
     k = int(round(float(topk)))
     if abs(float(topk) - k) > 1e-9:
         raise ValueError("fused inner-product scan requires an integer pricing_topk")
@@ -390,7 +396,7 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
     f = _to_device(source_dual, device, torch.float64).view(-1)
     g = _to_device(target_dual, device, torch.float64).view(-1)
     rv, ri, cv, ci, stats = l2sq_scan(x, y, a, b, f - a, g - b, k, dot_scale=float(dot_scale),
-                                      precision=str(compute_precision))
+                                      precision=str(compute_precision), exact=bool(exact))
     rows_t, cols_t = flatten_candidates(rv, ri, cv, ci, theta)
     s = stats.cpu().tolist()
     num_sq, den_sq, max_pos, cost_linf, count = s[0], s[1], s[2], s[3], int(round(s[4]))
@@ -419,7 +425,10 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
         "pairwise_passes": 2,
         "scan_traversal": "fused_tensor_core_bidirectional",
         "cost_compute_precision": str(compute_precision),
+        "fp64_recheck": bool(exact),
     }
+    if exact:
+        diagnostics["fp64_rescanned_lists"] = sum(l2sq_last_rescans())
     if collect_linf_diagnostics:
         diagnostics.update({"dual_feasibility_cost_linf": float(cost_linf),
                             "relative_linf_dual_feasibility": float(max_violation) / (1.0 + float(cost_linf))})

@@ -81,7 +81,7 @@ class ShardedPricingScan:
 
     def __init__(self, group=None, *, local_scan: Optional[Callable] = None, merge: Optional[Callable] = None,
                  dot_scale: float = 2.0, precision: str = "fp32", passes: Optional[int] = None,
-                 exact: bool = False):
+                 exact: bool = True):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
