@@ -366,8 +366,8 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
             if (K > 0) {
                 mask |= ((ok0 && sf.x >= thr) ? (1u << j) : 0u) | ((ok1 && sf.y >= thr) ? (2u << j) : 0u);
                 if (ONE) {
-                    const float2 cyy = *reinterpret_cast<const float2*>(cy + j);  // negated thresholds
-                    cm |= ((ok0 && sf.x >= -cyy.x) ? (1u << j) : 0u) | ((ok1 && sf.y >= -cyy.y) ? (2u << j) : 0u);
+                    const float2 cyy = *reinterpret_cast<const float2*>(cy + j);
+                    cm |= ((ok0 && sf.x >= cyy.x) ? (1u << j) : 0u) | ((ok1 && sf.y >= cyy.y) ? (2u << j) : 0u);
                 }
             }
         }
@@ -391,86 +391,6 @@ __device__ __forceinline__ uint32_t chunk_phase1(const float (&v)[32], float sca
     if (SM & kCostStats) {
         acc[1] += ((double)den4[0] + (double)den4[1]) + ((double)den4[2] + (double)den4[3]);
         acc[3] = fmax(acc[3], (double)mcost);
-    }
-    cmask = cm;
-    return mask;
-}
-
-// Phase 1 of a full chunk (all 32 columns valid for the whole warp), fast form: the same
-// fp32 scores, certificate partials and candidate tests as chunk_phase1, but the row and
-// column screens only keep a running maximum per thread -- rmax = max_j sf_j and
-// cslack = max_j (sf_j - threshold_j) -- instead of building the masks pair by pair.  The
-// masks (chunk_masks) are built afterwards only when rmax reaches the row threshold or
-// cslack reaches zero, which after the first tiles is rare.  sf - th >= 0 exactly when
-// sf >= th (a rounded difference of two floats keeps its sign; +-inf thresholds give
-// +-inf), so the masks are the ones chunk_phase1 builds.  mpos comes from rmax.
-template <int K, int SM, bool SWAP, bool ONE>
-__device__ __forceinline__ void chunk_screen_full(const float (&v)[32], float scale, const float* cx, const float* cyn,
-                                                  const float* cz, float rbias_f, float rcost_f, float& rmax,
-                                                  float& cslack, double (&acc)[5]) {
-    uint64_t num2[2] = {0, 0}, den2[2] = {0, 0};
-    float mcost = 0.0f, rm = -INFINITY, cs = -INFINITY;
-    int cnt = 0;
-    const uint64_t sc2 = pk2(scale, scale), nsc2 = pk2(-scale, -scale);
-    const uint64_t rb2 = pk2(rbias_f, rbias_f), rc2 = pk2(rcost_f, rcost_f);
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-        const uint64_t v2 = pk2(v[j], v[j + 1]);
-        if (K > 0 || (SM & kScoreStats)) {
-            const uint64_t cx2 = *reinterpret_cast<const uint64_t*>(cx + j);  // broadcast
-            const uint64_t sf2 = SWAP ? add_x2(fma_x2(sc2, v2, cx2), rb2) : add_x2(fma_x2(sc2, v2, rb2), cx2);
-            const float2 sf = upk2(sf2);
-            rm = fmaxf(rm, fmaxf(sf.x, sf.y));
-            if (SM & kScoreStats) {
-                const bool pos0 = sf.x > 0.0f, pos1 = sf.y > 0.0f;
-                num2[(j >> 1) & 1] = fma_x2(sf2, pk2(pos0 ? sf.x : 0.0f, pos1 ? sf.y : 0.0f), num2[(j >> 1) & 1]);
-                cnt += (pos0 ? 1 : 0) + (pos1 ? 1 : 0);
-            }
-            if (ONE && K > 0) {
-                const float2 d = upk2(add_x2(sf2, *reinterpret_cast<const uint64_t*>(cyn + j)));
-                cs = fmaxf(cs, fmaxf(d.x, d.y));
-            }
-        }
-        if (SM & kCostStats) {
-            const uint64_t cz2 = *reinterpret_cast<const uint64_t*>(cz + j);
-            const uint64_t cf2 = fma_x2(nsc2, v2, add_x2(rc2, cz2));
-            const float2 cf = upk2(cf2);
-            den2[(j >> 1) & 1] = fma_x2(cf2, cf2, den2[(j >> 1) & 1]);
-            mcost = fmaxf(mcost, fmaxf(fabsf(cf.x), fabsf(cf.y)));
-        }
-    }
-    const float2 n01 = upk2(num2[0]), n23 = upk2(num2[1]), d01 = upk2(den2[0]), d23 = upk2(den2[1]);
-    if (SM & kScoreStats) {
-        acc[0] += ((double)n01.x + (double)n01.y) + ((double)n23.x + (double)n23.y);
-        acc[2] = fmax(acc[2], (double)rm);
-        acc[4] += (double)cnt;
-    }
-    if (SM & kCostStats) {
-        acc[1] += ((double)d01.x + (double)d01.y) + ((double)d23.x + (double)d23.y);
-        acc[3] = fmax(acc[3], (double)mcost);
-    }
-    rmax = rm;
-    cslack = cs;
-}
-
-// The candidate masks of a full chunk (rare path after chunk_screen_full): bit j of the row
-// mask when sf_j >= thr, of the column mask when sf_j >= th_j; the scores are recomputed with
-// the same instructions, so they are the screen's.
-template <bool SWAP, bool ONE>
-__device__ __forceinline__ uint32_t chunk_masks(const float (&v)[32], float scale, const float* cx, const float* cyn,
-                                                float rbias_f, float thr, bool rows, bool cols, uint32_t& cmask) {
-    uint32_t mask = 0, cm = 0;
-    const uint64_t sc2 = pk2(scale, scale), rb2 = pk2(rbias_f, rbias_f);
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-        const uint64_t v2 = pk2(v[j], v[j + 1]);
-        const uint64_t cx2 = *reinterpret_cast<const uint64_t*>(cx + j);
-        const float2 sf = upk2(SWAP ? add_x2(fma_x2(sc2, v2, cx2), rb2) : add_x2(fma_x2(sc2, v2, rb2), cx2));
-        if (rows) mask |= (sf.x >= thr ? (1u << j) : 0u) | (sf.y >= thr ? (2u << j) : 0u);
-        if (ONE && cols) {
-            const float2 cyy = *reinterpret_cast<const float2*>(cyn + j);
-            cm |= (sf.x >= -cyy.x ? (1u << j) : 0u) | (sf.y >= -cyy.y ? (2u << j) : 0u);
-        }
     }
     cmask = cm;
     return mask;
@@ -657,32 +577,27 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                     th = screen_threshold(th, 0x1p-20f * (fabsf(bf) + rbmax));
                 }
                 cbm = max(cbm, __float_as_uint(fabsf(bf)));
-                wcx[c] = bf; wcy[c] = -th; wcz[c] = cf;  // thresholds stored negated (screen: sf + (-th) >= 0)
+                wcx[c] = bf; wcy[c] = th; wcz[c] = cf;
             }
             const float cbmax = __uint_as_float(__reduce_max_sync(0xffffffffu, cbm));
             __syncwarp();
             if (!mbar_wait(&s.tfull[buf], aph, &s.abort, p.status)) return;
             tc_fence_after();
             const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + buf * BN + slice * SLICE;
-            // The chunks' TMEM reads are double-buffered: chunk c + 1 is read while chunk c is
-            // processed (tcgen05.wait::ld waits for all of a thread's reads, so each read is
-            // waited for only after the other buffer's chunk has been processed).
-            auto chunk = [&](float (&v)[32], const int ch) {
+            for (int ch = 0; ch < SLICE / 32 && ch * 32 < ncols; ++ch) {
+                float v[32];
+                tmem_ld32(taddr + ch * 32, v);
+                tmem_wait_ld(v);
                 const int cb = ch * 32;
                 const int live = rvalid ? min(32, ncols - cb) : 0;  // valid columns of this chunk
                 const float thr = top.i[KK - 1] == INT32_MAX ? -INFINITY
                                   : screen_threshold(__fsub_rd(__double2float_rd(top.v[KK - 1]), rband),
                                                      0x1p-20f * cbmax + rmarg_f);
-                uint32_t mask, cmask = 0u;
-                if (__all_sync(0xffffffffu, live == 32)) {
-                    float rmax, cslack;
-                    chunk_screen_full<K, SM, SWAP, ONE>(v, scale, wcx + cb, wcy + cb, wcz + cb, rbias_f, rcost_f, rmax,
-                                                        cslack, acc);
-                    const bool rows = K > 0 && rmax >= thr, cols = ONE && K > 0 && cslack >= 0.0f;
-                    mask = (rows || cols) ? chunk_masks<SWAP, ONE>(v, scale, wcx + cb, wcy + cb, rbias_f, thr, rows,
-                                                                  cols, cmask)
-                                          : 0u;
-                } else
+                uint32_t mask, cmask;
+                if (__all_sync(0xffffffffu, live == 32))
+                    mask = chunk_phase1<K, SM, SWAP, true, ONE>(v, scale, wcx + cb, wcy + cb, wcz + cb, rbias_f, rcost_f,
+                                                                live, thr, cmask, acc);
+                else
                     mask = chunk_phase1<K, SM, SWAP, false, ONE>(v, scale, wcx + cb, wcy + cb, wcz + cb, rbias_f, rcost_f,
                                                                  live, thr, cmask, acc);
                 const bool colwork = ONE && K > 0 && __any_sync(0xffffffffu, cmask != 0u);
@@ -702,23 +617,6 @@ __device__ __forceinline__ void epilogue(const Params& p, Smem<ONE, PAIR>& s, ui
                 if (colwork)
                     column_update<K>(p, s, cmask, ew, lane, rb * BM + quarter * 32, c0 + cb, wbias[cb + lane],
                                      list_base, scale);
-            };
-            const int nch = min(SLICE / 32, (ncols + 31) / 32);  // ncols may be <= 0
-            float va[32], vb[32];
-            if (nch > 0) {
-                tmem_ld32(taddr, va);
-                tmem_wait_ld(va);
-            }
-            for (int ch = 0; ch < nch; ch += 2) {
-                const bool has1 = ch + 1 < nch, has2 = ch + 2 < nch;
-                if (has1) tmem_ld32(taddr + (ch + 1) * 32, vb);
-                chunk(va, ch);
-                if (has1) {
-                    tmem_wait_ld(vb);
-                    if (has2) tmem_ld32(taddr + (ch + 2) * 32, va);
-                    chunk(vb, ch + 1);
-                    if (has2) tmem_wait_ld(va);
-                }
             }
             tc_fence_before();
             if (PAIR && rank != 0) mbar_arrive_remote(tempty_peer + buf * (uint32_t)sizeof(uint64_t));
