@@ -245,39 +245,19 @@ def reference_cpu_scan(x, y, a, b, f, g, k, scale, threads):
     return rows.numel(), stats
 
 
-def cpu_reference_rate(x, y, a, b, f, g, k, scale, target_s, threads):
-    """Gpairs/s of the reference CPU scan on a row sample sized for ~target_s seconds."""
-    x, y, a, b, f, g = (t.detach().cpu() for t in (x, y, a, b, f, g))
-    probe = min(64, x.shape[0])
-    t0 = time.perf_counter()
-    reference_cpu_scan(x[:probe], y, a[:probe], b, f[:probe], g, k, scale, threads)
-    dt = time.perf_counter() - t0
-    rows = int(min(x.shape[0], max(probe, probe * target_s / max(dt, 1e-3))))
-    rows = max(probe, (rows // 64) * 64)
-    t0 = time.perf_counter()
-    reference_cpu_scan(x[:rows], y, a[:rows], b, f[:rows], g, k, scale, threads)
-    dt = time.perf_counter() - t0
-    return rows * y.shape[0] / dt / 1e9, rows, dt
-
-
-# ------------------------------------------------------------------ main arms
-def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+def reference_scan_sample(args, steps, warmup):
+    """Seconds per step of the reference's CPU scan over a bounded row sample of the
+    configured workload (same seed and distribution as the device clouds, generated on
+    the host), sized so one step takes about cpu_seconds / 2.  Both the reference arm
+    and the repo arm's cpu_baseline leg time the scan through this function, the repo
+    arm before any GPU work, so the two figures measure the same thing."""
     import oracle
 
-    try:
-        oracle.load_ref("scan")
-    except Exception as exc:  # the reference's CPU build is missing
-        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU backend not built: {exc}"}))
-        return
+    oracle.load_ref("scan")  # raises when the reference's CPU build is missing
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     n, d, k = args.n, args.d, args.k
-    # same distribution, generated on the CPU (the reference arm uses no GPU)
-    x, y, a, b, f, g, med = make_workload(n, d, 42, torch.device("cpu"), rows=(0, 16384))
-    # one step ~ cpu_seconds / 2 of reference work
+    x, y, a, b, f, g, _ = make_workload(n, d, 42, torch.device("cpu"), rows=(0, 16384))
     probe = 64
     t0 = time.perf_counter()
     reference_cpu_scan(x[:probe], y, a[:probe], b, f[:probe], g, k, 2.0, threads)
@@ -285,14 +265,29 @@ def run_reference(args):
     rows = int(min(x.shape[0], max(probe, probe * (args.cpu_seconds / 2) / max(dt, 1e-3))))
     rows = max(probe, rows // 64 * 64)
     times = []
-    for i in range(args.warmup + args.steps):
+    for i in range(warmup + steps):
         t0 = time.perf_counter()
         reference_cpu_scan(x[:rows], y, a[:rows], b, f[:rows], g, k, 2.0, threads)
-        if i >= args.warmup:
+        if i >= warmup:
             times.append(time.perf_counter() - t0)
     sec = sum(times) / len(times)
+    sample = (f"{rows} source rows x {n} targets per step (d={d}, k={k}), reference dot_tile (scan.cpp) + "
+              f"torch.mm tiles, {warmup} warm-up + {steps} timed step(s)")
+    return sec, rows, threads, sample
+
+
+# ------------------------------------------------------------------ main arms
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    try:
+        sec, rows, threads, sample = reference_scan_sample(args, args.steps, args.warmup)
+    except Exception as exc:  # the reference's CPU build is missing
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU backend not built: {exc}"}))
+        return
+    n = args.n
     value = rows * n / sec / 1e9
-    sample = f"{rows} source rows x {n} targets per step (d={d}, k={k}), reference dot_tile + torch.mm"
     print(json.dumps({
         "impl": "reference", "metric": "pricing-scan Gpairs/s (m·n)", "value": value, "unit": "Gpairs/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
@@ -332,6 +327,15 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu:  # before any GPU work, as the reference arm runs
+        try:
+            csec, crows, cthreads, csample = reference_scan_sample(args, 1, 1)
+            cpu_baseline = {"value": crows * args.n / csec / 1e9, "unit": "Gpairs/s", "cores": cthreads,
+                            "kind": "reference", "sample": csample}
+        except Exception as exc:  # reference CPU build missing
+            cpu_baseline = {"value": None, "unit": "Gpairs/s", "cores": 0, "kind": "reference",
+                            "sample": f"unavailable: {exc}"}
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     import torch.distributed as dist
@@ -459,19 +463,8 @@ def run_ours(args):
                           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                           "api": "raw_lowrank_bidir_feasibility_pricing_scan (host arrays)" if world == 1
                           else "ShardedPricingScan.scan from pinned host blocks"}
-    # ---- CPU baseline: the reference's CPU scan on a bounded row sample (rank 0, N=1)
-    if rank == 0 and world == 1 and not args.no_cpu:
-        try:
-            threads = os.cpu_count() or 1
-            torch.set_num_threads(threads)
-            rate, rows, dt = cpu_reference_rate(x[:65536], y, a[:65536], b, f[:65536], g, k, 2.0,
-                                                args.cpu_seconds, threads)
-            out["cpu_baseline"] = {"value": rate, "unit": "Gpairs/s", "cores": threads, "kind": "reference",
-                                   "sample": f"{rows} source rows x {n} targets (d={d}, k={k}) in {dt:.1f} s; "
-                                             "reference dot_tile (scan.cpp) + torch.mm tiles"}
-        except Exception as exc:  # reference CPU build missing
-            out["cpu_baseline"] = {"value": None, "unit": "Gpairs/s", "cores": 0, "kind": "reference",
-                                   "sample": f"unavailable: {exc}"}
+    if rank == 0 and cpu_baseline is not None:
+        out["cpu_baseline"] = cpu_baseline
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

@@ -8,13 +8,17 @@
 //
 // Layout in HBM: edges sorted by (source row, original index), so a source
 // row's edges are contiguous; a target's incident edges are kept as a list of
-// positions in that order, sorted by original edge index.  Per iteration three
-// kernels run: the edge pass (primal update, reflection, Halpern averaging,
-// thread per edge), the source pass (source dual update, thread per row) and
-// the target pass (target dual update, thread per target).  Each node's incident sum is
-// accumulated sequentially in the reference's edge order and this file is
-// compiled without fma contraction, so with the same step sizes one block of
-// iterations reproduces the reference arithmetic bit for bit.
+// positions in that order, sorted by original edge index, and (for the fused
+// passes) the per-edge state is kept a second time in that target order.  Per
+// iteration one fused launch runs on sparse supports: a warp per 32 nodes of either
+// side applies the per-edge update (primal step, reflection, Halpern averaging) to
+// its nodes' contiguous edges in its own copy of the state, sums each node's
+// reflected primal and updates the node's dual; both copies see the same
+// operations, so they stay equal.  Dense sides (a coarsest level's complete
+// support) and atomic node sums use an edge pass plus node passes instead.  Each
+// node's incident sum is accumulated sequentially in the reference's edge order
+// and this file is compiled without fma contraction, so with the same step sizes
+// one block of iterations reproduces the reference arithmetic bit for bit.
 //
 // Control (evaluation every `frequency` iterations, adaptive restarts, PID
 // primal weight, termination) runs on the host exactly as solver.cpp:157-312;
@@ -43,6 +47,8 @@ constexpr int STEP_CAP = 8192;
 struct Step {
     double primal_step, dual_step, halpern;
     int checkpoint, major;
+    int parity;  // fused passes: the node-scale buffer the iteration reads (it writes the other)
+    int pad;
 };
 
 struct Dev {
@@ -58,6 +64,11 @@ struct Dev {
     double *mass, *scale, *bs, *ns, *ay, *y, *py, *dy, *td;
     double* sd;     // [n] source dual / node scale, the value every edge of the row uses
     double *ssum, *tsum;  // [n], [m] node sums of the reflected primal (atomic mode; zero between passes)
+    // fused passes: the edge state also in target order (by target, then original index) and
+    // the node scales double-buffered (sdb[b] / tdb[b]; buffer 0 is sd / td)
+    double *tx, *tax, *tcs;
+    int *t_row, *t_col;
+    double *sdb[2], *tdb[2];
     double* red;    // [RED_BLOCKS][8]
     Step* steps;    // [frequency] the current block's per-iteration parameters
     double* scal;   // [16] reduced scalars
@@ -171,7 +182,8 @@ __global__ void init_state(Dev D, const double* masses, const double* y0, const 
 // ------------------------------------------------------------------ iteration
 
 
-// One PDHG iteration runs as three kernels (solver.cpp:255-281):
+// One PDHG iteration runs as three kernels (solver.cpp:255-281) when the node sums are
+// accumulated with atomics or a side is dense (otherwise the fused passes below, one launch):
 //  edge_pass   : thread per edge, primal update, reflection, Halpern averaging
 //                (coalesced over the source-sorted edges, perfectly balanced);
 //  source_pass : warp per 32 source rows (coalesced staging), ordered sum of
@@ -363,6 +375,118 @@ __global__ void __launch_bounds__(256) node_pass_wide(Dev D, int it, int src_blo
     if (lane == 0) dual_update(D, D.steps[it], target ? D.n + v : v, sum);
 }
 
+// Fused passes (the default for sparse supports): one launch per iteration.  The edge state
+// is kept twice, in source order (x, ax, cs) and in target order (tx, tax, tcs); a warp takes
+// 32 consecutive nodes of one side, applies the per-edge update (primal step, reflection,
+// Halpern averaging: the same operations as edge_pass, so both copies stay equal bit for bit)
+// to the nodes' contiguous edge range in coalesced chunks staged through shared memory, adds
+// each node's reflected primal in edge order (the reference's order) and updates the node's
+// dual.  The edge updates read the node scales of buffer `parity` and the dual updates write
+// the other buffer, so the source and target sides run side by side in one launch.  The
+// source side also writes px / dx, which the evaluation and restart kernels read.
+template <bool TGT>
+__device__ __forceinline__ void fused_side(const Dev& D, const Step& s, int v0, double* stage) {
+    const int lane = threadIdx.x & 31, nodes = TGT ? D.m : D.n, v = v0 + lane;
+    const int* off = TGT ? D.t_off : D.s_off;
+    const int w0 = off[v0], w1 = off[min(v0 + 32, nodes)];
+    const int b0 = v < nodes ? off[v] : w1, b1 = v < nodes ? off[v + 1] : w1;
+    // the warp's own nodes' scales, one per lane; each edge takes its node's by a shuffle
+    const double own = v < nodes ? (TGT ? D.tdb : D.sdb)[s.parity][v] : 0.0;
+    const double* other = TGT ? D.sdb[s.parity] : D.tdb[s.parity];
+    double* X = TGT ? D.tx : D.x;
+    const double* AX = TGT ? D.tax : D.ax;
+    const double* CS = TGT ? D.tcs : D.cs;
+    const int* O = TGT ? D.t_row : D.e_col;  // the other endpoint of each edge
+    double sum = 0.0;
+    constexpr int PER = 4;  // edges per lane loaded together (two batches per 256-edge chunk)
+    for (int c0 = w0; c0 < w1; c0 += SEG_CHUNK) {
+        const int c1 = min(w1, c0 + SEG_CHUNK);
+        // each batch issues all of the lane's loads first (the other side's node scales are
+        // gathered from L2), so they are in flight together; then the updates and the stores
+#pragma unroll
+        for (int h = 0; h < SEG_CHUNK / (32 * PER); ++h) {
+            int oo[PER];
+            double xv[PER], av[PER], cv[PER], at[PER];
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int q = c0 + (h * PER + u) * 32 + lane;
+                if (q < c1) {
+                    oo[u] = __ldg(O + q);
+                    xv[u] = X[q]; av[u] = __ldg(AX + q); cv[u] = __ldg(CS + q);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int q = c0 + (h * PER + u) * 32 + lane;
+                // the lane owning edge q: the last lane whose segment starts at or before q
+                int l = 0;
+#pragma unroll
+                for (int stp = 16; stp > 0; stp >>= 1) {
+                    const int cand = l + stp;
+                    const int bc = __shfl_sync(0xffffffffu, b0, cand & 31);
+                    if (cand < 32 && bc <= q) l = cand;
+                }
+                const double mine = __shfl_sync(0xffffffffu, own, l);
+                if (q < c1) {
+                    const double o = __ldg(other + oo[u]);
+                    at[u] = TGT ? o + mine : mine + o;  // sd[row] + td[col], the edge pass's order
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int q = c0 + (h * PER + u) * 32 + lane;
+                if (q >= c1) continue;
+                const double pxv = max0(xv[u] - s.primal_step * (cv[u] - at[u]));
+                const double r = 2.0 * pxv - xv[u];
+                if (!TGT) {
+                    if (s.checkpoint) D.dx[q] = r - xv[u];
+                    if (s.major) D.px[q] = pxv;
+                }
+                X[q] = s.halpern * r + (1.0 - s.halpern) * av[u];
+                stage[q - c0] = r;
+            }
+        }
+        __syncwarp();
+        const int lo = max(b0, c0), hi = min(b1, c1);
+        for (int q = lo; q < hi; ++q) sum += stage[q - c0];
+        __syncwarp();
+    }
+    if (v >= nodes) return;
+    const int i = TGT ? D.n + v : v;
+    const double yv = D.y[i];
+    const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
+    const double refl = 2.0 * pyv - yv;
+    if (s.checkpoint) D.dy[i] = refl - yv;
+    const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
+    D.y[i] = ynew;
+    if (s.major) D.py[i] = pyv;
+    (TGT ? D.tdb : D.sdb)[s.parity ^ 1][v] = ynew / D.ns[i];
+}
+
+// Blocks [0, src_blocks) take 8 x 32 sources each, the rest 8 x 32 targets each.
+__global__ void __launch_bounds__(256, 4) fused_pass(Dev D, int it, int src_blocks) {
+    __shared__ double stage[8][SEG_CHUNK];
+    const Step s = D.steps[it];
+    const int warp = threadIdx.x >> 5;
+    const bool target = (int)blockIdx.x >= src_blocks;  // block-uniform
+    const int v0 = (((int)blockIdx.x - (target ? src_blocks : 0)) * 8 + warp) * 32;
+    if (v0 >= (target ? D.m : D.n)) return;  // warp-uniform
+    if (target) fused_side<true>(D, s, v0, stage[warp]);
+    else fused_side<false>(D, s, v0, stage[warp]);
+}
+
+// The target-order copy of the edge state: structure (once), cost and primal (at the
+// start and after every restart, from the source-order state).
+__global__ void target_copy(Dev D, int structure) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < D.e; q += stride) {
+        const int p = D.t_pos[q];
+        if (structure) { D.t_row[q] = D.e_row[p]; D.t_col[q] = D.e_col[p]; D.tcs[q] = D.cs[p]; }
+        D.tx[q] = D.x[p];
+        D.tax[q] = D.ax[p];
+    }
+}
+
 // ------------------------------------------------------------------ reductions
 template <int CNT>
 __device__ __forceinline__ void block_store(double (&v)[CNT], double* red) {
@@ -429,18 +553,23 @@ __global__ void __launch_bounds__(RED_THREADS) restart_dist_kernel(Dev D) {
     block_store<2>(v, D.red);
 }
 
-// Restart to the last PDHG iterate (solver.cpp:238-242).
-__global__ void restart_kernel(Dev D) {
+// Restart to the last PDHG iterate (solver.cpp:238-242); the node scales go to buffer
+// `parity` (the one the next iteration reads), the target-order copy follows (fused passes).
+__global__ void restart_kernel(Dev D, int parity, int fused) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += stride) {
         const double v = D.px[p];
         D.ax[p] = v; D.x[p] = v;
+        if (fused) {
+            const double t = D.px[D.t_pos[p]];
+            D.tax[p] = t; D.tx[p] = t;
+        }
     }
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < D.nodes; i += stride) {
         const double v = D.py[i];
         D.ay[i] = v; D.y[i] = v;
-        if (i >= D.n) D.td[i - D.n] = v / D.ns[i];
-        else D.sd[i] = v / D.ns[i];
+        if (i >= D.n) D.tdb[parity][i - D.n] = v / D.ns[i];
+        else D.sdb[parity][i] = v / D.ns[i];
     }
 }
 
@@ -494,6 +623,9 @@ PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e)
     take_d(D.dx, e);
     take_d(D.mass, nodes); take_d(D.scale, nodes); take_d(D.bs, nodes); take_d(D.ns, nodes); take_d(D.ay, nodes);
     take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m); take_d(D.sd, n); take_d(D.ssum, n); take_d(D.tsum, m);
+    take_d(D.tx, e); take_d(D.tax, e); take_d(D.tcs, e); take_i(D.t_row, e); take_i(D.t_col, e);
+    D.sdb[0] = D.sd; D.tdb[0] = D.td;
+    take_d(D.sdb[1], n); take_d(D.tdb[1], m);
     take_d(D.red, (size_t)pdlp::RED_BLOCKS * 8); take_d(D.scal, 16);
     D.steps = ar.take<pdlp::Step>((size_t)pdlp::STEP_CAP);
     if (base && !D.steps) L.ok = false;
@@ -608,10 +740,20 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     int tlen = 0;
     const int F = ctl.frequency;
     const bool wide_sources = e >= (int64_t)pdlp::WIDE_DEGREE * n, wide_targets = e >= (int64_t)pdlp::WIDE_DEGREE * m;
-    const int per_iter = (!ctl.atomic && wide_sources && wide_targets) ? 2 : 3;  // kernels per iteration
+    // fused passes (one launch per iteration) unless node sums are atomic or a side is dense
+    const bool fused = !ctl.atomic && !wide_sources && !wide_targets;
+    const int per_iter = fused ? 1 : (!ctl.atomic && wide_sources && wide_targets) ? 2 : 3;  // kernels per iteration
+    const int fsb = (int)((n + 255) / 256), ftb = (int)((m + 255) / 256);  // fused pass: source / target blocks
+    int parity = 0;  // fused passes: the node-scale buffer the next iteration reads
+    if (fused) {
+        pdlp::target_copy<<<gb, 256, 0, st>>>(D, 1);
+        HB_LAUNCHED(1);
+    }
     // One iteration: the three kernels reading D.steps[it].
     auto launch_iteration = [&](cudaStream_t s_, int it, bool counted) {
-        if (ctl.atomic) {
+        if (fused) {
+            pdlp::fused_pass<<<(unsigned)(fsb + ftb), 256, 0, s_>>>(D, it, fsb);
+        } else if (ctl.atomic) {
             pdlp::edge_pass<true><<<gb, 256, 0, s_>>>(D, it);
             pdlp::source_pass<true><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);
             pdlp::target_pass<true><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
@@ -716,7 +858,7 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             inner = 0;
             last_trial = inf;
             ++restarts;
-            pdlp::restart_kernel<<<gb, 256, 0, st>>>(D);
+            pdlp::restart_kernel<<<gb, 256, 0, st>>>(D, parity, fused ? 1 : 0);
             HB_LAUNCHED(1);
         }
         const double primal_step = 0.998 / weight, dual_step = 0.998 * weight;
@@ -728,6 +870,8 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             s.halpern = double(inner + t + 1) / double(inner + t + 2);
             s.major = ((count + t + 1) % F) == 0;
             s.checkpoint = s.major || (t == 0 && restart);
+            s.parity = fused ? ((parity + t) & 1) : 0;
+            s.pad = 0;
             return s;
         };
         if (first_block) timing_mark(st);
@@ -752,6 +896,7 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         }
         count += F;
         inner += F;
+        if (fused) parity ^= (F & 1);
         if (first_block) timing_mark(st);
         if (cudaGetLastError() != cudaSuccess) return fail("iteration");
     }
