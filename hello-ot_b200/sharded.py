@@ -6,10 +6,15 @@ the target cloud (y, b, g; y is broadcast once per solve, g per scan).  Each
 rank runs the fused bidirectional scan on its block; the exchange steps are
 
   * certificate: all-reduce of (sum s+^2, sum c^2, count) and (max s+, max |c|);
-  * column top-k: all-gather of the per-rank column lists (n x k scores + global
-    source indices) and a merge with the scan's order and tie rule;
-  * candidates: all-gather of the row-side candidate pairs to assemble the
-    reference's candidate order (source rows ascending, then target columns).
+  * column top-k: every rank owns a contiguous block of target columns; an
+    all-to-all sends each rank's lists for a block (n/N x k scores + global source
+    indices) to the block's owner, which merges them with the scan's order and tie
+    rule, and an all-gather of the merged blocks gives every rank the merged n x k
+    lists (each rank sends and receives about 2 (N-1)/N of one rank's lists, where
+    an all-gather of the unmerged lists would move N-1 times them);
+  * candidates: the row-side candidate pairs go to rank 0 alone (an all-to-all with
+    every other destination empty), which assembles the reference's candidate order
+    (source rows ascending, then target columns).
 
 All collectives go through torch.distributed (NCCL over NVLink on the GPU box,
 gloo in the CPU tests); kernel inputs are always local HBM.
@@ -56,6 +61,14 @@ class ShardedScanResult:
     col_idx: torch.Tensor
     row_vals: torch.Tensor         # this rank's rows (local block)
     row_idx: torch.Tensor
+
+
+def _all_to_all(t: torch.Tensor, send: list, recv: list, group) -> torch.Tensor:
+    """Rows [sum(send[:j]), sum(send[:j+1])) of t to rank j; the rows received from rank j
+    land at [sum(recv[:j]), ...) of the result."""
+    out = torch.empty((sum(recv), *t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_to_all_single(out, t.contiguous(), recv, send, group=group)
+    return out
 
 
 def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
@@ -106,11 +119,25 @@ class ShardedPricingScan:
             dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
             dist.all_reduce(maxs, op=dist.ReduceOp.MAX, group=group)
         total = torch.stack((sums[0], sums[1], maxs[0], maxs[1], sums[2]))
-        # column lists
+        # column lists: merged by the owner of each column block, then gathered
         if world > 1:
-            gv = _all_gather(cv.contiguous(), world, group)
-            gi = _all_gather(ci.to(torch.int32).contiguous(), world, group)
-            cv_m, ci_m = self.merge(gv, gi, k)
+            n = cv.shape[0]
+            blocks = [row_partition(n, world, r) for r in range(world)]
+            sizes = [hi - lo for lo, hi in blocks]
+            mine = sizes[self.rank]
+            kk = cv.shape[1]
+            pv = _all_to_all(cv, sizes, [mine] * world, group).view(world, mine, kk)
+            pi = _all_to_all(ci.to(torch.int32), sizes, [mine] * world, group).view(world, mine, kk)
+            mv, mi = self.merge(pv, pi, k)
+            width = max(sizes)  # blocks differ by one row at most: pad to the widest
+            bv = torch.full((width, k), float("-inf"), dtype=torch.float64, device=cv.device)
+            bi = torch.full((width, k), -1, dtype=torch.int32, device=cv.device)
+            bv[:mine] = mv
+            bi[:mine] = mi.to(torch.int32)
+            gv = _all_gather(bv, world, group)
+            gi = _all_gather(bi, world, group)
+            cv_m = torch.cat([gv[r, :sizes[r]] for r in range(world)])
+            ci_m = torch.cat([gi[r, :sizes[r]] for r in range(world)])
         else:
             cv_m, ci_m = cv, ci
         rows = cols = None
@@ -119,14 +146,12 @@ class ShardedPricingScan:
             local_rows = torch.nonzero(rmask, as_tuple=False)[:, 0] + int(row_offset)
             local_cols = ri[rmask].to(torch.int64)
             pairs = torch.stack((local_rows.to(torch.int64), local_cols))
-            if world > 1:
+            if world > 1:  # to rank 0 alone, in rank (= source row) order
                 count = torch.tensor([pairs.shape[1]], dtype=torch.int64, device=pairs.device)
-                counts = _all_gather(count, world, group).view(-1)
-                width = int(counts.max().item())
-                padded = torch.full((2, width), -1, dtype=torch.int64, device=pairs.device)
-                padded[:, :pairs.shape[1]] = pairs
-                allp = _all_gather(padded, world, group)
-                pairs = torch.cat([allp[r, :, :int(counts[r])] for r in range(world)], dim=1)
+                counts = [int(c) for c in _all_gather(count, world, group).view(-1).tolist()]
+                send = [pairs.shape[1] if r == 0 else 0 for r in range(world)]
+                recv = counts if self.rank == 0 else [0] * world
+                pairs = _all_to_all(pairs.t(), send, recv, group).t()
             if self.rank == 0:
                 cmask = (cv_m > float(theta)) & (ci_m >= 0)
                 d_local = torch.nonzero(cmask, as_tuple=False)[:, 0]

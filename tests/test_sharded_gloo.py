@@ -1,9 +1,11 @@
-"""Multi-rank exchange logic of the row-sharded scan, on CPU with gloo (world size 2).
+"""Multi-rank exchange logic of the row-sharded scan, on CPU with gloo (world sizes 2 and 3).
 
 The per-rank scan is the oracle (the GPU kernel's stand-in on CPU) and the
 column merge a numpy restatement; the test checks the partition, the
-certificate all-reduce, the column-list all-gather + merge and the candidate
-gather against a single-process oracle scan of the whole problem.
+certificate all-reduce, the column-list exchange (all-to-all by column block,
+merge by the block's owner, all-gather of the merged blocks; every rank's copy)
+and the candidate gather to rank 0 against a single-process oracle scan of the
+whole problem; world size 3 gives uneven blocks.
 """
 import os
 import socket
@@ -77,12 +79,16 @@ def _worker(rank, world, port, k, out_path):
         if rank == 0:
             np.savez(out_path, rows=res.rows.numpy(), cols=res.cols.numpy(), stats=res.stats.numpy(),
                      cv=res.col_vals.numpy(), ci=res.col_idx.numpy())
+        else:
+            assert res.rows is None and res.cols is None
+            np.savez(f"{out_path}.{rank}.npz", cv=res.col_vals.numpy(), ci=res.col_idx.numpy(),
+                     stats=res.stats.numpy())
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 3])
 def test_sharded_scan_matches_single_process(oracle, tmp_path, world):
     k = 3
     out = tmp_path / "res.npz"
@@ -95,6 +101,10 @@ def test_sharded_scan_matches_single_process(oracle, tmp_path, world):
     assert np.array_equal(got["rows"], rows) and np.array_equal(got["cols"], cols)
     assert np.array_equal(got["ci"], ci) and np.array_equal(got["cv"], cv)
     np.testing.assert_allclose(got["stats"], st, rtol=1e-12)
+    for r in range(1, world):  # every rank holds the same merged column lists and certificate
+        other = np.load(f"{out}.{r}.npz")
+        assert np.array_equal(other["ci"], ci) and np.array_equal(other["cv"], cv)
+        np.testing.assert_allclose(other["stats"], st, rtol=1e-12)
 
 
 def _pairs_worker(rank, world, port, out_path):
