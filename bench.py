@@ -532,12 +532,19 @@ def run_pdlp(args, hb, dev, peaks):
     fast_ms = hb.last_kernel_times()
     hb.set_kernel_timing(False)
     fast_iter = (fast_ms[0] / 200 / 1e3) if fast_ms else fast_sec / iters
+    # algorithmic bytes: one copy of the edge state (x read + write, anchor, scaled cost, both
+    # endpoints) and the node state; the fused pass streams the edge state in both orders:
+    # per edge and side x, anchor, scaled cost, x write (8 B each), the other endpoint (4 B),
+    # the own endpoint's place in its tile (1 B)
     bytes_iter = 44 * e + 32 * (n + m)
+    stream_iter = 2 * 37 * e + 64 * (n + m)
     achieved = bytes_iter / per_iter / 1e9
     extra = {"dtype": "f64", "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                                           "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                                          "kernel": "hb::pdlp::edge_pass + source_pass + target_pass (one iteration)",
-                                          "bytes_per_iteration": bytes_iter, "iteration_us": per_iter * 1e6},
+                                          "kernel": "hb::pdlp::fused_pass (one launch per iteration, both sides)",
+                                          "bytes_per_iteration": bytes_iter, "iteration_us": per_iter * 1e6,
+                                          "streamed_bytes_per_iteration": stream_iter,
+                                          "streamed_gbs": stream_iter / per_iter / 1e9},
              "atomic_sums": {"iterations_per_s": iters / fast_sec, "iteration_us": fast_iter * 1e6,
                              "achieved_gbs": bytes_iter / fast_iter / 1e9,
                              "note": "deterministic=False: node sums by atomics in the edge pass"}}
@@ -589,7 +596,8 @@ def run_pairs(args, hb, dev, peaks):
     achieved = bytes_call / (kms[0] / 1e3) / 1e9 if kms else bytes_call / sec / 1e9
     extra = {"dtype": "f32 in, f64 accumulate", "roofline": {
         "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-        "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "hb::pairs::pair_kernel<3,32,1>",
+        "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+        "kernel": f"hb::pairs::pair_kernel_rows<3,{d // 128}>" if d in (128, 256, 512) else "hb::pairs::pair_kernel",
         "bytes_per_edge": bytes_call / e,
         "note": "each source row once, each target row per edge (no target reuse on a random support)"},
         "random_order": {"value": e / sec_r / 1e9, "unit": "Gedges/s",

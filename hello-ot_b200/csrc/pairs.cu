@@ -93,6 +93,95 @@ __global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, 
     }
 }
 
+// d = 128 NV with 16-byte-aligned rows: a warp per edge, lane l holding the float4 chunks
+// l + 32 v (v < NV) of the source row converted to fp64 in registers while consecutive edges
+// share the source row (the reference's source-grouped order), so each edge converts only
+// its target row.  The same chunks, order and reduction tree as pair_kernel<KIND, 32, true>:
+// the results are identical.
+template <int KIND, int NV>
+__global__ void __launch_bounds__(256, NV <= 1 ? 4 : NV == 2 ? 3 : 2) pair_kernel_rows(const float* __restrict__ x, const float* __restrict__ y,
+                                                        int64_t nx, int64_t ny, int d, const double* __restrict__ a,
+                                                        const double* __restrict__ b, double scale,
+                                                        const int64_t* __restrict__ rows,
+                                                        const int64_t* __restrict__ cols, int64_t count,
+                                                        double* __restrict__ out, int* status, const Perturb pert) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t per_warp = (count + warps - 1) / warps;
+    const int64_t e_end = min(count, (warp_id + 1) * per_warp);
+    // one edge ahead: the next edge's indices, target row chunks and (when it starts a new
+    // source row) source row chunks are loaded before this edge's arithmetic
+    double xd[NV * 4];
+    float4 yv[NV], yn[NV], xn[NV];
+    int64_t e = warp_id * per_warp;
+    int64_t r = 0, c = 0, held = -1;
+    bool ok = false, fresh = false;  // fresh: xn holds this edge's source row (a new one)
+    auto fetch = [&](int64_t ee, int64_t prev, int64_t& rr, int64_t& cc, bool& okk, bool& fr) {
+        rr = rows[ee];
+        cc = cols[ee];
+        okk = rr >= 0 && rr < nx && cc >= 0 && cc < ny;
+        fr = okk && rr != prev;
+        if (okk) {
+            const float4* y4 = reinterpret_cast<const float4*>(y + cc * d);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) yn[v] = __ldg(y4 + lane + 32 * v);
+        }
+        if (fr) {
+            const float4* x4 = reinterpret_cast<const float4*>(x + rr * d);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) xn[v] = __ldg(x4 + lane + 32 * v);
+        }
+    };
+    if (e < e_end) fetch(e, held, r, c, ok, fresh);
+    for (; e < e_end; ++e) {  // warp-uniform
+        if (fresh) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                xd[4 * v] = xn[v].x; xd[4 * v + 1] = xn[v].y; xd[4 * v + 2] = xn[v].z; xd[4 * v + 3] = xn[v].w;
+            }
+            held = r;
+        }
+#pragma unroll
+        for (int v = 0; v < NV; ++v) yv[v] = yn[v];
+        const int64_t rc = r, cc = c;
+        const bool okc = ok;
+        if (e + 1 < e_end) fetch(e + 1, held, r, c, ok, fresh);
+        double acc = 0.0;
+        if (okc) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                const float yy[4] = {yv[v].x, yv[v].y, yv[v].z, yv[v].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const double xa = xd[4 * v + j], yb = (double)yy[j];
+                    if (KIND == 3) {
+                        acc = fma(xa, yb, acc);
+                    } else {
+                        const double z = yb - xa;
+                        acc = KIND == 0 ? acc + fabs(z) : KIND == 1 ? fmax(acc, fabs(z)) : fma(z, z, acc);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc = combine<KIND>(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+        if (lane == 0) {
+            if (!okc) {
+                atomicOr(status, kErrBadInput);
+                out[e] = __longlong_as_double(0x7ff8000000000000LL);
+            } else if (KIND == 3) {
+                out[e] = (a[rc] + b[cc]) - scale * acc;
+            } else {
+                const double dist = KIND == 2 ? sqrt(acc) : acc;
+                out[e] = pert.sigma != 0.0 ? dist + noise_of(pert, noise_input(pert, pert.row_index[rc]),
+                                                                noise_input(pert, pert.col_index[cc]))
+                                           : dist;
+            }
+        }
+    }
+}
+
 template <int KIND, int G>
 void launch_g(bool vec, const float* x, const float* y, int64_t nx, int64_t ny, int d, const double* a,
               const double* b, double s, const int64_t* rows, const int64_t* cols, int64_t count, double* out,
@@ -116,6 +205,18 @@ void launch_kind(const float* x, const float* y, int64_t nx, int64_t ny, int d, 
     int64_t want = (count * g + 255) / 256;
     const int64_t cap = (int64_t)sms * 16;
     const int blocks = (int)(want < 1 ? 1 : (want > cap ? cap : want));
+    if (vec && (d == 128 || d == 256 || d == 512)) {
+        timing_mark(st);
+        if (d == 128)
+            pair_kernel_rows<KIND, 1><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
+        else if (d == 256)
+            pair_kernel_rows<KIND, 2><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
+        else
+            pair_kernel_rows<KIND, 4><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
+        timing_mark(st);
+        count_launches(1);
+        return;
+    }
     switch (g) {
         case 1: launch_g<KIND, 1>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;
         case 2: launch_g<KIND, 2>(vec, x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, blocks, st, pert); break;

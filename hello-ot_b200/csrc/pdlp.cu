@@ -69,6 +69,8 @@ struct Dev {
     double *tx, *tax, *tcs;
     int *t_row, *t_col;
     double *sdb[2], *tdb[2];
+    unsigned char *e_lane, *t_lane;  // fused passes: the own endpoint's place in its tile (node % 256), both orders
+    int* fp_part;   // fused passes: tile runs of the blocks, sources then targets ([2][FP_MAX_RUNS + 1])
     double* red;    // [RED_BLOCKS][8]
     Step* steps;    // [frequency] the current block's per-iteration parameters
     double* scal;   // [16] reduced scalars
@@ -376,103 +378,243 @@ __global__ void __launch_bounds__(256) node_pass_wide(Dev D, int it, int src_blo
 }
 
 // Fused passes (the default for sparse supports): one launch per iteration.  The edge state
-// is kept twice, in source order (x, ax, cs) and in target order (tx, tax, tcs); a warp takes
-// 32 consecutive nodes of one side, applies the per-edge update (primal step, reflection,
-// Halpern averaging: the same operations as edge_pass, so both copies stay equal bit for bit)
-// to the nodes' contiguous edge range in coalesced chunks staged through shared memory, adds
-// each node's reflected primal in edge order (the reference's order) and updates the node's
-// dual.  The edge updates read the node scales of buffer `parity` and the dual updates write
+// is kept twice, in source order (x, ax, cs) and in target order (tx, tax, tcs), so each side
+// reads its nodes' edges contiguously.  Tiles are FP_NODES consecutive nodes of one side
+// (node v at place v % FP_NODES, one per thread).  A persistent block owns a run of
+// consecutive tiles of one side, the runs balanced by edges, and streams the run's edge
+// state through a ring of C::ST shared-memory stages of C::CH edges, filled by bulk copies
+// (cp.async.bulk issued by one thread, completion on one mbarrier per stage).  Per stage:
+// the threads apply the per-edge update (primal step, reflection, Halpern averaging: the
+// operations of edge_pass, so both copies stay equal bit for bit) to the stage's edges,
+// thread-strided, write the new primal and stage the reflected primal; after one barrier
+// the stage is refilled, the node scales of the next stage's edges are gathered (from L2;
+// they arrive while the block works on), and each thread adds its node's reflected primals
+// in edge order (the reference's order), updating its node's dual when its tile's edges
+// end.  The edge updates read the node scales of buffer `parity` and the dual updates write
 // the other buffer, so the source and target sides run side by side in one launch.  The
 // source side also writes px / dx, which the evaluation and restart kernels read.
-template <bool TGT>
-__device__ __forceinline__ void fused_side(const Dev& D, const Step& s, int v0, double* stage) {
-    const int lane = threadIdx.x & 31, nodes = TGT ? D.m : D.n, v = v0 + lane;
+constexpr int FP_NODES = 256;      // nodes per tile = threads per block
+constexpr int FP_MAX_RUNS = 4096;  // blocks per side, at most
+
+template <int CH_, int ST_, int BPS_, bool CG_ = false>
+struct FpCfg {
+    static constexpr int CH = CH_;    // edges per stage
+    static constexpr int ST = ST_;    // stages
+    static constexpr int BPS = BPS_;  // blocks per SM
+    static constexpr bool CG = CG_;   // node-scale gathers cached in L2 only
+    static constexpr int PER = CH / FP_NODES;  // edges per thread in one stage
+};
+
+template <class C>
+struct FpStage {  // 16-byte-aligned starts, each array rounded so the next stays aligned
+    double x[C::CH + 4], ax[C::CH + 4], cs[C::CH + 4];
+    int o[C::CH + 4];
+    unsigned char ln[C::CH + 16];
+};
+template <class C>
+struct alignas(16) FpShared {
+    FpStage<C> st[C::ST];
+    double rs[2][C::CH];  // reflected primals of the last two stages
+    uint64_t bar[C::ST];
+    int abort_flag;
+};
+
+template <class C, bool TGT>
+__device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int te, FpShared<C>& sh) {
+    constexpr int CH = C::CH, ST = C::ST, PER = C::PER;
+    const int t = threadIdx.x, nodes = TGT ? D.m : D.n;
     const int* off = TGT ? D.t_off : D.s_off;
-    const int w0 = off[v0], w1 = off[min(v0 + 32, nodes)];
-    const int b0 = v < nodes ? off[v] : w1, b1 = v < nodes ? off[v + 1] : w1;
-    // the warp's own nodes' scales, one per lane; each edge takes its node's by a shuffle
-    const double own = v < nodes ? (TGT ? D.tdb : D.sdb)[s.parity][v] : 0.0;
-    const double* other = TGT ? D.sdb[s.parity] : D.tdb[s.parity];
     double* X = TGT ? D.tx : D.x;
     const double* AX = TGT ? D.tax : D.ax;
     const double* CS = TGT ? D.tcs : D.cs;
-    const int* O = TGT ? D.t_row : D.e_col;  // the other endpoint of each edge
-    double sum = 0.0;
-    constexpr int PER = 4;  // edges per lane loaded together (two batches per 256-edge chunk)
-    for (int c0 = w0; c0 < w1; c0 += SEG_CHUNK) {
-        const int c1 = min(w1, c0 + SEG_CHUNK);
-        // each batch issues all of the lane's loads first (the other side's node scales are
-        // gathered from L2), so they are in flight together; then the updates and the stores
+    const int* O = TGT ? D.t_row : D.e_col;                 // the other endpoint of each edge
+    const unsigned char* LN = TGT ? D.t_lane : D.e_lane;    // the own endpoint's place in its tile
+    const double* ownb = (TGT ? D.tdb : D.sdb)[s.parity];
+    const double* other = TGT ? D.sdb[s.parity] : D.tdb[s.parity];
+    auto tile_end = [&](int tl) { return off[min(tl * FP_NODES + FP_NODES, nodes)]; };
+    const int E0 = off[tb * FP_NODES], E1 = tile_end(te - 1);
+    const int nch = (E1 - E0 + CH - 1) / CH;
+    auto issue = [&](int k) {  // one thread: the bulk copies of chunk k into stage k % ST
+        const int c0 = E0 + k * CH, c1 = min(E1, c0 + CH);
+        const int d0 = c0 & ~1, d1 = (c1 + 1) & ~1, i0 = c0 & ~3, i1 = (c1 + 3) & ~3, b0 = c0 & ~15,
+                  b1 = (c1 + 15) & ~15;
+        FpStage<C>& S = sh.st[k % ST];
+        uint64_t* bar = &sh.bar[k % ST];
+        const uint32_t nd = (uint32_t)(d1 - d0) * 8u, ni = (uint32_t)(i1 - i0) * 4u, nb = (uint32_t)(b1 - b0);
+        mbar_arrive_expect_tx(bar, 3u * nd + ni + nb);
+        bulk_load_1d(S.x, X + d0, nd, bar);
+        bulk_load_1d(S.ax, AX + d0, nd, bar);
+        bulk_load_1d(S.cs, CS + d0, nd, bar);
+        bulk_load_1d(S.o, O + i0, ni, bar);
+        bulk_load_1d(S.ln, LN + b0, nb, bar);
+    };
+    if (t == 0)
+        for (int k = 0; k < ST && k < nch; ++k) issue(k);
+    // gather cursor: tile gt holds the first edge of the stage being gathered; gT1 / gT2 are
+    // the ends of tiles gt and gt + 1 (the run's end past the run)
+    int gt = tb, gT1 = tile_end(tb), gT2 = tb + 1 < te ? tile_end(tb + 1) : E1;
+    double o[PER], m[PER];  // the other and own node scales of the stage's edges
+    auto gather = [&](int k) {  // false: the stage's copies never completed
+        if (!mbar_wait(&sh.bar[k % ST], (uint32_t)((k / ST) & 1), &sh.abort_flag, D.status)) return false;
+        const FpStage<C>& S = sh.st[k % ST];
+        const int c0 = E0 + k * CH, c1 = min(E1, c0 + CH), i0 = c0 & ~3, lb0 = c0 & ~15;
+        while (gT1 <= c0 && gt + 1 < te) {  // block-uniform
+            ++gt;
+            gT1 = gT2;
+            gT2 = gt + 1 < te ? tile_end(gt + 1) : E1;
+        }
 #pragma unroll
-        for (int h = 0; h < SEG_CHUNK / (32 * PER); ++h) {
-            int oo[PER];
-            double xv[PER], av[PER], cv[PER], at[PER];
-#pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                const int q = c0 + (h * PER + u) * 32 + lane;
-                if (q < c1) {
-                    oo[u] = __ldg(O + q);
-                    xv[u] = X[q]; av[u] = __ldg(AX + q); cv[u] = __ldg(CS + q);
+        for (int j = 0; j < PER; ++j) {
+            const int q = c0 + j * FP_NODES + t;
+            o[j] = m[j] = 0.0;
+            if (q < c1) {
+                int tl = q < gT1 ? gt : gt + 1;
+                if (q >= gT2) {  // past tile gt + 1 (tiles of few edges): the last tile starting at or before q
+                    int lo = gt + 2, hi = te - 1;
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (off[mid * FP_NODES] <= q) lo = mid; else hi = mid - 1;
+                    }
+                    tl = lo;
                 }
-            }
-#pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                const int q = c0 + (h * PER + u) * 32 + lane;
-                // the lane owning edge q: the last lane whose segment starts at or before q
-                int l = 0;
-#pragma unroll
-                for (int stp = 16; stp > 0; stp >>= 1) {
-                    const int cand = l + stp;
-                    const int bc = __shfl_sync(0xffffffffu, b0, cand & 31);
-                    if (cand < 32 && bc <= q) l = cand;
+                if (C::CG) {
+                    o[j] = __ldcg(other + S.o[q - i0]);
+                    m[j] = __ldcg(ownb + tl * FP_NODES + S.ln[q - lb0]);
+                } else {
+                    o[j] = __ldg(other + S.o[q - i0]);
+                    m[j] = __ldg(ownb + tl * FP_NODES + S.ln[q - lb0]);
                 }
-                const double mine = __shfl_sync(0xffffffffu, own, l);
-                if (q < c1) {
-                    const double o = __ldg(other + oo[u]);
-                    at[u] = TGT ? o + mine : mine + o;  // sd[row] + td[col], the edge pass's order
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                const int q = c0 + (h * PER + u) * 32 + lane;
-                if (q >= c1) continue;
-                const double pxv = max0(xv[u] - s.primal_step * (cv[u] - at[u]));
-                const double r = 2.0 * pxv - xv[u];
-                if (!TGT) {
-                    if (s.checkpoint) D.dx[q] = r - xv[u];
-                    if (s.major) D.px[q] = pxv;
-                }
-                X[q] = s.halpern * r + (1.0 - s.halpern) * av[u];
-                stage[q - c0] = r;
             }
         }
-        __syncwarp();
-        const int lo = max(b0, c0), hi = min(b1, c1);
-        for (int q = lo; q < hi; ++q) sum += stage[q - c0];
-        __syncwarp();
+        return true;
+    };
+    auto drain = [&](int k) {  // after a failed wait: a bounded wait for the copies in flight
+        for (int j = k + 1; j < nch && j < k + ST; ++j)
+            for (int u = 0; u < 64 && !mbar_try_wait(&sh.bar[j % ST], (uint32_t)((j / ST) & 1)); ++u) {
+            }
+    };
+    // sum cursor: this thread's node of tile `tile`, its edge range, its state; the next
+    // tile's offsets are loaded one tile ahead
+    int tile = tb, v = tb * FP_NODES + t;
+    int T1 = gT1;
+    int b0 = v < nodes ? off[v] : T1, b1 = v < nodes ? off[v + 1] : T1;
+    int nT1 = 0, nb0 = 0, nb1 = 0;
+    auto prefetch_next = [&]() {
+        if (tile + 1 >= te) return;
+        const int nv = (tile + 1) * FP_NODES + t;
+        nT1 = tile_end(tile + 1);
+        nb0 = nv < nodes ? off[nv] : nT1;
+        nb1 = nv < nodes ? off[nv + 1] : nT1;
+    };
+    prefetch_next();
+    double yv, nsv, bsv, ayv;
+    auto node_state = [&]() {
+        const int i = (TGT ? D.n : 0) + (v < nodes ? v : 0);
+        yv = D.y[i]; nsv = D.ns[i]; bsv = D.bs[i]; ayv = D.ay[i];
+    };
+    node_state();
+    double sum = 0.0;
+    auto finish_tile = [&]() {  // the dual update of this thread's node; false past the run
+        if (v < nodes) {
+            const int i = TGT ? D.n + v : v;
+            const double pyv = yv - s.dual_step * (sum / nsv - bsv);
+            const double refl = 2.0 * pyv - yv;
+            if (s.checkpoint) D.dy[i] = refl - yv;
+            const double ynew = s.halpern * refl + (1.0 - s.halpern) * ayv;
+            D.y[i] = ynew;
+            if (s.major) D.py[i] = pyv;
+            (TGT ? D.tdb : D.sdb)[s.parity ^ 1][v] = ynew / nsv;
+        }
+        sum = 0.0;
+        if (++tile >= te) return false;
+        v = tile * FP_NODES + t;
+        T1 = nT1; b0 = nb0; b1 = nb1;
+        prefetch_next();
+        node_state();
+        return true;
+    };
+    bool more = true;
+    if (nch > 0 && !gather(0)) { drain(0); return; }
+    for (int k = 0; k < nch; ++k) {
+        const FpStage<C>& S = sh.st[k % ST];
+        const int c0 = E0 + k * CH, c1 = min(E1, c0 + CH), d0 = c0 & ~1;
+        double* rs = sh.rs[k & 1];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int q = c0 + j * FP_NODES + t;
+            if (q >= c1) continue;
+            const double xv = S.x[q - d0];
+            const double at = TGT ? o[j] + m[j] : m[j] + o[j];  // sd[row] + td[col]
+            const double pxv = max0(xv - s.primal_step * (S.cs[q - d0] - at));
+            const double r = 2.0 * pxv - xv;
+            if (!TGT) {
+                if (s.checkpoint) D.dx[q] = r - xv;
+                if (s.major) D.px[q] = pxv;
+            }
+            X[q] = s.halpern * r + (1.0 - s.halpern) * S.ax[q - d0];
+            rs[q - c0] = r;
+        }
+        __syncthreads();  // stage k is consumed; rs[k & 1] is complete
+        if (t == 0 && k + ST < nch) issue(k + ST);
+        if (k + 1 < nch && !gather(k + 1)) { drain(k + 1); return; }
+        for (;;) {  // this thread's nodes with edges in the stage
+            const int l0 = max(b0, c0), h0 = min(b1, c1);
+            int q = l0;
+            for (; q + 4 <= h0; q += 4) {  // loads side by side, adds in edge order
+                const double r0 = rs[q - c0], r1 = rs[q + 1 - c0], r2 = rs[q + 2 - c0], r3 = rs[q + 3 - c0];
+                sum += r0; sum += r1; sum += r2; sum += r3;
+            }
+            for (; q < h0; ++q) sum += rs[q - c0];
+            if (T1 > c1) break;  // the tile goes on into the next stage
+            if (!(more = finish_tile())) break;
+        }
     }
-    if (v >= nodes) return;
-    const int i = TGT ? D.n + v : v;
-    const double yv = D.y[i];
-    const double pyv = yv - s.dual_step * (sum / D.ns[i] - D.bs[i]);
-    const double refl = 2.0 * pyv - yv;
-    if (s.checkpoint) D.dy[i] = refl - yv;
-    const double ynew = s.halpern * refl + (1.0 - s.halpern) * D.ay[i];
-    D.y[i] = ynew;
-    if (s.major) D.py[i] = pyv;
-    (TGT ? D.tdb : D.sdb)[s.parity ^ 1][v] = ynew / D.ns[i];
+    while (more) more = finish_tile();  // tiles without edges after the last stage
 }
 
-// Blocks [0, src_blocks) take 8 x 32 sources each, the rest 8 x 32 targets each.
-__global__ void __launch_bounds__(256, 4) fused_pass(Dev D, int it, int src_blocks) {
-    __shared__ double stage[8][SEG_CHUNK];
+// Blocks [0, runs) take source runs, [runs, 2 runs) target runs; run r of a side covers the
+// tiles [part[r], part[r + 1]).
+template <class C>
+__global__ void __launch_bounds__(FP_NODES, C::BPS) fused_pass(Dev D, int it, int runs) {
+    extern __shared__ __align__(128) unsigned char fp_smem[];
+    FpShared<C>& sh = *reinterpret_cast<FpShared<C>*>(fp_smem);
+    const bool target = (int)blockIdx.x >= runs;
+    const int r = target ? (int)blockIdx.x - runs : (int)blockIdx.x;
+    const int* part = D.fp_part + (target ? FP_MAX_RUNS + 1 : 0);
+    const int tb = part[r], te = part[r + 1];
+    if (tb >= te) return;  // block-uniform
+    if (threadIdx.x == 0) {
+        sh.abort_flag = 0;
+        for (int j = 0; j < C::ST; ++j) mbar_init(&sh.bar[j], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
     const Step s = D.steps[it];
-    const int warp = threadIdx.x >> 5;
-    const bool target = (int)blockIdx.x >= src_blocks;  // block-uniform
-    const int v0 = (((int)blockIdx.x - (target ? src_blocks : 0)) * 8 + warp) * 32;
-    if (v0 >= (target ? D.m : D.n)) return;  // warp-uniform
-    if (target) fused_side<true>(D, s, v0, stage[warp]);
-    else fused_side<false>(D, s, v0, stage[warp]);
+    if (target) fp_side<C, true>(D, s, tb, te, sh);
+    else fp_side<C, false>(D, s, tb, te, sh);
+}
+
+// Tile runs balanced by edges: part[r] = the first tile whose first edge is at or after
+// r * E / runs, part[runs] = all tiles; sources at fp_part, targets at fp_part + FP_MAX_RUNS + 1.
+__global__ void fp_partition(Dev D, int runs) {
+    for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < 2 * (runs + 1); u += gridDim.x * blockDim.x) {
+        const bool target = u > runs;
+        const int r = target ? u - runs - 1 : u;
+        const int nodes = target ? D.m : D.n;
+        const int* off = target ? D.t_off : D.s_off;
+        const int tiles = (nodes + FP_NODES - 1) / FP_NODES;
+        int res = tiles;
+        if (r < runs) {
+            const int64_t want = D.e * (int64_t)r / runs;
+            int lo = 0, hi = tiles;  // first tile with off[FP_NODES tile] >= want
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (off[mid * FP_NODES] < want) lo = mid + 1; else hi = mid;
+            }
+            res = lo;
+        }
+        D.fp_part[(target ? FP_MAX_RUNS + 1 : 0) + r] = res;
+    }
 }
 
 // The target-order copy of the edge state: structure (once), cost and primal (at the
@@ -481,7 +623,11 @@ __global__ void target_copy(Dev D, int structure) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < D.e; q += stride) {
         const int p = D.t_pos[q];
-        if (structure) { D.t_row[q] = D.e_row[p]; D.t_col[q] = D.e_col[p]; D.tcs[q] = D.cs[p]; }
+        if (structure) {
+            D.t_row[q] = D.e_row[p]; D.t_col[q] = D.e_col[p]; D.tcs[q] = D.cs[p];
+            D.t_lane[q] = (unsigned char)(D.e_col[p] & 255);
+            D.e_lane[q] = (unsigned char)(D.e_row[q] & 255);
+        }
         D.tx[q] = D.x[p];
         D.tax[q] = D.ax[p];
     }
@@ -613,17 +759,32 @@ struct PdlpLayout {
 PdlpLayout pdlp_layout(void* base, size_t size, int64_t n, int64_t m, int64_t e) {
     PdlpLayout L;
     const int64_t nodes = n + m;
-    Arena ar{static_cast<char*>(base), size, 0};
+    // arrays start on 256-byte boundaries of the device address space (the fused passes
+    // bulk-copy edge arrays from 16-byte-aligned starts); the edge arrays the fused passes
+    // stream hold e rounded up to 4 elements, as the copies read whole 4-element groups
+    char* b = static_cast<char*>(base);
+    if (b) {
+        const uintptr_t a = (reinterpret_cast<uintptr_t>(b) + 255) & ~uintptr_t(255);
+        const size_t skip = a - reinterpret_cast<uintptr_t>(b);
+        size = size > skip ? size - skip : 0;
+        b = reinterpret_cast<char*>(a);
+    }
+    Arena ar{b, size, 0};
+    const int64_t e4 = (e + 3) & ~int64_t(3);
     auto take_i = [&](int*& p, size_t c) { p = ar.take<int>(c); if (base && !p) L.ok = false; };
     auto take_d = [&](double*& p, size_t c) { p = ar.take<double>(c); if (base && !p) L.ok = false; };
     pdlp::Dev& D = L.D;
-    take_i(D.e_row, e); take_i(D.e_col, e); take_i(D.e_orig, e); take_i(D.s_off, n + 1); take_i(D.t_off, m + 1);
+    take_i(D.e_row, e); take_i(D.e_col, e4); take_i(D.e_orig, e); take_i(D.s_off, n + 1); take_i(D.t_off, m + 1);
     take_i(D.t_pos, e);
-    take_d(D.cost, e); take_d(D.cs, e); take_d(D.ax, e); take_d(D.x, e); take_d(D.px, e); take_d(D.rx, e);
+    take_d(D.cost, e); take_d(D.cs, e4); take_d(D.ax, e4); take_d(D.x, e4); take_d(D.px, e); take_d(D.rx, e);
     take_d(D.dx, e);
     take_d(D.mass, nodes); take_d(D.scale, nodes); take_d(D.bs, nodes); take_d(D.ns, nodes); take_d(D.ay, nodes);
     take_d(D.y, nodes); take_d(D.py, nodes); take_d(D.dy, nodes); take_d(D.td, m); take_d(D.sd, n); take_d(D.ssum, n); take_d(D.tsum, m);
-    take_d(D.tx, e); take_d(D.tax, e); take_d(D.tcs, e); take_i(D.t_row, e); take_i(D.t_col, e);
+    take_d(D.tx, e4); take_d(D.tax, e4); take_d(D.tcs, e4); take_i(D.t_row, e4); take_i(D.t_col, e);
+    take_i(D.fp_part, 2 * (pdlp::FP_MAX_RUNS + 1));
+    D.e_lane = ar.take<unsigned char>((size_t)((e + 15) & ~int64_t(15)));
+    D.t_lane = ar.take<unsigned char>((size_t)((e + 15) & ~int64_t(15)));
+    if (base && (!D.e_lane || !D.t_lane)) L.ok = false;
     D.sdb[0] = D.sd; D.tdb[0] = D.td;
     take_d(D.sdb[1], n); take_d(D.tdb[1], m);
     take_d(D.red, (size_t)pdlp::RED_BLOCKS * 8); take_d(D.scal, 16);
@@ -653,7 +814,7 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
                size_t ws_bytes, cudaStream_t st, std::string& err) {
     using Clock = std::chrono::steady_clock;
     const auto started = Clock::now();
-    if (n < 1 || m < 1 || e < 1 || e > INT32_MAX - 1 || n + m > INT32_MAX - 1 || ctl.frequency < 1 ||
+    if (n < 1 || m < 1 || e < 1 || e > INT32_MAX - 1024 || n + m > INT32_MAX - 1 || ctl.frequency < 1 ||
         ctl.iteration_limit < 1 || !(ctl.time_limit > 0)) {
         err = "invalid restricted OT dimensions or runtime limits";
         return 2;
@@ -743,16 +904,25 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     // fused passes (one launch per iteration) unless node sums are atomic or a side is dense
     const bool fused = !ctl.atomic && !wide_sources && !wide_targets;
     const int per_iter = fused ? 1 : (!ctl.atomic && wide_sources && wide_targets) ? 2 : 3;  // kernels per iteration
-    const int fsb = (int)((n + 255) / 256), ftb = (int)((m + 255) / 256);  // fused pass: source / target blocks
+    // fused passes: persistent blocks, half of them per side; stages of 512 edges, two per block
+    // (a third stage measured slower), four blocks per SM, node-scale gathers cached in L2 only
+    using FpDefault = pdlp::FpCfg<512, 2, 4, true>;
+    void (*fp_kernel)(pdlp::Dev, int, int) = pdlp::fused_pass<FpDefault>;
+    const int fp_bps = FpDefault::BPS;
+    const size_t fp_bytes = sizeof(pdlp::FpShared<FpDefault>);
+    const int runs = std::min(sms * fp_bps / 2, pdlp::FP_MAX_RUNS);
     int parity = 0;  // fused passes: the node-scale buffer the next iteration reads
     if (fused) {
+        if (cudaFuncSetAttribute(fp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fp_bytes) != cudaSuccess)
+            return fail("fused pass shared memory");
         pdlp::target_copy<<<gb, 256, 0, st>>>(D, 1);
-        HB_LAUNCHED(1);
+        pdlp::fp_partition<<<(2 * runs + 257) / 256, 256, 0, st>>>(D, runs);
+        HB_LAUNCHED(2);
     }
     // One iteration: the three kernels reading D.steps[it].
     auto launch_iteration = [&](cudaStream_t s_, int it, bool counted) {
         if (fused) {
-            pdlp::fused_pass<<<(unsigned)(fsb + ftb), 256, 0, s_>>>(D, it, fsb);
+            fp_kernel<<<(unsigned)(2 * runs), pdlp::FP_NODES, fp_bytes, s_>>>(D, it, runs);
         } else if (ctl.atomic) {
             pdlp::edge_pass<true><<<gb, 256, 0, s_>>>(D, it);
             pdlp::source_pass<true><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);

@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
-@pytest.mark.parametrize("d", [1, 3, 4, 16, 70, 257, 1024])
+@pytest.mark.parametrize("d", [1, 3, 4, 16, 70, 128, 256, 257, 512, 1024])
 @pytest.mark.parametrize("kind", ["l1", "linf", "l2", "lowrank"])
 def test_pair_costs_match_oracle(hb, cuda, oracle, d, kind):
     rng = np.random.default_rng(d)
@@ -17,6 +17,31 @@ def test_pair_costs_match_oracle(hb, cuda, oracle, d, kind):
     y = rng.normal(size=(200, d)).astype(np.float32)
     e = 5000
     rows, cols = rng.integers(0, 300, e), rng.integers(0, 200, e)
+    a = (x.astype(np.float64) ** 2).sum(1)
+    b = (y.astype(np.float64) ** 2).sum(1)
+    if kind == "lowrank":
+        got = hb.cost_pairs_lowrank(dict(F=x, G=y, a=a, b=b, dot_scale=2.0), rows, cols)
+        exp = oracle.pair_costs("raw", x, y, rows, cols, a, b, dot_scale=2.0)
+        np.testing.assert_allclose(got, exp, rtol=0, atol=1e-12 * (np.abs(a[rows]) + np.abs(b[cols]) + 1).max())
+    else:
+        got = hb.pair_costs_metric(source_points=x, target_points=y, rows=rows, cols=cols, cost_type=kind)
+        exp = oracle.pair_costs(kind, x, y, rows, cols)
+        if kind == "linf":
+            assert np.array_equal(got, exp)
+        else:
+            np.testing.assert_allclose(got, exp, rtol=1e-13, atol=0)
+
+
+@pytest.mark.parametrize("d", [128, 256, 512])
+@pytest.mark.parametrize("kind", ["l1", "linf", "l2", "lowrank"])
+def test_pair_costs_source_grouped(hb, cuda, oracle, d, kind):
+    """Edges grouped by source row: runs of equal rows, which the kernel for d = 128, 256,
+    512 serves from the source row it holds in registers."""
+    rng = np.random.default_rng(d + 7)
+    x = rng.normal(size=(90, d)).astype(np.float32)
+    y = rng.normal(size=(300, d)).astype(np.float32)
+    rows = np.sort(rng.integers(0, 90, 4000))
+    cols = rng.integers(0, 300, 4000)
     a = (x.astype(np.float64) ** 2).sum(1)
     b = (y.astype(np.float64) ** 2).sum(1)
     if kind == "lowrank":
