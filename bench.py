@@ -111,9 +111,10 @@ def make_workload(n, d, seed, device, rows=None):
     gx = torch.Generator(device=device)
     gx.manual_seed(x_full_seed)
     lo, hi = rows if rows is not None else (0, n)
-    # generate the source cloud in fixed 65536-row chunks so a block equals the full cloud's rows
+    # generate the source cloud in fixed 65536-row chunks so a block equals the full cloud's
+    # rows, written in place (config 4's clouds are 42 GB each: no concatenated copies)
     chunk = 65536
-    parts = []
+    x = torch.empty(hi - lo, d, device=device)
     for c0 in range(0, n, chunk):
         c1 = min(n, c0 + chunk)
         gc = torch.Generator(device=device)
@@ -121,16 +122,26 @@ def make_workload(n, d, seed, device, rows=None):
         if c1 <= lo or c0 >= hi:
             continue
         block = torch.randn(c1 - c0, d, device=device, generator=gc)
-        parts.append(block[max(lo, c0) - c0:min(hi, c1) - c0])
-    x = torch.cat(parts)
-    a = (x.double() ** 2).sum(1)
-    b = (y.double() ** 2).sum(1)
+        s0, s1 = max(lo, c0), min(hi, c1)
+        x[s0 - lo:s1 - lo] = block[s0 - c0:s1 - c0]
+        del block
+
+    def sq_norms(v):  # row norms in fp64, a chunk of rows at a time
+        out = torch.empty(v.shape[0], dtype=torch.float64, device=device)
+        for r0 in range(0, v.shape[0], chunk):
+            out[r0:r0 + chunk] = (v[r0:r0 + chunk].double() ** 2).sum(1)
+        return out
+
+    a = sq_norms(x)
+    b = sq_norms(y)
     # median pairwise cost from 65536 sampled pairs (seed 42)
     gs = torch.Generator(device=device)
     gs.manual_seed(42)
     si = torch.randint(0, x.shape[0], (65536,), device=device, generator=gs)
     sj = torch.randint(0, n, (65536,), device=device, generator=gs)
-    med = float(((x[si].double() - y[sj].double()) ** 2).sum(1).median().item())
+    costs = torch.cat([((x[si[c:c + 4096]].double() - y[sj[c:c + 4096]].double()) ** 2).sum(1)
+                       for c in range(0, si.numel(), 4096)])
+    med = float(costs.median().item())
     f = torch.randn(x.shape[0], device=device, dtype=torch.float64, generator=gs) * med
     gd = torch.randn(n, device=device, dtype=torch.float64, generator=gs) * med
     return x, y, a, b, f, gd, med
@@ -307,7 +318,8 @@ def scan_mode(args):
 
 
 def workload_config(args):
-    return {"workload": f"C5 isolated pricing scan, l2sq, m=n={args.n}, d={args.d}, k={args.k}",
+    name = {(1_048_576, 256): "C5", (1_280_000, 8192): "C4"}.get((args.n, args.d), "custom")
+    return {"workload": f"{name} isolated pricing scan, l2sq, m=n={args.n}, d={args.d}, k={args.k}",
             "n": args.n, "m": args.n, "d": args.d, "topk": args.k, "cost": "l2sq", "dot_scale": 2.0,
             "precision": {"fp32": "3-term fp16 split (fp32-class dot)", "tf32": "1xTF32"}[args.precision],
             "lists": "exact fp64 top-k (fp64 re-check)" if args.exact else "fp32-class top-k",
