@@ -46,8 +46,9 @@ sys.path.insert(0, str(REPO))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per pair of the scan kernel from an ncu capture of the full
-# config-5 launch, scaled by the pairs of the launch
-DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass"): 1.1672}
+# config-5 launch (dram__bytes_read.sum + dram__bytes_write.sum over its 2^40 pairs), scaled by
+# the pairs of the launch; keyed by (d, precision, mode, exact lists)
+DRAM_BYTES_PER_PAIR = {(256, "fp32", "one-pass", False): 1.1672, (256, "fp32", "one-pass", True): 1.2835}
 
 
 # per-path default sizes: config 5 (m = n = 2^20, d = 256) for the l2sq scans, pair costs and
@@ -411,7 +412,7 @@ def run_ours(args):
         flops = 2.0 * d * rows_local * n  # algorithmic flops of one launch: one dot product per pair
         achieved = flops / (pass1_ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
-        per_pair = DRAM_BYTES_PER_PAIR.get((d, args.precision, mode))
+        per_pair = DRAM_BYTES_PER_PAIR.get((d, args.precision, mode, bool(args.exact)))
         traffic = per_pair * rows_local * n if per_pair else None
         out = {
             "metric": "pricing-scan Gpairs/s (m·n)", "value": value, "unit": "Gpairs/s", "n_gpus": world,
