@@ -60,10 +60,13 @@ def _fold_extras(x, y, query_cost, query_bias, dot_scale, raw_extras):
 
 
 def bidirectional(x, y, f, g, k, kind, *, raw_costs=None, raw_biases=None, dot_scale=2., workspace_bytes=None,
-                  perturbation=None, compute_precision=0, raw_extras=None, tile_limits=None, planned_tiles=None):
+                  perturbation=None, compute_precision=0, raw_extras=None, tile_limits=None, planned_tiles=None,
+                  exact=True):
     """(rv q x k, ri int64, cv n x k, ci int64, num, den, max s+, max |c|, count int64):
     row and column top-k of the scores and the full certificate (generic_scan.py:328-404).
-    kind 3 (raw l2^2) takes raw_costs = (nx, ny) and raw_biases = (f - nx, g - ny)."""
+    kind 3 (raw l2^2) takes raw_costs = (nx, ny) and raw_biases = (f - nx, g - ny); its lists
+    are the exact fp64 top-k (the fp64 re-check, as ScanExtension's default) unless
+    exact=False."""
     _check(x, y, k, (f, len(x)), (g, len(y)))
     raw = raw_costs is not None
     _precision(compute_precision, raw, x)
@@ -78,7 +81,7 @@ def bidirectional(x, y, f, g, k, kind, *, raw_costs=None, raw_biases=None, dot_s
         if dot_scale not in (1., 2.):
             raise ValueError("dot_scale must be exactly 1 or 2")
         xx, yy, nxx, qbb = _fold_extras(x, y, nx, qb, dot_scale, raw_extras)
-        rv, ri, cv, ci, s = l2sq_scan(xx, yy, nxx, ny, qbb, dbb, k, dot_scale=float(dot_scale))
+        rv, ri, cv, ci, s = l2sq_scan(xx, yy, nxx, ny, qbb, dbb, k, dot_scale=float(dot_scale), exact=bool(exact))
     else:
         pert = _perturbation(x, y, perturbation)
         rv, ri, cv, ci, s = norm_scan(x, y, f, g, k, kind, perturbation=pert)
