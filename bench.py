@@ -610,7 +610,7 @@ def run_pairs(args, hb, dev, peaks):
     extra = {"dtype": "f32 in, f64 accumulate", "roofline": {
         "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-        "kernel": f"hb::pairs::pair_kernel_rows<3,{d // 128}>" if d in (128, 256, 512) else "hb::pairs::pair_kernel",
+        "kernel": f"hb::pairs::pair_kernel_ring<3,{d // 128}>" if d in (128, 256, 512) else "hb::pairs::pair_kernel",
         "bytes_per_edge": bytes_call / e,
         "note": "each source row once, each target row per edge (no target reuse on a random support)"},
         "random_order": {"value": e / sec_r / 1e9, "unit": "Gedges/s",

@@ -12,7 +12,10 @@
 // group reduces with a fixed xor-shuffle tree, so results are deterministic.
 // Each warp takes one contiguous block of edges, so the source row of edges
 // grouped by source (the reference's CSR-blocked order) is read from HBM once
-// and then from L1.  HBM-bound: every edge gathers its database row once.
+// and then from L1.  For d = 128, 256, 512 (pair_kernel_ring) a warp serves one
+// edge at a time from a ring of target rows in shared memory, filled ahead by
+// bulk copies, with the source row held in registers.  HBM-bound: every edge
+// gathers its database row once.
 #include <string>
 
 #include "common.cuh"
@@ -93,65 +96,81 @@ __global__ void __launch_bounds__(256) pair_kernel(const float* __restrict__ x, 
     }
 }
 
-// d = 128 NV with 16-byte-aligned rows: a warp per edge, lane l holding the float4 chunks
-// l + 32 v (v < NV) of the source row converted to fp64 in registers while consecutive edges
-// share the source row (the reference's source-grouped order), so each edge converts only
-// its target row.  The same chunks, order and reduction tree as pair_kernel<KIND, 32, true>:
-// the results are identical.
+// d = 128 NV with 16-byte-aligned rows, target rows through a shared-memory ring: each
+// warp keeps RING edges' target rows in flight as bulk copies (cp.async.bulk of the d-float
+// row, issued by lane 0, one mbarrier per slot), so a warp's loads need no registers; the
+// source row is held in registers as fp64 while the run of one source row lasts.  Same
+// chunks, order and reduction tree as pair_kernel<KIND, 32, true>: the results are identical.
+constexpr int RING = 4;  // slots per warp (deeper rings cost resident warps and measured slower)
+template <int NV>
+constexpr size_t ring_smem() { return (size_t)8 * RING * (NV * 512 + 8) + 16; }
+
 template <int KIND, int NV>
-__global__ void __launch_bounds__(256, NV <= 1 ? 4 : NV == 2 ? 3 : 2) pair_kernel_rows(const float* __restrict__ x, const float* __restrict__ y,
+__global__ void __launch_bounds__(256) pair_kernel_ring(const float* __restrict__ x, const float* __restrict__ y,
                                                         int64_t nx, int64_t ny, int d, const double* __restrict__ a,
                                                         const double* __restrict__ b, double scale,
                                                         const int64_t* __restrict__ rows,
                                                         const int64_t* __restrict__ cols, int64_t count,
                                                         double* __restrict__ out, int* status, const Perturb pert) {
-    const int lane = threadIdx.x & 31;
+    extern __shared__ __align__(128) unsigned char ring_buf[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4* slots = reinterpret_cast<float4*>(ring_buf) + (size_t)warp * RING * 32 * NV;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring_buf + (size_t)8 * RING * NV * 512) + warp * RING;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(ring_buf + (size_t)8 * RING * (NV * 512 + 8));
+    if (threadIdx.x == 0) *abort_flag = 0;
+    if (lane == 0) {
+        for (int j = 0; j < RING; ++j) mbar_init(&bars[j], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
     const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int64_t per_warp = (count + warps - 1) / warps;
-    const int64_t e_end = min(count, (warp_id + 1) * per_warp);
-    // one edge ahead: the next edge's indices, target row chunks and (when it starts a new
-    // source row) source row chunks are loaded before this edge's arithmetic
-    double xd[NV * 4];
-    float4 yv[NV], yn[NV], xn[NV];
-    int64_t e = warp_id * per_warp;
-    int64_t r = 0, c = 0, held = -1;
-    bool ok = false, fresh = false;  // fresh: xn holds this edge's source row (a new one)
-    auto fetch = [&](int64_t ee, int64_t prev, int64_t& rr, int64_t& cc, bool& okk, bool& fr) {
-        rr = rows[ee];
-        cc = cols[ee];
-        okk = rr >= 0 && rr < nx && cc >= 0 && cc < ny;
-        fr = okk && rr != prev;
-        if (okk) {
-            const float4* y4 = reinterpret_cast<const float4*>(y + cc * d);
-#pragma unroll
-            for (int v = 0; v < NV; ++v) yn[v] = __ldg(y4 + lane + 32 * v);
-        }
-        if (fr) {
-            const float4* x4 = reinterpret_cast<const float4*>(x + rr * d);
-#pragma unroll
-            for (int v = 0; v < NV; ++v) xn[v] = __ldg(x4 + lane + 32 * v);
+    const int64_t e0 = warp_id * per_warp, e1 = min(count, e0 + per_warp);
+    const uint32_t row_bytes = (uint32_t)d * 4u;
+    auto issue = [&](int64_t e) {  // lane 0: edge e's target row into slot (e - e0) % RING
+        const int slot = (int)((e - e0) % RING);
+        const int64_t c = cols[e], r = rows[e];
+        if (r >= 0 && r < nx && c >= 0 && c < ny) {
+            mbar_arrive_expect_tx(&bars[slot], row_bytes);
+            bulk_load_1d(slots + slot * 32 * NV, y + c * d, row_bytes, &bars[slot]);
+        } else {
+            mbar_arrive(&bars[slot]);  // nothing to copy: the phase completes at once
         }
     };
-    if (e < e_end) fetch(e, held, r, c, ok, fresh);
-    for (; e < e_end; ++e) {  // warp-uniform
-        if (fresh) {
-#pragma unroll
-            for (int v = 0; v < NV; ++v) {
-                xd[4 * v] = xn[v].x; xd[4 * v + 1] = xn[v].y; xd[4 * v + 2] = xn[v].z; xd[4 * v + 3] = xn[v].w;
-            }
-            held = r;
+    if (lane == 0)
+        for (int64_t e = e0; e < e1 && e < e0 + RING; ++e) issue(e);
+    int64_t held = -1;
+    double xd[NV * 4];
+    for (int64_t e = e0; e < e1; ++e) {  // warp-uniform
+        const int slot = (int)((e - e0) % RING);
+        const uint32_t par = (uint32_t)(((e - e0) / RING) & 1);
+        const int64_t r = rows[e], c = cols[e];
+        const bool ok = r >= 0 && r < nx && c >= 0 && c < ny;
+        if (!mbar_wait(&bars[slot], par, abort_flag, status)) {
+            // a copy never completed: give the copies in flight a bounded time, then leave
+            for (int64_t f = e + 1; f < e1 && f < e + RING; ++f)
+                for (int t = 0; t < 64 && !mbar_try_wait(&bars[(f - e0) % RING], (uint32_t)(((f - e0) / RING) & 1));
+                     ++t) {
+                }
+            return;
         }
-#pragma unroll
-        for (int v = 0; v < NV; ++v) yv[v] = yn[v];
-        const int64_t rc = r, cc = c;
-        const bool okc = ok;
-        if (e + 1 < e_end) fetch(e + 1, held, r, c, ok, fresh);
         double acc = 0.0;
-        if (okc) {
+        if (ok) {
+            if (r != held) {
+                const float4* x4 = reinterpret_cast<const float4*>(x + r * d);
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    const float4 u = __ldg(x4 + lane + 32 * v);
+                    xd[4 * v] = u.x; xd[4 * v + 1] = u.y; xd[4 * v + 2] = u.z; xd[4 * v + 3] = u.w;
+                }
+                held = r;
+            }
+            const float4* yr = slots + slot * 32 * NV;
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
-                const float yy[4] = {yv[v].x, yv[v].y, yv[v].z, yv[v].w};
+                const float4 yv = yr[lane + 32 * v];
+                const float yy[4] = {yv.x, yv.y, yv.z, yv.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const double xa = xd[4 * v + j], yb = (double)yy[j];
@@ -164,18 +183,20 @@ __global__ void __launch_bounds__(256, NV <= 1 ? 4 : NV == 2 ? 3 : 2) pair_kerne
                 }
             }
         }
+        __syncwarp();  // every lane is done with the slot
+        if (lane == 0 && e + RING < e1) issue(e + RING);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) acc = combine<KIND>(acc, __shfl_xor_sync(0xffffffffu, acc, off));
         if (lane == 0) {
-            if (!okc) {
+            if (!ok) {
                 atomicOr(status, kErrBadInput);
                 out[e] = __longlong_as_double(0x7ff8000000000000LL);
             } else if (KIND == 3) {
-                out[e] = (a[rc] + b[cc]) - scale * acc;
+                out[e] = (a[r] + b[c]) - scale * acc;
             } else {
                 const double dist = KIND == 2 ? sqrt(acc) : acc;
-                out[e] = pert.sigma != 0.0 ? dist + noise_of(pert, noise_input(pert, pert.row_index[rc]),
-                                                                noise_input(pert, pert.col_index[cc]))
+                out[e] = pert.sigma != 0.0 ? dist + noise_of(pert, noise_input(pert, pert.row_index[r]),
+                                                                noise_input(pert, pert.col_index[c]))
                                            : dist;
             }
         }
@@ -206,13 +227,15 @@ void launch_kind(const float* x, const float* y, int64_t nx, int64_t ny, int d, 
     const int64_t cap = (int64_t)sms * 16;
     const int blocks = (int)(want < 1 ? 1 : (want > cap ? cap : want));
     if (vec && (d == 128 || d == 256 || d == 512)) {
+        const size_t sm = d == 128 ? ring_smem<1>() : d == 256 ? ring_smem<2>() : ring_smem<4>();
+        auto kern = d == 128 ? pair_kernel_ring<KIND, 1> : d == 256 ? pair_kernel_ring<KIND, 2> : pair_kernel_ring<KIND, 4>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        int per = 4;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, sm);
+        const int64_t cap2 = (int64_t)sms * (per > 0 ? per : 1);
+        const int nb = (int)(want < 1 ? 1 : (want > cap2 ? cap2 : want));
         timing_mark(st);
-        if (d == 128)
-            pair_kernel_rows<KIND, 1><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
-        else if (d == 256)
-            pair_kernel_rows<KIND, 2><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
-        else
-            pair_kernel_rows<KIND, 4><<<blocks, 256, 0, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
+        kern<<<nb, 256, sm, st>>>(x, y, nx, ny, d, a, b, s, rows, cols, count, out, status, pert);
         timing_mark(st);
         count_launches(1);
         return;
