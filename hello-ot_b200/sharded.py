@@ -106,11 +106,26 @@ class ShardedPricingScan:
                                  passes=passes, exact=exact)
         self.local_scan = local_scan
         self.merge = merge or merge_topk
+        self.time_phases = False  # set True to time the local scan and the exchange of each call
+        self._marks = None
+
+    def last_phase_ms(self):
+        """(local scan ms, exchange and merge ms) of the last timed call (after a synchronize)."""
+        if not self._marks:
+            return None
+        m = self._marks
+        return m[0].elapsed_time(m[1]), m[1].elapsed_time(m[2])
 
     def scan(self, x_block, y, a_block, b, f_block, g, k: int, *, row_offset: int, theta: float = 0.0,
              gather_candidates: bool = True) -> ShardedScanResult:
         world, group = self.world, self.group
+        marks = None
+        if self.time_phases and x_block.is_cuda:  # CUDA events: local scan | exchange and merges
+            marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            marks[0].record()
         rv, ri, cv, ci, stats = self.local_scan(x_block, y, a_block, b, f_block - a_block, g - b, k)
+        if marks:
+            marks[1].record()
         ci = torch.where(ci >= 0, ci + int(row_offset), ci)
         # certificate
         sums = stats[[0, 1, 4]].contiguous()
@@ -158,6 +173,9 @@ class ShardedPricingScan:
                 d_match = ci_m[cmask].to(torch.int64)
                 rows = torch.cat((pairs[0], d_match))
                 cols = torch.cat((pairs[1], d_local.to(torch.int64)))
+        if marks:
+            marks[2].record()
+            self._marks = marks
         return ShardedScanResult(rows=rows, cols=cols, stats=total, col_vals=cv_m, col_idx=ci_m, row_vals=rv,
                                  row_idx=ri)
 
