@@ -343,7 +343,7 @@ def run_ours(args):
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu:  # before any GPU work, as the reference arm runs
         try:
-            csec, crows, cthreads, csample = reference_scan_sample(args, 1, 1)
+            csec, crows, cthreads, csample = reference_scan_sample(args, args.steps, args.warmup)
             cpu_baseline = {"value": crows * args.n / csec / 1e9, "unit": "Gpairs/s", "cores": cthreads,
                             "kind": "reference", "sample": csample}
         except Exception as exc:  # reference CPU build missing
