@@ -288,6 +288,29 @@ def reference_scan_sample(args, steps, warmup):
     return sec, rows, threads, sample
 
 
+def reference_arm_baseline(args):
+    """The repo arm's cpu_baseline: the reference arm itself (`--impl reference` with this run's
+    workload, warm-up and step counts) in a child process started before any GPU work, so the
+    two figures come from the same procedure in the same kind of process (timed inside this
+    process instead, the same sample ran up to 2.7x slower than in the reference arm's)."""
+    import subprocess
+    cmd = [sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", str(args.steps),
+           "--warmup", str(args.warmup), "--n", str(args.n), "--d", str(args.d), "--k", str(args.k),
+           "--cpu-seconds", str(args.cpu_seconds), "--precision", args.precision, "--exact", str(args.exact)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE")}
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+        line = [ln for ln in res.stdout.splitlines() if ln.startswith("{")][-1]
+        ref = json.loads(line)
+        if "unavailable" in ref:
+            raise RuntimeError(ref["unavailable"])
+        cb = dict(ref["cpu_baseline"])
+        cb["sample"] += "; the reference arm run as a child process before the GPU work"
+        return cb
+    except Exception as exc:  # reference CPU build missing, or the child failed
+        return {"value": None, "unit": "Gpairs/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {exc}"}
+
+
 # ------------------------------------------------------------------ main arms
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -341,14 +364,8 @@ def run_ours(args):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     cpu_baseline = None
-    if rank == 0 and world == 1 and not args.no_cpu:  # before any GPU work, as the reference arm runs
-        try:
-            csec, crows, cthreads, csample = reference_scan_sample(args, args.steps, args.warmup)
-            cpu_baseline = {"value": crows * args.n / csec / 1e9, "unit": "Gpairs/s", "cores": cthreads,
-                            "kind": "reference", "sample": csample}
-        except Exception as exc:  # reference CPU build missing
-            cpu_baseline = {"value": None, "unit": "Gpairs/s", "cores": 0, "kind": "reference",
-                            "sample": f"unavailable: {exc}"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu_baseline = reference_arm_baseline(args)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     import torch.distributed as dist
