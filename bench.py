@@ -83,6 +83,8 @@ def parse_args():
                    help="1 (default): the fp64 re-check of the l2sq lists (HB_L2SQ_EXACT); 0: fp32-class lists")
     p.add_argument("--passes", type=int, choices=[1, 2], default=None,
                    help="force a one-pass (k <= 8) or two-pass scan (default: the library's choice)")
+    p.add_argument("--ctas", type=int, choices=[1, 2], default=None,
+                   help="one-pass l2sq kernel: 2 = CTA pairs, 1 = single CTAs (default: the library's choice)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
@@ -378,7 +380,8 @@ def run_ours(args):
     if world > 1:  # the target cloud is replicated from rank 0 (once per solve)
         dist.broadcast(y, 0)
         dist.broadcast(b, 0)
-    sharded = ShardedPricingScan(precision=args.precision, passes=args.passes, exact=bool(args.exact))
+    sharded = ShardedPricingScan(precision=args.precision, passes=args.passes, exact=bool(args.exact),
+                                 ctas=args.ctas)
     g_step = g.clone()
 
     def step():

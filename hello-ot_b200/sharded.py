@@ -94,7 +94,7 @@ class ShardedPricingScan:
 
     def __init__(self, group=None, *, local_scan: Optional[Callable] = None, merge: Optional[Callable] = None,
                  dot_scale: float = 2.0, precision: str = "fp32", passes: Optional[int] = None,
-                 exact: bool = True):
+                 exact: bool = True, ctas: Optional[int] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -103,7 +103,7 @@ class ShardedPricingScan:
 
             def local_scan(x, y, a, b, qb, dbb, k):
                 return l2sq_scan(x, y, a, b, qb, dbb, k, dot_scale=dot_scale, precision=precision,
-                                 passes=passes, exact=exact)
+                                 passes=passes, exact=exact, ctas=ctas)
         self.local_scan = local_scan
         self.merge = merge or merge_topk
         self.time_phases = False  # set True to time the local scan and the exchange of each call
