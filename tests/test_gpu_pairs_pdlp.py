@@ -81,6 +81,27 @@ def test_pair_costs_edges_and_errors(hb, cuda):
         hb.pair_costs(0, x, y, torch.tensor([0, 1], device=cuda), torch.tensor([1, 12], device=cuda))
 
 
+@pytest.mark.parametrize("d", [128, 256, 512])
+def test_pair_costs_ring_bad_indices(hb, cuda, d):
+    """The ring kernel (d = 128, 256, 512) reports an out-of-range index inside a run of one
+    source row (no copy is issued for it, its slot still completes) and stays usable."""
+    x = torch.randn(40, d, device=cuda)
+    y = torch.randn(70, d, device=cuda)
+    rows = torch.arange(40, device=cuda).repeat_interleave(5)
+    cols = torch.randint(0, 70, (200,), device=cuda)
+    for bad_rows, bad_cols in ((None, 70), (-1, None)):
+        r, c = rows.clone(), cols.clone()
+        if bad_cols is not None:
+            c[37] = bad_cols
+        if bad_rows is not None:
+            r[101] = bad_rows
+        with pytest.raises(ValueError):
+            hb.pair_costs(0, x, y, r, c)
+    got = hb.pair_costs(0, x, y, rows, cols).cpu().numpy()
+    want = np.abs(x[rows].double() - y[cols].double()).sum(1).cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-13, atol=0)
+
+
 def _random_support(ns, nt, extra, seed):
     rng = np.random.default_rng(seed)
     rows = np.concatenate([np.arange(ns), rng.integers(0, ns, extra), rng.integers(0, ns, nt)])
