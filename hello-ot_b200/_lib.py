@@ -13,7 +13,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libhello_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 HB_OK, HB_BAD_ARGUMENT, HB_BAD_INPUT, HB_WORKSPACE = 0, 1, 2, 3
 HB_CUDA, HB_TENSOR_MAP, HB_LAUNCH, HB_DEVICE_TIMEOUT = 4, 5, 6, 7
@@ -39,7 +39,7 @@ class PdlpControls(ctypes.Structure):
     _fields_ = [("evaluation_frequency", c_int32), ("scalar_rescaling", c_int32), ("iteration_limit", c_int64),
                 ("time_limit_seconds", c_double), ("tol_objective", c_double), ("tol_primal", c_double),
                 ("tol_dual", c_double), ("initial_primal_weight", c_double), ("atomic_sums", c_int32),
-                ("pad", c_int32)]
+                ("termination_norm", c_int32)]
 
 
 class Perturbation(ctypes.Structure):
@@ -53,7 +53,9 @@ class PdlpInfo(ctypes.Structure):
                 ("primal_objective", c_double), ("dual_objective", c_double), ("abs_primal_residual", c_double),
                 ("rel_primal_residual", c_double), ("abs_dual_residual", c_double), ("rel_dual_residual", c_double),
                 ("rel_gap", c_double), ("primal_weight", c_double), ("cost_norm", c_double),
-                ("mass_norm", c_double), ("setup_seconds", c_double), ("iteration_seconds", c_double)]
+                ("mass_norm", c_double), ("setup_seconds", c_double), ("iteration_seconds", c_double),
+                ("l2_abs_primal_residual", c_double), ("l2_rel_primal_residual", c_double),
+                ("l2_abs_dual_residual", c_double), ("l2_rel_dual_residual", c_double)]
 
 
 class PdlpTraceRow(ctypes.Structure):

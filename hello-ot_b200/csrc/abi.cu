@@ -381,6 +381,9 @@ int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const doubl
         return fail(HB_BAD_ARGUMENT, "atomic_sums must be one of HB_PDLP_SUMS_ORDERED, _ATOMIC, _TREE");
     ctl.atomic = controls->atomic_sums == HB_PDLP_SUMS_ATOMIC;
     ctl.tree = controls->atomic_sums == HB_PDLP_SUMS_TREE;
+    if (controls->termination_norm != HB_PDLP_NORM_L2 && controls->termination_norm != HB_PDLP_NORM_LINF)
+        return fail(HB_BAD_ARGUMENT, "termination_norm must be HB_PDLP_NORM_L2 or HB_PDLP_NORM_LINF");
+    ctl.linf = controls->termination_norm == HB_PDLP_NORM_LINF;
     hb::PdlpResult r{};
     static_assert(sizeof(hb::TraceRow) == sizeof(hb_pdlp_trace_row), "trace row layout");
     int tlen = 0;
@@ -406,6 +409,10 @@ int hb_restricted_ot_solve(const int64_t* rows, const int64_t* cols, const doubl
     info->mass_norm = r.mass_norm;
     info->setup_seconds = r.setup_seconds;
     info->iteration_seconds = r.iteration_seconds;
+    info->l2_abs_primal_residual = r.ap2;
+    info->l2_rel_primal_residual = r.rp2;
+    info->l2_abs_dual_residual = r.ad2;
+    info->l2_rel_dual_residual = r.rd2;
     if (trace_length) *trace_length = tlen;
     g_error.clear();
     return HB_OK;

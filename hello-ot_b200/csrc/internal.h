@@ -84,11 +84,13 @@ struct PdlpControls {
     double weight0;  // > 0: initial primal weight instead of the norm ratio
     int atomic;      // node sums by atomics in the edge pass (order varies run to run)
     int tree;        // high-degree sides summed by a fixed lane tree (not the reference's order)
+    int linf = 0;    // termination test in the max norm (cuPDLPx termination_norm = "linf")
 };
 struct PdlpResult {
     int64_t iterations, restarts;
     int reason;  // 1 OPTIMAL, 2 ITERATION_LIMIT, 3 NUMERICAL_DIVERGENCE, 4 TIME_LIMIT
-    double pobj, dobj, ap, rp, ad, rd, gap, weight, cost_norm, mass_norm;
+    double pobj, dobj, ap, rp, ad, rd, gap, weight, cost_norm, mass_norm;  // termination norm
+    double ap2, rp2, ad2, rd2;  // L2 residuals
     double setup_seconds, iteration_seconds;
 };
 struct TraceRow { double iteration, pobj, dobj, rp, rd, gap, weight; };

@@ -143,6 +143,35 @@ __global__ void sumsq2_kernel(const double* a, int64_t na, const double* b, int6
     if (threadIdx.x == 0) { red[blockIdx.x * 8 + 0] = sh[0][0]; red[blockIdx.x * 8 + 1] = sh[1][0]; }
 }
 
+// Block-partial maxima of |a| (over na) and |b| (over nb) into red[b][0..1].
+__global__ void maxabs2_kernel(const double* a, int64_t na, const double* b, int64_t nb, double* red) {
+    __shared__ double sh[2][RED_THREADS];
+    double ma = 0, mb = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na; i += (int64_t)gridDim.x * blockDim.x) ma = fmax(ma, fabs(a[i]));
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb; i += (int64_t)gridDim.x * blockDim.x) mb = fmax(mb, fabs(b[i]));
+    sh[0][threadIdx.x] = ma; sh[1][threadIdx.x] = mb;
+    __syncthreads();
+    for (int w = RED_THREADS / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            sh[0][threadIdx.x] = fmax(sh[0][threadIdx.x], sh[0][threadIdx.x + w]);
+            sh[1][threadIdx.x] = fmax(sh[1][threadIdx.x], sh[1][threadIdx.x + w]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) { red[blockIdx.x * 8 + 0] = sh[0][0]; red[blockIdx.x * 8 + 1] = sh[1][0]; }
+}
+
+// Maximum of the block partials: scal[base + j] = max_b red[b][first + j], j < cnt.
+__global__ void finish_red_max(const double* red, int blocks, int first, int cnt, double* scal, int base) {
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < cnt; ++j) {
+            double s = 0;
+            for (int b = 0; b < blocks; ++b) s = fmax(s, red[b * 8 + first + j]);
+            scal[base + j] = s;
+        }
+    }
+}
+
 // Fixed-order sum of the block partials: scal[base + j] = sum_b red[b][j], j < cnt.
 __global__ void finish_red(const double* red, int blocks, int cnt, double* scal, int base) {
     if (threadIdx.x == 0) {
@@ -653,11 +682,13 @@ __device__ __forceinline__ void block_store(double (&v)[CNT], double* red) {
 
 // Residuals of the unscaled problem (solver.cpp:115-136):
 // [0] sum of squared marginal errors, [1] sum of squared dual violations,
-// [2] primal objective, [3] dual objective.
-__global__ void __launch_bounds__(RED_THREADS) evaluate_kernel(Dev D, double vb, double objective) {
+// [2] primal objective, [3] dual objective; with `linf`, also [4] the largest |marginal
+// error| and [5] the largest dual violation (the max-norm termination test).
+__global__ void __launch_bounds__(RED_THREADS) evaluate_kernel(Dev D, double vb, double objective, int linf) {
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     double v[4] = {0, 0, 0, 0};
+    double mx[2] = {0, 0};
     for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < D.nodes; i += warps) {
         const bool src = i < D.n;
         const int b0 = src ? D.s_off[i] : D.t_off[i - D.n], b1 = src ? D.s_off[i + 1] : D.t_off[i - D.n + 1];
@@ -671,6 +702,7 @@ __global__ void __launch_bounds__(RED_THREADS) evaluate_kernel(Dev D, double vb,
             const double delta = sum - D.mass[i];
             v[0] += delta * delta;
             v[3] += D.mass[i] * (D.py[i] / (D.scale[i] * objective));
+            mx[0] = fmax(mx[0], fabs(delta));
         }
     }
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -680,8 +712,22 @@ __global__ void __launch_bounds__(RED_THREADS) evaluate_kernel(Dev D, double vb,
         const double viol = max0(score);
         v[1] += viol * viol;
         v[2] += D.cost[p] * (D.px[p] / vb);
+        mx[1] = fmax(mx[1], viol);
     }
     block_store<4>(v, D.red);
+    if (linf) {  // block maxima into red[b][4..5] (block_store's last barrier is behind every thread)
+        __shared__ double shm[2][RED_THREADS];
+        shm[0][threadIdx.x] = mx[0]; shm[1][threadIdx.x] = mx[1];
+        __syncthreads();
+        for (int w = RED_THREADS / 2; w > 0; w >>= 1) {
+            if (threadIdx.x < w) {
+                shm[0][threadIdx.x] = fmax(shm[0][threadIdx.x], shm[0][threadIdx.x + w]);
+                shm[1][threadIdx.x] = fmax(shm[1][threadIdx.x], shm[1][threadIdx.x + w]);
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) { D.red[blockIdx.x * 8 + 4] = shm[0][0]; D.red[blockIdx.x * 8 + 5] = shm[1][0]; }
+    }
 }
 
 // Restart distances: [0] |px - ax|^2, [1] |py - ay|^2 (solver.cpp:203-213).
@@ -864,13 +910,19 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     HB_LAUNCHED(1);
     pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 2, D.scal, 0);
     HB_LAUNCHED(1);
+    if (ctl.linf) {  // max norms of b and c for the max-norm termination test (cupdlpx/solver.cu:920-954)
+        pdlp::maxabs2_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(masses, n + m, costs, e, D.red);
+        pdlp::finish_red_max<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 0, 2, D.scal, 14);
+        HB_LAUNCHED(2);
+    }
     if (cudaGetLastError() != cudaSuccess) return fail("setup");
-    cudaMemcpyAsync(h, D.scal, 2 * sizeof(double), cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(h, D.scal, 16 * sizeof(double), cudaMemcpyDeviceToHost, st);
     int status = 0;
     cudaMemcpyAsync(&status, D.status, sizeof(int), cudaMemcpyDeviceToHost, st);
     if (cudaStreamSynchronize(st) != cudaSuccess) return fail("setup sync");
     if (status & kErrBadInput) { err = "active-support endpoint index is out of bounds"; return 2; }
     const double mass_norm = std::sqrt(h[0]), cost_norm = std::sqrt(h[1]);
+    const double mass_inf = ctl.linf ? h[14] : 0.0, cost_inf = ctl.linf ? h[15] : 0.0;
     const double bound = ctl.rescale ? 1.0 / std::max(1.0, mass_norm) : 1.0;
     const double objective = ctl.rescale ? 1.0 / std::max(1.0, cost_norm) : 1.0;
     const double variable = std::sqrt(2.0);
@@ -897,6 +949,7 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     int64_t count = 0, inner = 0, restarts = 0;
     int reason = 0;
     double pobj = 0, dobj = 0, ap = 0, rp = 0, ad = 0, rd = 0, gap = 0;
+    double tap = 0, trp = 0, tad = 0, trd = 0;  // residuals of the termination test
     bool restart = false;
     int tlen = 0;
     const int F = ctl.frequency;
@@ -974,10 +1027,14 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         cudaGetLastError();  // a failed capture leaves the direct launches below
     }
     for (;;) {
-        pdlp::evaluate_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D, vb, objective);
+        pdlp::evaluate_kernel<<<pdlp::RED_BLOCKS, pdlp::RED_THREADS, 0, st>>>(D, vb, objective, ctl.linf ? 1 : 0);
         HB_LAUNCHED(1);
         pdlp::finish_red<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 4, D.scal, 0);
         HB_LAUNCHED(1);
+        if (ctl.linf) {
+            pdlp::finish_red_max<<<1, 32, 0, st>>>(D.red, pdlp::RED_BLOCKS, 4, 2, D.scal, 12);
+            HB_LAUNCHED(1);
+        }
         if (cudaGetLastError() != cudaSuccess) return fail("evaluate");
         cudaMemcpyAsync(h, D.scal, 16 * sizeof(double), cudaMemcpyDeviceToHost, st);
         if (cudaStreamSynchronize(st) != cudaSuccess) return fail("evaluate sync");
@@ -997,11 +1054,17 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         rp = ap / (1.0 + mass_norm);
         rd = ad / (1.0 + cost_norm);
         gap = std::abs(pobj - dobj) / (1.0 + std::abs(pobj) + std::abs(dobj));
-        if (trace && tlen < trace_cap) trace[tlen++] = {(double)count, pobj, dobj, rp, rd, gap, weight};
+        // the termination test's residuals: L2 (solver.cpp), or the max norm (cuPDLPx "linf")
+        tap = ctl.linf ? h[12] : ap;
+        tad = ctl.linf ? h[13] : ad;
+        trp = ctl.linf ? tap / (1.0 + mass_inf) : rp;
+        trd = ctl.linf ? tad / (1.0 + cost_inf) : rd;
+        if (trace && tlen < trace_cap) trace[tlen++] = {(double)count, pobj, dobj, trp, trd, gap, weight};
         const bool finite = std::isfinite(pobj) && std::isfinite(dobj) && std::isfinite(ap) && std::isfinite(rp) &&
-                            std::isfinite(ad) && std::isfinite(rd) && std::isfinite(gap);
+                            std::isfinite(ad) && std::isfinite(rd) && std::isfinite(gap) && std::isfinite(trp) &&
+                            std::isfinite(trd);
         if (!finite || !std::isfinite(weight)) reason = 3;
-        else if (rp < ctl.tol_primal && rd < ctl.tol_dual && gap < ctl.tol_objective) reason = 1;
+        else if (trp < ctl.tol_primal && trd < ctl.tol_dual && gap < ctl.tol_objective) reason = 1;
         else if (count >= ctl.iteration_limit) reason = 2;
         else if (std::chrono::duration<double>(Clock::now() - started).count() >= ctl.time_limit) reason = 4;
         if (reason) break;
@@ -1083,8 +1146,11 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     res->iterations = count;
     res->restarts = restarts;
     res->reason = reason;
-    res->pobj = pobj; res->dobj = dobj; res->ap = ap; res->rp = rp; res->ad = ad; res->rd = rd; res->gap = gap;
-    res->weight = weight; res->cost_norm = cost_norm; res->mass_norm = mass_norm;
+    res->pobj = pobj; res->dobj = dobj; res->ap = tap; res->rp = trp; res->ad = tad; res->rd = trd; res->gap = gap;
+    res->ap2 = ap; res->rp2 = rp; res->ad2 = ad; res->rd2 = rd;
+    res->weight = weight;
+    res->cost_norm = ctl.linf ? cost_inf : cost_norm;
+    res->mass_norm = ctl.linf ? mass_inf : mass_norm;
     res->setup_seconds = setup_seconds;
     res->iteration_seconds = std::chrono::duration<double>(Clock::now() - iter_started).count();
     if (trace_len) *trace_len = tlen;

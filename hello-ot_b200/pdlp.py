@@ -21,6 +21,7 @@ from ._lib import PdlpControls, PdlpInfo, PdlpTraceRow, Workspace, check, lib, p
 
 REASONS = {1: "OPTIMAL", 2: "ITERATION_LIMIT", 3: "NUMERICAL_DIVERGENCE", 4: "TIME_LIMIT"}
 SUMMATION = {"ordered": 0, "atomic": 1, "tree": 2}  # hb_pdlp_controls.atomic_sums (HB_PDLP_SUMS_*)
+TERMINATION_NORMS = {"l2": 0, "linf": 1}  # hb_pdlp_controls.termination_norm (HB_PDLP_NORM_*)
 
 
 @dataclass
@@ -53,14 +54,19 @@ class NativeRestrictedOTPDLP:
 
     def __init__(self, *, device="cuda", evaluation_frequency: int = 200, time_limit_seconds: float = 3600.0,
                  iteration_limit: int = np.iinfo(np.int32).max, record_state_trace: bool = False,
-                 initial_primal_weight: float = 0.0, deterministic: bool = True, summation: str = None):
+                 initial_primal_weight: float = 0.0, deterministic: bool = True, summation: str = None,
+                 termination_norm: str = "l2"):
         """summation (node sums of the primal): "ordered" (the default) adds each node's
         edges in the reference's order, bit-identical to it; "atomic" (also chosen by
         deterministic=False) accumulates with atomics in the edge pass, about 1.5x faster
         per iteration on large random supports, but the order (so the last bits of the
         iterates) varies from run to run; "tree" is "ordered" except on a side whose mean
         degree is >= 64 (a dense support), where a fixed lane tree adds each node's edges:
-        reproducible run to run, not the reference's order, several times faster there."""
+        reproducible run to run, not the reference's order, several times faster there.
+        termination_norm: "l2" (solver.cpp's test) or "linf" (the native engine's
+        termination_norm = "linf", cupdlpx/utils.cu:1027-1041: primal and dual residuals in
+        the max norm relative to 1 + ||b||_inf and 1 + ||c||_inf; restarts and the primal
+        weight stay on the L2 residuals)."""
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("NativeRestrictedOTPDLP runs on CUDA devices only")
@@ -77,6 +83,9 @@ class NativeRestrictedOTPDLP:
             raise ValueError(f"summation must be one of {sorted(SUMMATION)}")
         self.summation = summation
         self.deterministic = summation != "atomic"
+        if termination_norm not in TERMINATION_NORMS:
+            raise ValueError("termination_norm must be one of: l2, linf")
+        self.termination_norm = termination_norm
         if self.evaluation_frequency < 1:
             raise ValueError("evaluation_frequency must be >= 1")
         if self.time_limit_seconds <= 0.0 or self.iteration_limit < 1:
@@ -132,7 +141,8 @@ class NativeRestrictedOTPDLP:
         y_out = torch.empty(n + m, dtype=torch.float64, device=dev)
         ctl = PdlpControls(self.evaluation_frequency, int(bool(scalar_rescaling)), self.iteration_limit,
                            self.time_limit_seconds, objective_tolerance, primal_tolerance, dual_tolerance,
-                           self.initial_primal_weight, SUMMATION[self.summation], 0)
+                           self.initial_primal_weight, SUMMATION[self.summation],
+                           TERMINATION_NORMS[self.termination_norm])
         info = PdlpInfo()
         cap = 4096 if self.record_state_trace else 0
         trace = (PdlpTraceRow * max(cap, 1))()
@@ -149,17 +159,17 @@ class NativeRestrictedOTPDLP:
         diag = {
             "backend": "hello_b200_pdhg", "device": str(dev), "dtype": "float64",
             "scaling_mode": "degree_sqrt" + ("_with_scalar_retry" if scalar_rescaling else ""),
-            "step_size": 0.998, "termination_norm": "l2",
+            "step_size": 0.998, "termination_norm": self.termination_norm,
             "termination_abs_primal_res": info.abs_primal_residual,
             "termination_rel_primal_res": info.rel_primal_residual,
             "termination_abs_dual_res": info.abs_dual_residual,
             "termination_rel_dual_res": info.rel_dual_residual,
             "termination_objective_vector_norm": info.cost_norm,
             "termination_constraint_bound_norm": info.mass_norm,
-            "algorithm_abs_primal_res_l2": info.abs_primal_residual,
-            "algorithm_rel_primal_res_l2": info.rel_primal_residual,
-            "algorithm_abs_dual_res_l2": info.abs_dual_residual,
-            "algorithm_rel_dual_res_l2": info.rel_dual_residual,
+            "algorithm_abs_primal_res_l2": info.l2_abs_primal_residual,
+            "algorithm_rel_primal_res_l2": info.l2_rel_primal_residual,
+            "algorithm_abs_dual_res_l2": info.l2_abs_dual_residual,
+            "algorithm_rel_dual_res_l2": info.l2_rel_dual_residual,
             "relative_primal_dual_gap": info.rel_gap, "primal_weight": info.primal_weight,
             "restart_count": int(info.restarts), "runtime_sec": duration,
             "setup_time_sec": info.setup_seconds, "iteration_time_sec": info.iteration_seconds,

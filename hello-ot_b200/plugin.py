@@ -269,7 +269,8 @@ def install(hello_ot=None, *, device=None):
         if config.solver_engine == "cupdlpx":
             _count("lp:engine")
             dev = lp_device if lp_device is not None else torch.device("cuda", torch.cuda.current_device())
-            return B200RestrictedOTPDLP(device=dev)
+            return B200RestrictedOTPDLP(device=dev,
+                                        termination_norm=str(getattr(config, "lp_termination_norm", "l2")))
         return original_build(config)
 
     _rebind(root, original_build, build_lp_backend, undo)

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define HB_ABI_VERSION 1
+#define HB_ABI_VERSION 2
 
 enum {
     HB_OK = 0,
@@ -280,10 +280,17 @@ typedef struct hb_pdlp_controls {
                                         >= 64 (a dense support, e.g. a coarsest level) sums each node
                                         in a fixed lane-strided tree: bit-reproducible run to run,
                                         not the reference's order, several times faster there */
-    int32_t pad;
+    int32_t termination_norm;      /* norm of the termination test, one of HB_PDLP_NORM_*:
+                                      L2 (0): solver.cpp's, ||Ax - b||_2 / (1 + ||b||_2) and
+                                        ||(A^T y - c)_+||_2 / (1 + ||c||_2);
+                                      LINF (1): cuPDLPx's termination_norm = "linf"
+                                        (cupdlpx/utils.cu:1027-1041): the same residuals in the
+                                        max norm over (1 + ||b||_inf), (1 + ||c||_inf); restarts and
+                                        the primal weight stay on the L2 residuals */
 } hb_pdlp_controls;
 
 enum { HB_PDLP_SUMS_ORDERED = 0, HB_PDLP_SUMS_ATOMIC = 1, HB_PDLP_SUMS_TREE = 2 };
+enum { HB_PDLP_NORM_L2 = 0, HB_PDLP_NORM_LINF = 1 };
 
 enum { HB_PDLP_OPTIMAL = 1, HB_PDLP_ITERATION_LIMIT = 2, HB_PDLP_NUMERICAL_DIVERGENCE = 3, HB_PDLP_TIME_LIMIT = 4 };
 
@@ -291,9 +298,12 @@ typedef struct hb_pdlp_info {
     int64_t iterations, restarts;
     int32_t termination, pad;
     double primal_objective, dual_objective;
+    /* residuals in the termination norm, and the norms of c and b they are relative to */
     double abs_primal_residual, rel_primal_residual, abs_dual_residual, rel_dual_residual, rel_gap;
     double primal_weight, cost_norm, mass_norm;
     double setup_seconds, iteration_seconds;
+    /* the L2 residuals (the restart and weight rules use these in either norm) */
+    double l2_abs_primal_residual, l2_rel_primal_residual, l2_abs_dual_residual, l2_rel_dual_residual;
 } hb_pdlp_info;
 
 typedef struct hb_pdlp_trace_row {

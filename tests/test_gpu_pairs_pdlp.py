@@ -98,7 +98,7 @@ def test_pair_costs_ring_bad_indices(hb, cuda, d):
         with pytest.raises(ValueError):
             hb.pair_costs(0, x, y, r, c)
     got = hb.pair_costs(0, x, y, rows, cols).cpu().numpy()
-    want = np.abs(x[rows].double() - y[cols].double()).sum(1).cpu().numpy()
+    want = (x[rows].double() - y[cols].double()).abs().sum(1).cpu().numpy()
     np.testing.assert_allclose(got, want, rtol=1e-13, atol=0)
 
 
@@ -150,6 +150,38 @@ def test_pdlp_converges_like_oracle(hb, cuda, oracle, shape):
     assert got.obj_val == pytest.approx(ref["obj_val"], rel=1e-6)
     assert got.primal_feas < 1e-7 and got.dual_feas < 1e-7 and got.gap < 1e-7
     assert abs(got.iterations - ref["iterations"]) <= 2 * 200
+
+
+@pytest.mark.parametrize("shape", [(300, 400, 4000), (1000, 700, 20000)])
+def test_pdlp_linf_termination(hb, cuda, shape):
+    """termination_norm="linf" (the native engine's cuPDLPx rule): at termination the
+    reported residuals are the max-norm residuals of the returned iterate relative to
+    1 + ||b||_inf and 1 + ||c||_inf, below the tolerance; the L2 ones are reported beside."""
+    rows, cols, c, a, b = _random_support(*shape, seed=shape[0] + 1)
+    n, m = len(a), len(b)
+    tol = 1e-7
+    res = {}
+    for norm in ("l2", "linf"):
+        solver = hb.NativeRestrictedOTPDLP(device=cuda, termination_norm=norm)
+        res[norm] = solver.solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b,
+                                            tolerance=tol)
+        assert res[norm].termination_reason == "OPTIMAL"
+        assert res[norm].solver_diag["termination_norm"] == norm
+    r = res["linf"]
+    x, y = r.x.cpu().numpy(), r.y.cpu().numpy()
+    masses = np.concatenate((a, b))
+    sums = np.concatenate((np.bincount(rows, x, minlength=n), np.bincount(cols, x, minlength=m)))
+    primal = np.abs(sums - masses).max() / (1.0 + np.abs(masses).max())
+    dual = np.maximum(y[rows] + y[n + cols] - c, 0.0).max() / (1.0 + np.abs(c).max())
+    assert r.primal_feas == pytest.approx(primal, rel=1e-9, abs=1e-16) and r.primal_feas < tol
+    assert r.dual_feas == pytest.approx(dual, rel=1e-9, abs=1e-16) and r.dual_feas < tol
+    d = r.solver_diag
+    assert d["termination_rel_primal_res"] == r.primal_feas
+    l2p = np.sqrt(((sums - masses) ** 2).sum()) / (1.0 + np.sqrt((masses ** 2).sum()))
+    assert d["algorithm_rel_primal_res_l2"] == pytest.approx(l2p, rel=1e-9, abs=1e-16)
+    assert r.obj_val == pytest.approx(res["l2"].obj_val, rel=1e-6)
+    with pytest.raises(ValueError):
+        hb.NativeRestrictedOTPDLP(device=cuda, termination_norm="l1")
 
 
 @pytest.mark.parametrize("shape", [(30, 40, 180), (1000, 700, 20000), (3000, 2500, 60000)])

@@ -24,7 +24,7 @@ def test_library_exports_every_declared_symbol(hb):
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in hello_b200.h but not exported"
     assert declared == set(hb._lib.EXPORTS)
-    assert lib.hb_abi_version() == 1
+    assert lib.hb_abi_version() == hb._lib.ABI_VERSION == 2
 
 
 def test_header_cites_reference_interfaces():
@@ -119,13 +119,19 @@ def test_python_flags_match_the_header(hb):
     another pass mode, CTA layout or node-sum order)."""
     header = (REPO / "include" / "hello_b200.h").read_text()
     defs = {m.group(1): int(m.group(2), 0) for m in re.finditer(r"#define (HB_\w+) (0x[0-9a-fA-F]+|\d+)\b", header)}
-    enums = {m.group(1): int(m.group(2)) for m in re.finditer(r"(HB_PDLP_SUMS_\w+) = (\d+)", header)}
+    enums = {m.group(1): int(m.group(2)) for m in re.finditer(r"(HB_PDLP_(?:SUMS|NORM)_\w+) = (\d+)", header)}
     scan = hb.scan
     assert scan.L2SQ_PASS_FLAGS[2] == defs["HB_L2SQ_TWO_PASS"] and scan.L2SQ_PASS_FLAGS[1] == defs["HB_L2SQ_ONE_PASS"]
     assert scan.L2SQ_CTA_FLAGS[2] == defs["HB_L2SQ_CTA_PAIRS"] and scan.L2SQ_CTA_FLAGS[1] == defs["HB_L2SQ_SINGLE_CTA"]
     assert scan.NORM_TWO_PASS == defs["HB_NORM_TWO_PASS"]
     assert hb.pdlp.SUMMATION == {"ordered": enums["HB_PDLP_SUMS_ORDERED"], "atomic": enums["HB_PDLP_SUMS_ATOMIC"],
                                  "tree": enums["HB_PDLP_SUMS_TREE"]}
+    assert hb.pdlp.TERMINATION_NORMS == {"l2": enums["HB_PDLP_NORM_L2"], "linf": enums["HB_PDLP_NORM_LINF"]}
+    # the ctypes structures carry the header's fields in its order
+    from hello_ot_b200._lib import PdlpControls, PdlpInfo
+    assert [f[0] for f in PdlpControls._fields_][-2:] == ["atomic_sums", "termination_norm"]
+    assert [f[0] for f in PdlpInfo._fields_][-4:] == ["l2_abs_primal_residual", "l2_rel_primal_residual",
+                                                       "l2_abs_dual_residual", "l2_rel_dual_residual"]
 
 
 def test_generic_scan_validates_before_launch(hb):
