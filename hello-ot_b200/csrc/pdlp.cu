@@ -408,8 +408,9 @@ __global__ void __launch_bounds__(256) node_pass_wide(Dev D, int it, int src_blo
 
 // Fused passes (the default for sparse supports): one launch per iteration.  The edge state
 // is kept twice, in source order (x, ax, cs) and in target order (tx, tax, tcs), so each side
-// reads its nodes' edges contiguously.  Tiles are FP_NODES consecutive nodes of one side
-// (node v at place v % FP_NODES, one per thread).  A persistent block owns a run of
+// reads its nodes' edges contiguously.  Tiles are C::TN consecutive nodes of one side (node v
+// at place v % C::TN, owned by thread v % C::TN; 256 per tile, or 64 on small supports so
+// that every block has a tile).  A persistent block of FP_THREADS threads owns a run of
 // consecutive tiles of one side, the runs balanced by edges, and streams the run's edge
 // state through a ring of C::ST shared-memory stages of C::CH edges, filled by bulk copies
 // (cp.async.bulk issued by one thread, completion on one mbarrier per stage).  Per stage:
@@ -422,16 +423,17 @@ __global__ void __launch_bounds__(256) node_pass_wide(Dev D, int it, int src_blo
 // end.  The edge updates read the node scales of buffer `parity` and the dual updates write
 // the other buffer, so the source and target sides run side by side in one launch.  The
 // source side also writes px / dx, which the evaluation and restart kernels read.
-constexpr int FP_NODES = 256;      // nodes per tile = threads per block
+constexpr int FP_THREADS = 256;    // threads per block
 constexpr int FP_MAX_RUNS = 4096;  // blocks per side, at most
 
-template <int CH_, int ST_, int BPS_, bool CG_ = false>
+template <int CH_, int ST_, int BPS_, bool CG_ = false, int TN_ = 256>
 struct FpCfg {
+    static constexpr int TN = TN_;    // nodes per tile (divides 256: the lane byte is node % 256)
     static constexpr int CH = CH_;    // edges per stage
     static constexpr int ST = ST_;    // stages
     static constexpr int BPS = BPS_;  // blocks per SM
     static constexpr bool CG = CG_;   // node-scale gathers cached in L2 only
-    static constexpr int PER = CH / FP_NODES;  // edges per thread in one stage
+    static constexpr int PER = CH / FP_THREADS;  // edges per thread in one stage
 };
 
 template <class C>
@@ -460,8 +462,9 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
     const unsigned char* LN = TGT ? D.t_lane : D.e_lane;    // the own endpoint's place in its tile
     const double* ownb = (TGT ? D.tdb : D.sdb)[s.parity];
     const double* other = TGT ? D.sdb[s.parity] : D.tdb[s.parity];
-    auto tile_end = [&](int tl) { return off[min(tl * FP_NODES + FP_NODES, nodes)]; };
-    const int E0 = off[tb * FP_NODES], E1 = tile_end(te - 1);
+    constexpr int TN = C::TN;
+    auto tile_end = [&](int tl) { return off[min(tl * TN + TN, nodes)]; };
+    const int E0 = off[tb * TN], E1 = tile_end(te - 1);
     const int nch = (E1 - E0 + CH - 1) / CH;
     auto issue = [&](int k) {  // one thread: the bulk copies of chunk k into stage k % ST
         const int c0 = E0 + k * CH, c1 = min(E1, c0 + CH);
@@ -494,7 +497,7 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
         }
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
-            const int q = c0 + j * FP_NODES + t;
+            const int q = c0 + j * FP_THREADS + t;
             o[j] = m[j] = 0.0;
             if (q < c1) {
                 int tl = q < gT1 ? gt : gt + 1;
@@ -502,16 +505,16 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
                     int lo = gt + 2, hi = te - 1;
                     while (lo < hi) {
                         const int mid = (lo + hi + 1) >> 1;
-                        if (off[mid * FP_NODES] <= q) lo = mid; else hi = mid - 1;
+                        if (off[mid * TN] <= q) lo = mid; else hi = mid - 1;
                     }
                     tl = lo;
                 }
                 if (C::CG) {
                     o[j] = __ldcg(other + S.o[q - i0]);
-                    m[j] = __ldcg(ownb + tl * FP_NODES + S.ln[q - lb0]);
+                    m[j] = __ldcg(ownb + tl * TN + (S.ln[q - lb0] & (TN - 1)));
                 } else {
                     o[j] = __ldg(other + S.o[q - i0]);
-                    m[j] = __ldg(ownb + tl * FP_NODES + S.ln[q - lb0]);
+                    m[j] = __ldg(ownb + tl * TN + (S.ln[q - lb0] & (TN - 1)));
                 }
             }
         }
@@ -524,13 +527,15 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
     };
     // sum cursor: this thread's node of tile `tile`, its edge range, its state; the next
     // tile's offsets are loaded one tile ahead
-    int tile = tb, v = tb * FP_NODES + t;
+    // threads t >= TN own no node (v = nodes: empty segment, no dual update)
+    auto node_of = [&](int tl) { return t < TN ? min(tl * TN + t, nodes) : nodes; };
+    int tile = tb, v = node_of(tb);
     int T1 = gT1;
     int b0 = v < nodes ? off[v] : T1, b1 = v < nodes ? off[v + 1] : T1;
     int nT1 = 0, nb0 = 0, nb1 = 0;
     auto prefetch_next = [&]() {
         if (tile + 1 >= te) return;
-        const int nv = (tile + 1) * FP_NODES + t;
+        const int nv = node_of(tile + 1);
         nT1 = tile_end(tile + 1);
         nb0 = nv < nodes ? off[nv] : nT1;
         nb1 = nv < nodes ? off[nv + 1] : nT1;
@@ -556,7 +561,7 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
         }
         sum = 0.0;
         if (++tile >= te) return false;
-        v = tile * FP_NODES + t;
+        v = node_of(tile);
         T1 = nT1; b0 = nb0; b1 = nb1;
         prefetch_next();
         node_state();
@@ -570,7 +575,7 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
         double* rs = sh.rs[k & 1];
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
-            const int q = c0 + j * FP_NODES + t;
+            const int q = c0 + j * FP_THREADS + t;
             if (q >= c1) continue;
             const double xv = S.x[q - d0];
             const double at = TGT ? o[j] + m[j] : m[j] + o[j];  // sd[row] + td[col]
@@ -604,7 +609,7 @@ __device__ __forceinline__ void fp_side(const Dev& D, const Step& s, int tb, int
 // Blocks [0, runs) take source runs, [runs, 2 runs) target runs; run r of a side covers the
 // tiles [part[r], part[r + 1]).
 template <class C>
-__global__ void __launch_bounds__(FP_NODES, C::BPS) fused_pass(Dev D, int it, int runs) {
+__global__ void __launch_bounds__(FP_THREADS, C::BPS) fused_pass(Dev D, int it, int runs) {
     extern __shared__ __align__(128) unsigned char fp_smem[];
     FpShared<C>& sh = *reinterpret_cast<FpShared<C>*>(fp_smem);
     const bool target = (int)blockIdx.x >= runs;
@@ -625,20 +630,20 @@ __global__ void __launch_bounds__(FP_NODES, C::BPS) fused_pass(Dev D, int it, in
 
 // Tile runs balanced by edges: part[r] = the first tile whose first edge is at or after
 // r * E / runs, part[runs] = all tiles; sources at fp_part, targets at fp_part + FP_MAX_RUNS + 1.
-__global__ void fp_partition(Dev D, int runs) {
+__global__ void fp_partition(Dev D, int runs, int tn) {
     for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < 2 * (runs + 1); u += gridDim.x * blockDim.x) {
         const bool target = u > runs;
         const int r = target ? u - runs - 1 : u;
         const int nodes = target ? D.m : D.n;
         const int* off = target ? D.t_off : D.s_off;
-        const int tiles = (nodes + FP_NODES - 1) / FP_NODES;
+        const int tiles = (nodes + tn - 1) / tn;
         int res = tiles;
         if (r < runs) {
             const int64_t want = D.e * (int64_t)r / runs;
-            int lo = 0, hi = tiles;  // first tile with off[FP_NODES tile] >= want
+            int lo = 0, hi = tiles;  // first tile with off[tn tile] >= want
             while (lo < hi) {
                 const int mid = (lo + hi) >> 1;
-                if (off[mid * FP_NODES] < want) lo = mid + 1; else hi = mid;
+                if (off[mid * tn] < want) lo = mid + 1; else hi = mid;
             }
             res = lo;
         }
@@ -961,9 +966,15 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     // stages of 512 edges, two per block (a third stage measured slower, 489 against 394 us per
     // iteration at E = 21M, also with the grid sized to its occupancy), node-scale gathers cached
     // in L2 only
-    using FpDefault = pdlp::FpCfg<512, 2, 4, true>;
-    void (*fp_kernel)(pdlp::Dev, int, int) = pdlp::fused_pass<FpDefault>;
-    const size_t fp_bytes = sizeof(pdlp::FpShared<FpDefault>);
+    using FpBig = pdlp::FpCfg<512, 2, 4, true, 256>;
+    using FpSmall = pdlp::FpCfg<512, 2, 4, true, 64>;
+    // 64-node tiles below about four 256-node tiles per block and side (19.3 against 29.6 us per
+    // iteration at n = m = 32768, equal at 131072 and 262144, 256-node tiles 7% faster at 2^20)
+    const bool small_tiles = std::max(n, m) < (int64_t)4 * 256 * sms * FpBig::BPS / 2;
+    const int fp_tn = small_tiles ? FpSmall::TN : FpBig::TN;
+    void (*fp_kernel)(pdlp::Dev, int, int) = small_tiles ? pdlp::fused_pass<FpSmall> : pdlp::fused_pass<FpBig>;
+    const size_t fp_bytes = small_tiles ? sizeof(pdlp::FpShared<FpSmall>) : sizeof(pdlp::FpShared<FpBig>);
+    using FpDefault = FpBig;
     int fp_per_sm = FpDefault::BPS;  // resident blocks per SM: one wave of persistent blocks
     int runs = 1;
     int parity = 0;  // fused passes: the node-scale buffer the next iteration reads
@@ -971,18 +982,18 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
         if (cudaFuncSetAttribute(fp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fp_bytes) != cudaSuccess)
             return fail("fused pass shared memory");
         int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fp_kernel, pdlp::FP_NODES, fp_bytes) == cudaSuccess &&
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fp_kernel, pdlp::FP_THREADS, fp_bytes) == cudaSuccess &&
             occ > 0)
             fp_per_sm = occ;
         runs = std::max(1, std::min(sms * fp_per_sm / 2, pdlp::FP_MAX_RUNS));
         pdlp::target_copy<<<gb, 256, 0, st>>>(D, 1);
-        pdlp::fp_partition<<<(2 * runs + 257) / 256, 256, 0, st>>>(D, runs);
+        pdlp::fp_partition<<<(2 * runs + 257) / 256, 256, 0, st>>>(D, runs, fp_tn);
         HB_LAUNCHED(2);
     }
     // One iteration: the three kernels reading D.steps[it].
     auto launch_iteration = [&](cudaStream_t s_, int it, bool counted) {
         if (fused) {
-            fp_kernel<<<(unsigned)(2 * runs), pdlp::FP_NODES, fp_bytes, s_>>>(D, it, runs);
+            fp_kernel<<<(unsigned)(2 * runs), pdlp::FP_THREADS, fp_bytes, s_>>>(D, it, runs);
         } else if (ctl.atomic) {
             pdlp::edge_pass<true><<<gb, 256, 0, s_>>>(D, it);
             pdlp::source_pass<true><<<(unsigned)((n + 255) / 256), 256, 0, s_>>>(D, it);

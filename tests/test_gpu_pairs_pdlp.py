@@ -184,6 +184,20 @@ def test_pdlp_linf_termination(hb, cuda, shape):
         hb.NativeRestrictedOTPDLP(device=cuda, termination_norm="l1")
 
 
+def test_pdlp_block_is_bit_exact_large_tiles(hb, cuda, oracle):
+    """Above about 300k nodes per side the fused pass takes 256-node tiles (64 below, which
+    the smaller cases cover): one block of iterations is bit-exact there as well."""
+    rows, cols, c, a, b = _random_support(320000, 310000, 1_200_000, seed=9)
+    F = 20
+    ref = oracle.pdlp(rows, cols, c, a, b, frequency=F, iteration_limit=F, tolerance=0.0)
+    solver = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=F, iteration_limit=F,
+                                       initial_primal_weight=ref["primal_weight"])
+    got = solver.solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=0.0)
+    assert got.iterations == ref["iterations"] == F
+    assert np.array_equal(got.x.cpu().numpy(), ref["x"])
+    assert np.array_equal(got.y.cpu().numpy(), ref["y"])
+
+
 @pytest.mark.parametrize("shape", [(30, 40, 180), (1000, 700, 20000), (3000, 2500, 60000)])
 def test_pdlp_atomic_sums_converge_like_oracle(hb, cuda, oracle, shape):
     """Atomic node sums change the summation order (so the last bits) but not the solve:
