@@ -58,7 +58,7 @@ class NativeRestrictedOTPDLP:
                  termination_norm: str = "l2"):
         """summation (node sums of the primal): "ordered" (the default) adds each node's
         edges in the reference's order, bit-identical to it; "atomic" (also chosen by
-        deterministic=False) accumulates with atomics in the edge pass, about 1.5x faster
+        deterministic=False) accumulates with atomics in the edge pass, about 1.2x faster
         per iteration on large random supports, but the order (so the last bits of the
         iterates) varies from run to run; "tree" is "ordered" except on a side whose mean
         degree is >= 64 (a dense support), where a fixed lane tree adds each node's edges:
