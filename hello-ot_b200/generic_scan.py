@@ -25,11 +25,14 @@ from .scan import _check, l2sq_scan, l2sq_topk, norm_scan, norm_topk
 _ROUTES = Counter()  # route diagnostics, incremented by callers as in the reference
 
 
-def _precision(compute_precision, raw, x):
+def _precision(compute_precision, raw, x, fp64_lists=False):
+    """compute_precision 1 (fp64) is served only where the lists can be the exact fp64 top-k
+    of fp32 coordinates (raw bidirectional scans, fp64_lists=True: the fp64 re-check)."""
     if compute_precision not in (0, 1) or (not raw and x.dtype != torch.float32):
         raise ValueError("norm scans require FP32 coordinate storage and precision 0 or 1")
-    if compute_precision == 1 or x.dtype != torch.float32:
-        raise NotImplementedError("hello_ot_b200 scans compute from fp32 coordinates (compute_precision=0)")
+    if x.dtype != torch.float32 or (compute_precision == 1 and not (raw and fp64_lists)):
+        raise NotImplementedError("hello_ot_b200 scans compute from fp32 coordinates (compute_precision=0; "
+                                  "compute_precision=1 only for raw bidirectional scans, as exact fp64 lists)")
 
 
 def _perturbation(x, y, args):
@@ -66,10 +69,12 @@ def bidirectional(x, y, f, g, k, kind, *, raw_costs=None, raw_biases=None, dot_s
     row and column top-k of the scores and the full certificate (generic_scan.py:328-404).
     kind 3 (raw l2^2) takes raw_costs = (nx, ny) and raw_biases = (f - nx, g - ny); its lists
     are the exact fp64 top-k (the fp64 re-check, as ScanExtension's default) unless
-    exact=False."""
+    exact=False; compute_precision=1 (fp64) asks for them in any case."""
     _check(x, y, k, (f, len(x)), (g, len(y)))
     raw = raw_costs is not None
-    _precision(compute_precision, raw, x)
+    _precision(compute_precision, raw, x, fp64_lists=True)
+    if compute_precision == 1:
+        exact = True
     if raw and perturbation is not None and float(perturbation[2]) != 0:
         raise ValueError("norm perturbation does not apply to raw pricing")
     if kind not in (0, 1, 2, 3) or (kind == 3 and not raw):

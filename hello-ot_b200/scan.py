@@ -357,6 +357,20 @@ def _to_device(a, device, dtype):
     return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype).to(device, non_blocking=True).contiguous()
 
 
+def _holds_fp32(feat) -> bool:
+    """True when every element of feat is an fp32 value (fp32 storage, or fp64 values that
+    round-trip through fp32 exactly)."""
+    if torch.is_tensor(feat):
+        if feat.dtype == torch.float32:
+            return True
+        v = feat.detach()
+        return bool(torch.equal(v.to(torch.float32).to(v.dtype), v))
+    arr = np.asarray(feat)
+    if arr.dtype == np.float32:
+        return True
+    return bool(np.array_equal(arr.astype(np.float32).astype(arr.dtype), arr))
+
+
 def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_cost, target_cost, source_dual,
                                                target_dual, *, topk, theta=0.0, gpu_id=0, memory_floor_mib=768.0,
                                                resident_multiplier=1.10, col_reduce_tile=256, col_kernel="auto",
@@ -368,16 +382,25 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
     Score of pair (i, j): (s<x_i,y_j> + (f_i - a_i)) + (g_j - b_j); candidates are the
     top-k of every source row and every target column with score > theta.  exact (the
     default): the lists are the exact fp64 top-k (the fp64 re-check, HB_L2SQ_EXACT);
-    exact=False keeps the fp32-class ranking of the tensor-core dot."""
+    exact=False keeps the fp32-class ranking of the tensor-core dot.  compute_precision
+    "fp64" (the reference's fp64 dots, cost.cu:108-122) gives the exact fp64 lists
+    whatever `exact` says, for features holding fp32 values; the certificate terms are
+    fp32-class in every mode (diagnostics["certificate_precision"])."""
     k = int(round(float(topk)))
     if abs(float(topk) - k) > 1e-9:
         raise ValueError("fused inner-product scan requires an integer pricing_topk")
     kernel_k = topk_bucket(k)
     if str(compute_precision) not in {"fp32", "fp64", "tf32"}:
         raise ValueError("compute_precision must be one of: fp32, fp64")
-    if str(compute_precision) == "fp64":
-        raise NotImplementedError("hello_ot_b200 computes the bilinear dot on tensor cores (fp32-class 3-term fp16 split); "
-                                  "compute_precision='fp64' is not implemented")
+    fp64 = str(compute_precision) == "fp64"
+    if fp64:
+        # fp64 ranking: the exact fp64 top-k lists of the fp64 scores of the fp32 features (the
+        # fp64 re-check); features given in fp64 must hold fp32 values (the reference stores
+        # points as fp32, types.py:26), and the certificate terms stay fp32-class
+        for name, feat in (("source", source_feat), ("target", target_feat)):
+            if not _holds_fp32(feat):
+                raise NotImplementedError(f"compute_precision='fp64' needs {name} features representable in fp32")
+        exact = True
     if col_kernel not in ("auto", "current", "warp2", "warp4"):
         raise ValueError("col_kernel must be one of {auto, current, warp2, warp4}")
     device = torch.device(f"cuda:{int(gpu_id)}")
@@ -396,7 +419,7 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
     f = _to_device(source_dual, device, torch.float64).view(-1)
     g = _to_device(target_dual, device, torch.float64).view(-1)
     rv, ri, cv, ci, stats = l2sq_scan(x, y, a, b, f - a, g - b, k, dot_scale=float(dot_scale),
-                                      precision=str(compute_precision), exact=bool(exact))
+                                      precision="fp32" if fp64 else str(compute_precision), exact=bool(exact))
     rows_t, cols_t = flatten_candidates(rv, ri, cv, ci, theta)
     s = stats.cpu().tolist()
     num_sq, den_sq, max_pos, cost_linf, count = s[0], s[1], s[2], s[3], int(round(s[4]))
@@ -426,6 +449,7 @@ def raw_lowrank_bidir_feasibility_pricing_scan(source_feat, target_feat, source_
         "scan_traversal": "fused_tensor_core_bidirectional",
         "cost_compute_precision": str(compute_precision),
         "fp64_recheck": bool(exact),
+        "certificate_precision": "fp32-class",  # the certificate terms of the tensor-core scores
     }
     if exact:
         diagnostics["fp64_rescanned_lists"] = sum(l2sq_last_rescans())

@@ -79,3 +79,20 @@ def test_product_pricing_scan_matches_reference(hb, cuda, oracle, path, exact):
         score = oracle.pair_scores("raw", z["x"], z["y"], z["f"] - z["a"], z["g"] - z["b"], z["a"], z["b"],
                                    res.rows, res.cols, dot_scale=2.0)[0]
         assert np.all(score > -1e-9 * (1.0 + np.abs(z["f"]).max() + np.abs(z["g"]).max()))
+
+
+def test_product_pricing_scan_fp64_precision(hb, cuda):
+    """compute_precision="fp64" on features holding fp32 values (given as fp64 arrays) gives the
+    exact fp64 lists: the same candidates and certificate as the fp32 features with exact=True."""
+    path = sorted(GOLDEN.glob("scan_l2sq_*.npz"))[0]
+    with np.load(path) as z:
+        z = {key: z[key] for key in z.files}
+    k = int(z["k"])
+    args = (z["a"], z["b"], z["f"], z["g"])
+    ref = hb.raw_lowrank_bidir_feasibility_pricing_scan(z["x"], z["y"], *args, topk=k, dot_scale=2.0, exact=True)
+    got = hb.raw_lowrank_bidir_feasibility_pricing_scan(z["x"].astype(np.float64), z["y"].astype(np.float64), *args,
+                                                        topk=k, dot_scale=2.0, compute_precision="fp64", exact=False)
+    assert np.array_equal(got.rows, ref.rows) and np.array_equal(got.cols, ref.cols)
+    assert got.dual_feasibility == ref.dual_feasibility
+    assert got.diagnostics["fp64_recheck"] and got.diagnostics["cost_compute_precision"] == "fp64"
+

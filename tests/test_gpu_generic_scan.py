@@ -53,6 +53,10 @@ def test_bidirectional_raw_matches_scan_extension(hb, cuda):
     assert torch.equal(out[0], ref[0]) and torch.equal(out[1], ref[1].long())
     assert torch.equal(out[2], ref[2]) and torch.equal(out[3], ref[3].long())
     assert out[1].dtype == torch.int64 and out[8].dtype == torch.int64
+    # compute_precision=1 (fp64): the exact fp64 lists whatever exact says
+    out64 = gs.bidirectional(X, Y, F, G, 8, 3, raw_costs=(NX, NY), raw_biases=(F - NX, G - NY), compute_precision=1,
+                             exact=False)
+    assert all(torch.equal(u, v) for u, v in zip(out64[:4], out[:4]))
     _same_certificate(gs.certificate_only(X, Y, F, G, 3, raw_costs=(NX, NY)), out[4:])
     assert float(gs.certificate_only(X, Y, F, G, 3, raw_costs=(NX, NY), compute_denominator=False)[1]) == 0.0
 

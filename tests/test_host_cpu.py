@@ -156,3 +156,15 @@ def test_leaf_cost_matrix_validates_kind(hb):
         hb.leaf_cost_matrix(x, x, "cosine")
     with pytest.raises(ValueError, match="offset"):
         hb.leaf_cost_matrix(x, x, "l2^2")
+
+
+def test_fp64_pricing_needs_fp32_representable_features(hb):
+    """compute_precision="fp64" is served as exact fp64 lists over fp32 features; features that
+    are not fp32 values are refused before anything reaches the library."""
+    from hello_ot_b200.scan import _holds_fp32
+    x = np.random.default_rng(0).normal(size=(5, 3))
+    assert not _holds_fp32(x) and _holds_fp32(x.astype(np.float32)) and _holds_fp32(x.astype(np.float32).astype(float))
+    v = np.zeros(5)
+    with pytest.raises(NotImplementedError, match="representable in fp32"):
+        hb.raw_lowrank_bidir_feasibility_pricing_scan(x, x, v, v, v, v, topk=2, compute_precision="fp64")
+
