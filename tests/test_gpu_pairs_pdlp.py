@@ -184,6 +184,49 @@ def test_pdlp_linf_termination(hb, cuda, shape):
         hb.NativeRestrictedOTPDLP(device=cuda, termination_norm="l1")
 
 
+def _hub_support(ns, nt, seed):
+    """A transport-feasible support with one source joined to every target (a node whose
+    edges span many stages of the fused pass) and degree-1 or 2 elsewhere."""
+    rng = np.random.default_rng(seed)
+    rows = np.concatenate([np.zeros(nt, dtype=np.int64), np.arange(ns), rng.integers(0, ns, ns // 2)])
+    cols = np.concatenate([np.arange(nt), rng.integers(0, nt, ns), rng.integers(0, nt, ns // 2)])
+    key = np.unique(rows * nt + cols)
+    rows, cols = key // nt, key % nt
+    perm = rng.permutation(rows.size)
+    wa, wb = rng.uniform(0.5, 1.5, ns), rng.uniform(0.5, 1.5, nt)
+    return rows[perm], cols[perm], rng.random(rows.size) * 3, wa / wa.sum(), wb / wb.sum()
+
+
+def _sparse_support(ns, nt, seed):
+    """Degree 1-2 on both sides (a ring plus a few chords): tiles of few edges, so one stage of
+    the fused pass spans many tiles."""
+    rng = np.random.default_rng(seed)
+    k = max(ns, nt)
+    rows = np.concatenate([np.arange(k) % ns, (np.arange(k) + 1) % ns, rng.integers(0, ns, k // 8)])
+    cols = np.concatenate([np.arange(k) % nt, np.arange(k) % nt, rng.integers(0, nt, k // 8)])
+    key = np.unique(rows * nt + cols)
+    rows, cols = key // nt, key % nt
+    perm = rng.permutation(rows.size)
+    wa, wb = rng.uniform(0.5, 1.5, ns), rng.uniform(0.5, 1.5, nt)
+    return rows[perm], cols[perm], rng.random(rows.size) * 3, wa / wa.sum(), wb / wb.sum()
+
+
+@pytest.mark.parametrize("kind", ["hub", "sparse"])
+def test_pdlp_block_is_bit_exact_irregular(hb, cuda, oracle, kind):
+    """One block of iterations bit-exact on irregular supports: a node with thousands of edges
+    among degree-1/2 nodes, and degree 1-2 everywhere (stages spanning many tiles)."""
+    rows, cols, c, a, b = _hub_support(6000, 5000, 3) if kind == "hub" else _sparse_support(20000, 17000, 4)
+    assert rows.size < 64 * min(len(a), len(b))  # both sides sparse: the fused pass
+    F = 40
+    ref = oracle.pdlp(rows, cols, c, a, b, frequency=F, iteration_limit=F, tolerance=0.0)
+    solver = hb.NativeRestrictedOTPDLP(device=cuda, evaluation_frequency=F, iteration_limit=F,
+                                       initial_primal_weight=ref["primal_weight"])
+    got = solver.solve_restricted(rows=rows, cols=cols, costs=c, source_mass=a, target_mass=b, tolerance=0.0)
+    assert got.iterations == ref["iterations"] == F
+    assert np.array_equal(got.x.cpu().numpy(), ref["x"])
+    assert np.array_equal(got.y.cpu().numpy(), ref["y"])
+
+
 def test_pdlp_block_is_bit_exact_large_tiles(hb, cuda, oracle):
     """Above about 300k nodes per side the fused pass takes 256-node tiles (64 below, which
     the smaller cases cover): one block of iterations is bit-exact there as well."""
