@@ -140,9 +140,10 @@ def _pairs_worker(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
-def test_sharded_pair_costs_match_single_process(oracle, tmp_path):
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_pair_costs_match_single_process(oracle, tmp_path, world):
     out = tmp_path / "pairs.npz"
-    mp.spawn(_pairs_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    mp.spawn(_pairs_worker, args=(world, _free_port(), str(out)), nprocs=world, join=True)
     got = np.load(out)
     x, y, a, b, _, _ = _problem()
     want = oracle.pair_costs("raw", x, y, got["rows"], got["cols"], a, b, dot_scale=2.0)
