@@ -406,6 +406,36 @@ __global__ void __launch_bounds__(256) node_pass_wide(Dev D, int it, int src_blo
     if (lane == 0) dual_update(D, D.steps[it], target ? D.n + v : v, sum);
 }
 
+// Complete supports stored row-major (edge p = i * m + j after the source sort, e.g. a
+// coarsest level's dense transport), summation "tree": the target sums read the reflected
+// primal as a matrix, a block per 32 targets, warp w adding rows w, w + 32, ... of its lane's
+// column (32 consecutive columns: coalesced), then warp 0 adding the 32 partials in warp order.
+// A fixed order (not the reference's), like the lane tree of node_pass_wide, without its
+// stride-m gathers.
+__global__ void __launch_bounds__(1024) dense_target_pass(Dev D, int it) {
+    __shared__ double part[32][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j = blockIdx.x * 32 + lane;
+    double acc = 0.0;
+    if (j < D.m) {
+        const double* col = D.rx + j;
+        for (int i = warp; i < D.n; i += 32) acc += __ldg(col + (int64_t)i * D.m);
+    }
+    part[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && j < D.m) {
+        double sum = 0.0;
+        for (int w = 0; w < 32; ++w) sum += part[w][lane];
+        dual_update(D, D.steps[it], D.n + j, sum);
+    }
+}
+
+// flag = 1 unless every sorted edge p has target p % m (the row-major complete layout).
+__global__ void check_rowmajor(Dev D, int* flag) {
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < D.e; p += (int64_t)gridDim.x * blockDim.x)
+        if (D.e_col[p] != (int)(p % D.m)) atomicOr(flag, 1);
+}
+
 // Fused passes (the default for sparse supports): one launch per iteration.  The edge state
 // is kept twice, in source order (x, ax, cs) and in target order (tx, tax, tcs), so each side
 // reads its nodes' edges contiguously.  Tiles are C::TN consecutive nodes of one side (node v
@@ -961,7 +991,19 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
     const bool wide_sources = e >= (int64_t)pdlp::WIDE_DEGREE * n, wide_targets = e >= (int64_t)pdlp::WIDE_DEGREE * m;
     // fused passes (one launch per iteration) unless node sums are atomic or a side is dense
     const bool fused = !ctl.atomic && !wide_sources && !wide_targets;
-    const int per_iter = fused ? 1 : (!ctl.atomic && wide_sources && wide_targets) ? 2 : 3;  // kernels per iteration
+    // complete row-major support in tree mode: the coalesced target pass
+    bool dense_rm = false;
+    if (!fused && !ctl.atomic && ctl.tree && wide_targets && e == n * m) {
+        int* flag = reinterpret_cast<int*>(D.red);  // reduction scratch, free before the iterations
+        cudaMemsetAsync(flag, 0, sizeof(int), st);
+        pdlp::check_rowmajor<<<gb, 256, 0, st>>>(D, flag);
+        HB_LAUNCHED(1);
+        int hflag = 1;
+        cudaMemcpyAsync(&hflag, flag, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail("layout check");
+        dense_rm = hflag == 0;
+    }
+    const int per_iter = fused ? 1 : dense_rm ? 3 : (!ctl.atomic && wide_sources && wide_targets) ? 2 : 3;  // kernels per iteration
     // fused passes: persistent blocks (one wave at the kernel's occupancy), half of them per side;
     // stages of 512 edges, two per block (a third stage measured slower, 489 against 394 us per
     // iteration at E = 21M, also with the grid sized to its occupancy), node-scale gathers cached
@@ -1000,7 +1042,8 @@ int pdlp_solve(const int64_t* rows, const int64_t* cols, const double* costs, in
             pdlp::target_pass<true><<<(unsigned)((m + 255) / 256), 256, 0, s_>>>(D, it);
         } else {
             pdlp::edge_pass<false><<<gb, 256, 0, s_>>>(D, it);
-            const int sb = wide_sources ? (n + 7) / 8 : 0, tb = wide_targets ? (m + 7) / 8 : 0;
+            const int sb = wide_sources ? (n + 7) / 8 : 0, tb = wide_targets && !dense_rm ? (m + 7) / 8 : 0;
+            if (dense_rm) pdlp::dense_target_pass<<<(unsigned)((m + 31) / 32), 1024, 0, s_>>>(D, it);
             if (sb + tb > 0) {
                 if (ctl.tree) pdlp::node_pass_wide<true><<<(unsigned)(sb + tb), 256, 0, s_>>>(D, it, sb);
                 else pdlp::node_pass_wide<false><<<(unsigned)(sb + tb), 256, 0, s_>>>(D, it, sb);
