@@ -88,6 +88,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-rows", action="store_true",
+                   help="scan path at N = 1: skip the pair-cost and PDHG lines the headline line carries")
     args = p.parse_args()
     n0, d0 = PATH_SIZES[args.path]
     args.n = n0 if args.n is None else args.n
@@ -288,6 +290,28 @@ def reference_scan_sample(args, steps, warmup):
     sample = (f"{rows} source rows x {n} targets per step (d={d}, k={k}), reference dot_tile (scan.cpp) + "
               f"torch.mm tiles, {warmup} warm-up + {steps} timed step(s)")
     return sec, rows, threads, sample
+
+
+def other_rows(args):
+    """The pair-cost (SDDMM) and PDHG rows at their config-5 sizes, each measured by this
+    script's own --path run in a child process (CUDA-event timing as in the headline), so
+    the headline line carries them too."""
+    import subprocess
+    rows = {}
+    for path in ("pairs", "pdlp"):
+        cmd = [sys.executable, str(REPO / "bench.py"), "--path", path, "--steps", str(max(args.steps, 1)),
+               "--warmup", str(max(args.warmup, 1)), "--no-cpu"]
+        try:
+            res = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+            line = json.loads([ln for ln in res.stdout.splitlines() if ln.startswith("{")][-1])
+            roof = line.get("roofline", {})
+            rows[path] = {"metric": line["metric"], "value": line["value"], "unit": line["unit"],
+                          "workload": line["config"]["workload"], "kernel": roof.get("kernel"),
+                          "achieved_gbs": roof.get("achieved"), "frac": roof.get("frac"),
+                          "iteration_us": roof.get("iteration_us")}
+        except Exception as exc:  # report, do not fail the headline
+            rows[path] = {"unavailable": str(exc)[:200]}
+    return rows
 
 
 def reference_arm_baseline(args):
@@ -508,6 +532,8 @@ def run_ours(args):
                           else "ShardedPricingScan.scan from pinned host blocks"}
     if rank == 0 and cpu_baseline is not None:
         out["cpu_baseline"] = cpu_baseline
+    if rank == 0 and world == 1 and not args.no_rows:
+        out["other_rows"] = other_rows(args)
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
