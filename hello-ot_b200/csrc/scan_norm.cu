@@ -16,6 +16,7 @@
 // row, one per half of the columns) that keeps the row top-k in registers.
 #include <algorithm>
 #include <string>
+#include <type_traits>
 
 #include "../../include/hello_b200.h"
 #include "common.cuh"
@@ -28,10 +29,12 @@ namespace norm {
 
 constexpr int BM = 128, BN = 128, BKS = 8, THREADS = 256;
 
-// Slab position of tile row r: the 8 rows ty, ty+16, ..., ty+112 of the thread
-// with distance-block row ty sit side by side, so a thread reads its 8 values
-// with two 16-byte loads (and likewise for columns).
-__device__ __forceinline__ int slab_pos(int r) { return (r & 15) * 8 + (r >> 4); }
+// Slab position of tile row r: rows ty, ty+16, ty+32, ty+48 of the thread with
+// distance-block row ty fill the 16-byte chunk ty, rows ty+64..ty+112 the chunk
+// 16 + ty, so a thread reads its 8 values with two 16-byte loads (likewise for
+// columns) and the 8 lanes of a load phase read 8 consecutive chunks (no bank
+// conflict).
+__device__ __forceinline__ int slab_pos(int r) { return (r & 64) | ((r & 15) << 2) | ((r >> 4) & 3); }
 
 struct Smem {
     float xs[2][BKS][BM];  // k-major slabs, rows at slab_pos
@@ -48,6 +51,7 @@ struct Params {
     const float* x;  // query features (q x d)
     const float* y;  // database features (n x d)
     int q, n, d;
+    bool vec;        // d % 4 == 0 and both feature bases 16-byte aligned
     int groups, tpg, ct, units;
     const double* q_bias;
     const double* d_bias;
@@ -71,17 +75,32 @@ __device__ __forceinline__ float accumulate(float acc, float a, float b) {
     return fmaf(z, z, acc);
 }
 
+// 128 rows x 8 features, stored k-major.  Warp w covers features (w >> 2) * 4..+3
+// of 32 rows; lane (a = lane & 7, b = lane >> 3) takes row a + 8 (w & 1) +
+// 16 (b + 4 ((w >> 1) & 1)), whose slab position lands in bank 4 a + b, so each
+// of the four shared-memory stores is conflict-free.  vec: d % 4 == 0 and a
+// 16-byte aligned base, read with one 16-byte load per row.
 __device__ __forceinline__ void load_slab(const float* __restrict__ src, int rows_total, int d, int r0, int k0,
-                                          float (*dst)[BM]) {
-    // 128 rows x 8 features, stored k-major; thread t covers row t/2, features (t%2)*4..+3
-    const int t = threadIdx.x;
-    const int r = t >> 1, kb = (t & 1) * 4;
-    const int gr = r0 + r, pos = slab_pos(r);
+                                          float (*dst)[BM], bool vec) {
+    const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+    const int r = (lane & 7) + 8 * (w & 1) + 16 * ((lane >> 3) + 4 * ((w >> 1) & 1));
+    const int kb = (w >> 2) * 4;
+    const int gr = r0 + r, pos = slab_pos(r), k = k0 + kb;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (gr < rows_total) {
+        const float* row = src + (int64_t)gr * d;
+        if (vec) {
+            if (k < d) {
+                const float4 f = *reinterpret_cast<const float4*>(row + k);
+                v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+            }
+        } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int k = k0 + kb + j;
-        dst[kb + j][pos] = (gr < rows_total && k < d) ? src[(int64_t)gr * d + k] : 0.0f;
+            for (int j = 0; j < 4; ++j) v[j] = k + j < d ? row[k + j] : 0.0f;
+        }
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[kb + j][pos] = v[j];
 }
 
 // Order-preserving integer image of an fp32 value (atomicMax on thresholds).
@@ -153,24 +172,24 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) dist[i][j] = 0.0f;
             const int nslab = (p.d + BKS - 1) / BKS;
-            load_slab(p.x, p.q, p.d, rb * BM, 0, s.xs[0]);
-            load_slab(p.y, p.n, p.d, c0, 0, s.ys[0]);
+            load_slab(p.x, p.q, p.d, rb * BM, 0, s.xs[0], p.vec);
+            load_slab(p.y, p.n, p.d, c0, 0, s.ys[0], p.vec);
             __syncthreads();
             for (int sl = 0; sl < nslab; ++sl) {
                 const int cur = sl & 1;
                 if (sl + 1 < nslab) {
-                    load_slab(p.x, p.q, p.d, rb * BM, (sl + 1) * BKS, s.xs[cur ^ 1]);
-                    load_slab(p.y, p.n, p.d, c0, (sl + 1) * BKS, s.ys[cur ^ 1]);
+                    load_slab(p.x, p.q, p.d, rb * BM, (sl + 1) * BKS, s.xs[cur ^ 1], p.vec);
+                    load_slab(p.y, p.n, p.d, c0, (sl + 1) * BKS, s.ys[cur ^ 1], p.vec);
                 }
                 // features past d are zero in both slabs: they add |0 - 0| = 0 (or (0-0)^2),
                 // which leaves every fp32 partial sum unchanged, so the loop runs a full slab
                 // (not unrolled: unrolling hoists the slab loads and spills the 8x8 block)
 #pragma unroll 1
                 for (int k = 0; k < BKS; ++k) {
-                    const float4 xa = *reinterpret_cast<const float4*>(&s.xs[cur][k][ty * 8]);
-                    const float4 xb = *reinterpret_cast<const float4*>(&s.xs[cur][k][ty * 8 + 4]);
-                    const float4 ya = *reinterpret_cast<const float4*>(&s.ys[cur][k][tx * 8]);
-                    const float4 yb = *reinterpret_cast<const float4*>(&s.ys[cur][k][tx * 8 + 4]);
+                    const float4 xa = *reinterpret_cast<const float4*>(&s.xs[cur][k][ty * 4]);
+                    const float4 xb = *reinterpret_cast<const float4*>(&s.xs[cur][k][64 + ty * 4]);
+                    const float4 ya = *reinterpret_cast<const float4*>(&s.ys[cur][k][tx * 4]);
+                    const float4 yb = *reinterpret_cast<const float4*>(&s.ys[cur][k][64 + tx * 4]);
                     const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
                     const float yv[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
 #pragma unroll
@@ -203,28 +222,42 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                 const int cb0 = half * 64;
                 const int live = min(64, ncols - cb0);  // valid columns of this half
                 const double tv = top.v[KK - 1];
-                const int ti = top.i[KK - 1];
                 uint64_t mask = 0;
                 double num4[4] = {0, 0, 0, 0}, den4[4] = {0, 0, 0, 0};
                 double mpos = 0.0, mcost = 0.0;
                 int cnt = 0;
-                // phase 1, branch-free: scores, certificate terms, candidate mask
-#pragma unroll 16
-                for (int j = 0; j < 64; ++j) {
-                    const bool ok = j < live;
-                    const double cost = pcost(er, cb0 + j);
-                    const double cbias = s.dbias[cb0 + j];
-                    const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
-                    if (STATS) {
-                        den4[j & 3] += ok ? cost * cost : 0.0;
-                        mcost = fmax(mcost, ok ? fabs(cost) : 0.0);
-                        const bool pos = ok && sc > 0.0;
-                        num4[j & 3] += pos ? sc * sc : 0.0;
-                        mpos = fmax(mpos, pos ? sc : 0.0);
-                        cnt += pos ? 1 : 0;
+                // phase 1: scores, certificate terms and the candidate mask, in chunks of 16
+                // columns with constant mask bits; FULL (all 64 columns valid) drops the
+                // column checks.  The mask screens with sc >= the list's k-th score, a
+                // superset of the columns that beat it: phase 2's offer() decides exactly.
+                auto phase1 = [&](auto full) {
+                    constexpr bool FULL = decltype(full)::value;
+#pragma unroll 1
+                    for (int jb = 0; jb < 64; jb += 16) {
+                        uint32_t m16 = 0;
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) {
+                            const int j = jb + u;
+                            const bool ok = FULL || j < live;
+                            const double cost = pcost(er, cb0 + j);
+                            const double cbias = s.dbias[cb0 + j];
+                            const double sc = SWAP ? ((rbias - cost) + cbias) : ((cbias - cost) + rbias);
+                            if (STATS && ok) {
+                                den4[u & 3] = fma(cost, cost, den4[u & 3]);
+                                mcost = fmax(mcost, fabs(cost));
+                                if (sc > 0.0) {
+                                    num4[u & 3] = fma(sc, sc, num4[u & 3]);
+                                    mpos = fmax(mpos, sc);
+                                    ++cnt;
+                                }
+                            }
+                            if (K > 0 && ok && sc >= tv) m16 |= 1u << u;
+                        }
+                        mask |= (uint64_t)m16 << jb;
                     }
-                    if (K > 0) mask |= (ok && better(sc, c0 + cb0 + j, tv, ti)) ? (1ull << j) : 0ull;
-                }
+                };
+                if (live == 64) phase1(std::true_type{});
+                else phase1(std::false_type{});
                 if (STATS) {
                     acc[0] += (num4[0] + num4[1]) + (num4[2] + num4[3]);
                     acc[1] += (den4[0] + den4[1]) + (den4[2] + den4[3]);
@@ -249,11 +282,22 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                     const double cb = s.dbias[c];
                     const double thr = (double)s.cthr[c];
                     uint64_t cmask = 0;
-#pragma unroll 16
-                    for (int r = 0; r < 64; ++r) {
-                        const double sc = (cb - pcost(r0 + r, c)) + s.rbx[r0 + r];
-                        cmask |= (r < rlive && sc >= thr) ? (1ull << r) : 0ull;
-                    }
+                    auto screen = [&](auto full) {
+                        constexpr bool FULL = decltype(full)::value;
+#pragma unroll 1
+                        for (int rbk = 0; rbk < 64; rbk += 16) {
+                            uint32_t m16 = 0;
+#pragma unroll
+                            for (int u = 0; u < 16; ++u) {
+                                const int r = rbk + u;
+                                const double sc = (cb - pcost(r0 + r, c)) + s.rbx[r0 + r];
+                                if ((FULL || r < rlive) && sc >= thr) m16 |= 1u << u;
+                            }
+                            cmask |= (uint64_t)m16 << rbk;
+                        }
+                    };
+                    if (rlive == 64) screen(std::true_type{});
+                    else screen(std::false_type{});
                     if (cmask) {
                         const int64_t base = (list_base + c0 + c) * KK;
                         TopK<KK> cl;
@@ -460,6 +504,7 @@ int norm_scan(const float* x, const float* y, int64_t q, int64_t n, int64_t d, c
     if (!L.ok) { err = "workspace too small for the norm scan"; return 3; }
     norm::Params p{};
     p.x = x; p.y = y; p.q = (int)q; p.n = (int)n; p.d = (int)d;
+    p.vec = d % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
     p.q_bias = f; p.d_bias = g;
     p.part_v = L.pv1; p.part_i = L.pi1; p.cta_stats = L.cta;
     if (pert && pert->sigma != 0.0) p.pert = *pert;
