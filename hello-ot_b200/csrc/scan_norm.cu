@@ -181,11 +181,12 @@ __global__ void __launch_bounds__(THREADS, 2) scan_kernel(const Params p) {
                     load_slab(p.x, p.q, p.d, rb * BM, (sl + 1) * BKS, s.xs[cur ^ 1], p.vec);
                     load_slab(p.y, p.n, p.d, c0, (sl + 1) * BKS, s.ys[cur ^ 1], p.vec);
                 }
-                // features past d are zero in both slabs: they add |0 - 0| = 0 (or (0-0)^2),
-                // which leaves every fp32 partial sum unchanged, so the loop runs a full slab
-                // (not unrolled: unrolling hoists the slab loads and spills the 8x8 block)
+                // the slab's features below d, in increasing order (the slab rows past d
+                // hold zeros and are not read); not unrolled: unrolling hoists the slab
+                // loads and spills the 8x8 block
+                const int kend = min(BKS, p.d - sl * BKS);
 #pragma unroll 1
-                for (int k = 0; k < BKS; ++k) {
+                for (int k = 0; k < kend; ++k) {
                     const float4 xa = *reinterpret_cast<const float4*>(&s.xs[cur][k][ty * 4]);
                     const float4 xb = *reinterpret_cast<const float4*>(&s.xs[cur][k][64 + ty * 4]);
                     const float4 ya = *reinterpret_cast<const float4*>(&s.ys[cur][k][tx * 4]);
