@@ -211,6 +211,28 @@ def test_norm_scan_bit_exact(hb, cuda, oracle, kind, q, n, d, k):
     np.testing.assert_allclose(stats[:2], es[:2], rtol=1e-12)
 
 
+@pytest.mark.parametrize("kind", ["l1", "l2"])
+def test_norm_scan_unaligned_features(hb, cuda, kind):
+    """d % 4 == 0 but feature bases 4 bytes past a 16-byte boundary: the kernel reads the rows
+    with scalar loads instead of 16-byte ones and returns the same lists and certificate."""
+    rng = np.random.default_rng(17)
+    q, n, d, k = 300, 260, 12, 8
+    x = torch.as_tensor(rng.normal(size=(q, d)), dtype=torch.float32, device=cuda)
+    y = torch.as_tensor(rng.normal(size=(n, d)), dtype=torch.float32, device=cuda)
+    f = torch.as_tensor(rng.normal(size=q) * 3, dtype=torch.float64, device=cuda)
+    g = torch.as_tensor(rng.normal(size=n) * 3 + 5, dtype=torch.float64, device=cuda)
+    xb = torch.empty(q * d + 1, dtype=torch.float32, device=cuda)
+    yb = torch.empty(n * d + 1, dtype=torch.float32, device=cuda)
+    xu, yu = xb[1:].view(q, d), yb[1:].view(n, d)
+    xu.copy_(x)
+    yu.copy_(y)
+    assert xu.data_ptr() % 16 != 0 and yu.data_ptr() % 16 != 0
+    ref = hb.norm_scan(x, y, f, g, k, kind)
+    out = hb.norm_scan(xu, yu, f, g, k, kind)
+    for a, b in zip(out, ref):
+        assert torch.equal(a, b)
+
+
 # (q, n, d, k): several row blocks per row group, ragged tiles, k > n, one feature
 @pytest.mark.parametrize("shift", [-20, 20])
 @pytest.mark.parametrize("passes", [1, 2])
